@@ -1,0 +1,428 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention path of the DA3 ViT backbone (Vestra Engine).
+
+Metric: global-attention TFLOP/s at S=12 views (504x336, 866 tokens
+per view, 10,392-token window, E=768, 12 heads x 64), FLOPs = 4 * N^2 * d * heads.
+A step is one global attention sub-block over the whole window: LN1 output (F32,
+resident in HBM) -> QKV UMMA with QK-norm/RoPE epilogue -> fused flash attention ->
+output projection (F32).  With --gpus N > 1 the window's queries are split into N
+equal token slices (one process per GPU) and K'/V are all-gathered over NCCL.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  `value` is device-timed (CUDA events around each
+step on the launching stream, L2 flushed between steps, max over ranks); `e2e`
+goes through the public host API with pinned host buffers and the H2D/D2H copies
+inside the timed region.  `--impl reference` times the CPU F32 restatement of the
+reference attention (oracle/, the reference itself cannot be built here) on the
+host cores, on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vestra-engine_b200"))
+
+import synthetic as syn  # noqa: E402
+
+LAYER = 5           # a global block of the DA3-BASE schedule (alt_start 4: globals 5,7,9,11)
+L2_FLUSH_BYTES = 256 << 20
+# dram__bytes_read.sum + dram__bytes_write.sum of one flash launch, from the ncu
+# capture summarised in profiles/flash_fwd_d64_cfg3.md (None until captured).
+FLASH_DRAM_BYTES_PER_LAUNCH = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="cfg3_s12_global", choices=sorted(syn.CONFIGS))
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bound on the CPU-baseline sample (seconds of CPU work)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def cpu_info():
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return model
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="va_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.dev), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        mx = max(int(r[2]) for r in rows)
+        loaded = [s for s, r in zip(sm, rows) if float(r[3] or 0) > 200.0] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": int(statistics.median(loaded)), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3] or 0) for r in rows)}
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_attention_sample(wl, seconds_budget, threads=0):
+    """Times the CPU F32 restatement (oracle/) of the attention sub-block on a
+    bounded sample of the workload; returns (TFLOP/s, cores, sample description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle
+
+    oracle.build()
+    x = syn.hidden_states(wl.rows, wl.embed, seed=0)
+    p = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
+    pos = None
+    try:
+        import vestra_attn as va
+        pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
+    except Exception:
+        pass
+    seg = wl.seg_len
+    cores = threads or os.cpu_count() or 1
+    # Probe with a small row subset to size the sample.
+    probe_rows = np.sort(np.random.default_rng(1).choice(wl.rows, min(wl.rows, 256), replace=False))
+    t = time.perf_counter()
+    oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg if not wl.global_ else 0,
+                           q_rows=probe_rows, threads=threads)
+    t_probe = time.perf_counter() - t
+    # Per query row the attention costs 4*seg*64*heads FLOPs; K/V projection is fixed.
+    per_row = max(t_probe / len(probe_rows), 1e-9)
+    nq = int(min(wl.rows, max(256, seconds_budget / 3 / per_row)))
+    if nq >= wl.rows:
+        q_rows, sample = None, f"full window ({wl.rows} query rows), median of 3"
+        nq = wl.rows
+    else:
+        q_rows = np.sort(np.random.default_rng(2).choice(wl.rows, nq, replace=False)).astype(np.int64)
+        sample = f"{nq} of {wl.rows} query rows (seeded), all K/V rows projected, median of 3"
+    times = []
+    for _ in range(3):
+        t = time.perf_counter()
+        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg if not wl.global_ else 0,
+                               q_rows=q_rows, threads=threads)
+        times.append(time.perf_counter() - t)
+    flops = 4.0 * nq * seg * 64 * wl.heads
+    return flops / statistics.median(times) / 1e12, cores, sample
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    wl = syn.CONFIGS[args.workload]
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    oracle.build()
+    x = syn.hidden_states(wl.rows, wl.embed, seed=0)
+    p = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
+    import vestra_attn as va
+    pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
+    seg = wl.seg_len if not wl.global_ else 0
+    cores = os.cpu_count() or 1
+    # Size each step to at most ~3 s of CPU work (the whole run stays within minutes).
+    probe = np.sort(np.random.default_rng(1).choice(wl.rows, min(wl.rows, 256), replace=False))
+    t = time.perf_counter()
+    oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=probe)
+    per_row = (time.perf_counter() - t) / len(probe)
+    nq = int(min(wl.rows, max(256, 3.0 / max(per_row, 1e-9))))
+    q_rows = None if nq >= wl.rows else np.sort(
+        np.random.default_rng(2).choice(wl.rows, nq, replace=False)).astype(np.int64)
+    nq = wl.rows if q_rows is None else nq
+    for _ in range(args.warmup):
+        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=q_rows)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=q_rows)
+        times.append(time.perf_counter() - t)
+    flops = 4.0 * nq * wl.seg_len * 64 * wl.heads
+    total = sum(times)
+    value = flops * args.steps / total / 1e12
+    sample = ("full window" if q_rows is None else f"{nq} of {wl.rows} query rows (seeded)") + \
+        ", all K/V rows projected, per step"
+    line = {
+        "impl": "reference", "metric": "global-attention TFLOP/s", "value": round(value, 4),
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
+        "config": workload_config(wl, 1),
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                         "sample": sample, "cpu": cpu_info()},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU F32 restatement of the reference attention (vestra-kernels is un-vendored and no Rust "
+                "toolchain exists, so the reference binary cannot be built)",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(wl, n_gpus):
+    return {
+        "workload": wl.name, "views": wl.views, "tokens_per_view": wl.tokens_per_view, "window_tokens": wl.rows,
+        "embed": wl.embed, "heads": wl.heads, "head_dim": 64, "global": wl.global_,
+        "step": "one attention sub-block: LN1 out -> QKV (+QK-norm, 2D RoPE) -> flash attention -> proj",
+        "flops_per_step": wl.attention_flops(),
+        "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write)",
+        "parallelism": "single GPU" if n_gpus == 1 else
+        f"query-sharded window over {n_gpus} GPUs, K/V all-gather (NCCL)",
+    }
+
+
+# --------------------------------------------------------------------------- ours
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import vestra_attn as va
+
+    rank, world, local_rank = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local_rank))
+    wl = syn.CONFIGS[args.workload]
+    if not wl.global_ and world > 1:
+        raise SystemExit("the benchmark shards global blocks only")
+    row0, local = va.shard_rows(wl.rows, world, rank)
+    cfg = va.default_config(embed_dim=wl.embed, num_heads=wl.heads, num_register=wl.n_special - 1,
+                            max_rows=wl.rows, depth=12, rope_start=4, qknorm_start=4)
+    ctx = va.Context(cfg, local_rank)
+    ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))
+    if world > 1:
+        obj = [va.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.comm_init(obj[0], world, rank)
+
+    x_all = syn.hidden_states(wl.rows, wl.embed, seed=0)
+    x_local = np.ascontiguousarray(x_all[row0:row0 + local])
+    ln1 = torch.from_numpy(x_local).cuda()
+    out = torch.empty_like(ln1)
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def step():
+        if world == 1:
+            ctx.attention_device(LAYER, ln1, out, wl.gh, wl.gw, wl.views, wl.global_, stream=sp)
+        else:
+            ctx.attention_device_sharded(LAYER, ln1, out, wl.gh, wl.gw, wl.views, wl.global_, stream=sp)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        flush_buf.zero_()
+        step()
+    barrier()
+    ctx.check_device()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        for i in range(args.steps):
+            flush_buf.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        barrier()
+    ctx.check_device()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = max_over_ranks(sum(step_ms))
+    ms_per_step = total_ms / args.steps
+    flops = wl.attention_flops()
+    value = flops / (ms_per_step * 1e-3) / 1e12
+
+    # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    qk_scale = 1.0
+    q = (qk_scale * torch.randn(local, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
+    kw = torch.randn(wl.rows, wl.embed, device="cuda", generator=g).to(torch.bfloat16)
+    vw = torch.randn(wl.rows, wl.embed, device="cuda", generator=g).to(torch.bfloat16)
+    o = torch.empty(local, wl.embed, device="cuda", dtype=torch.bfloat16)
+    for _ in range(3):
+        ctx.flash_bf16(q, kw, vw, wl.heads, o, q_offset=row0, stream=sp)
+    k_ms = []
+    barrier()
+    for _ in range(args.steps):
+        flush_buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx.flash_bf16(q, kw, vw, wl.heads, o, q_offset=row0, stream=sp)
+        b.record(stream)
+        k_ms.append((a, b))
+    barrier()
+    ctx.check_device()
+    flash_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ms)
+    flash_flops = 4.0 * local * wl.rows * 64 * wl.heads
+    peak_tflops, _, peak_kind = load_peaks()
+    achieved = flash_flops / (flash_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API, pinned host buffers, copies timed
+    h_in = torch.from_numpy(x_local).pin_memory()
+    h_out = torch.empty_like(h_in).pin_memory()
+    if world == 1:
+        def e2e_step():
+            ctx.attention_host(LAYER, h_in, wl.gh, wl.gw, wl.views, wl.global_, out=h_out)
+    else:
+        d_in = torch.empty_like(ln1)
+        d_out = torch.empty_like(ln1)
+
+        def e2e_step():
+            d_in.copy_(h_in, non_blocking=True)
+            ctx.attention_device_sharded(LAYER, d_in, d_out, wl.gh, wl.gw, wl.views, wl.global_, stream=sp)
+            h_out.copy_(d_out, non_blocking=True)
+            stream.synchronize()
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e2e_s = 0.0
+    for _ in range(args.steps):
+        flush_buf.zero_()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        e2e_step()
+        e2e_s += time.perf_counter() - t
+    barrier()
+    e2e_s = max_over_ranks(e2e_s)
+    e2e_value = flops / (e2e_s / args.steps) / 1e12
+    # parity of the host path against the device path on this input
+    if world == 1:
+        ref_dev = out.cpu().numpy()
+        if not np.array_equal(ref_dev, h_out.numpy()):
+            raise SystemExit("e2e output differs from the device-path output")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_attention_sample(wl, args.cpu_seconds)
+        cpu = {"value": round(v, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample,
+               "cpu": cpu_info()}
+
+    if rank == 0:
+        line = {
+            "metric": "global-attention TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "ms_per_window_layer": round(ms_per_step, 4),
+            "pct_of_bf16_peak": round(100.0 * value / peak_tflops, 2),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, QK-norm gamma 1 beta 0)",
+            "config": workload_config(wl, world),
+            "roofline": {"bound": "tensor", "kernel": "flash_fwd_d64_kernel", "achieved": round(achieved, 2),
+                         "peak": peak_tflops, "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
+                         "peak_kind": f"bf16 burst ({peak_kind})", "flops_per_launch": flash_flops,
+                         "ms_per_launch": round(flash_ms, 4),
+                         "traffic": FLASH_DRAM_BYTES_PER_LAUNCH},
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
+                    "h2d_bytes_per_step": int(wl.rows * wl.embed * 4), "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),
+                    "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
+                    "pinned H2D + va_attention_device_sharded + D2H per rank"},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,176 @@
+/*
+ * vestra_attn.h -- C ABI of the B200 (sm_100a) attention path for the DA3 ViT
+ * backbone of Vestra Engine.
+ *
+ * This library replaces, on the attention path, the opt-in CUDA oracle slice of
+ * the reference (crates/da-engine/src/vit_block.rs:140-372, behind the
+ * `cuda-residual-oracle` feature) and the CPU `vestra_kernels::attention`
+ * call it falls back to.  A Rust FFI crate (vestra-cuda-sys) binds these symbols
+ * one-to-one; see INTEGRATION.md for the binding and the executor adapter.
+ *
+ * Conventions
+ *   - Every function returns an int status: VA_OK (0) or a VA_ERR_* code.  No
+ *     exceptions or panics cross the boundary, and there is NO CPU fallback: an
+ *     unsupported shape is VA_ERR_INVALID, never a silent host computation.
+ *   - va_last_error(ctx) returns a message for the last failing call on ctx.
+ *   - One context per host thread; calls on one context are serial (the
+ *     reference's executors are called serially from the block loop).
+ *   - Weight tensors use the reference's in-memory orientation: linear weights
+ *     are [in, out] row-major F32 (engine.rs:110-126 transposes GGUF's [out, in]
+ *     at load), vectors are F32.  The library converts and owns device copies.
+ *   - `stream` arguments are cudaStream_t values passed as void*; NULL is the
+ *     legacy default stream.
+ *   - Tokens are view-major: view v occupies rows [v*n, (v+1)*n) with
+ *     n = (1 + num_register) + gh*gw.
+ */
+#ifndef VESTRA_ATTN_H
+#define VESTRA_ATTN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VA_OK 0
+#define VA_ERR_INVALID 1 /* unsupported shape / bad argument (reference executor: None) */
+#define VA_ERR_CUDA 2    /* CUDA runtime failure */
+#define VA_ERR_DEVICE 3  /* a kernel gave up on a bounded wait and set the error word */
+#define VA_ERR_STATE 4   /* e.g. layer weights not loaded */
+#define VA_ERR_NCCL 5    /* communicator failure */
+
+typedef struct va_ctx va_ctx;
+
+/* Fields read by the attention path from ModelConfig (config.rs:146, from_gguf
+ * :219-264). */
+typedef struct va_config {
+  int32_t embed_dim;    /* E: 768 (DA3-BASE), 1024 (DA3-LARGE); multiple of 256 */
+  int32_t num_heads;    /* H: embed_dim / 64 */
+  int32_t head_dim;     /* must be 64 */
+  int32_t depth;        /* number of blocks whose weights the context holds */
+  int32_t num_register; /* special tokens per view = 1 + num_register (backbone.rs:347) */
+  int32_t rope_start;   /* RoPE on blocks i >= rope_start; -1 = never (vit_block.rs:839) */
+  int32_t qknorm_start; /* QK-norm on blocks i >= qknorm_start; -1 = never (:835-838) */
+  float rope_freq;      /* RoPE base, 100 for DA3 (cfg.rope_freq) */
+  float ln_eps;         /* block LayerNorm eps (cfg.ln_eps, 1e-6) */
+  float qk_norm_eps;    /* per-head QK LayerNorm eps, 1e-5 (QK_NORM_EPS, vit_block.rs:686) */
+  int32_t rope_pairing; /* 0: rotate-half pairs (i, i+16) per half (default); 1: interleaved */
+  int32_t max_rows;     /* workspace capacity in tokens (rows per call) */
+} va_config;
+
+/* Library version string, e.g. "vestra_attn 0.1 sm_100a". */
+const char* va_version(void);
+
+/* DA3-BASE defaults: E=768, H=12, d=64, depth=12, num_register=0, rope/qknorm
+ * start 4, rope_freq 100, ln_eps 1e-6, qk eps 1e-5, max_rows 12*866. */
+void va_default_config(va_config* cfg);
+
+/* Creates a context on CUDA device `device` and allocates its workspace.
+ * Replaces CudaAttentionExecutor::new / CudaTransformerTailExecutor::new
+ * (vit_block.rs:239-318, :375-397) together with the engine's
+ * enable_cuda_attention_oracle(device) (engine.rs:323). */
+int va_create(const va_config* cfg, int device, va_ctx** out);
+void va_destroy(va_ctx* ctx);
+const char* va_last_error(const va_ctx* ctx);
+
+/* Uploads one block's attention weights (names from vit_block.rs:30-53):
+ *   norm1_w/b [E]          vit.blk.{i}.norm1.{weight,bias}   (NULL: LN1 not fused)
+ *   qkv_w [E,3E], qkv_b [3E]  vit.blk.{i}.attn_qkv.*  columns [Q|K|V], each [H,64]
+ *   qnorm_w/b, knorm_w/b [64] vit.blk.{i}.attn_{q,k}norm.*    (NULL: absent tensor)
+ *   proj_w [E,E], proj_b [E]  vit.blk.{i}.attn_proj.*
+ *   ls1 [E]                vit.blk.{i}.ls1                   (NULL: absent tensor)
+ * Mirrors the per-layer uploads of CudaAttentionExecutor::new (vit_block.rs:262-316). */
+int va_load_layer(va_ctx* ctx, int layer, const float* norm1_w, const float* norm1_b,
+                  const float* qkv_w, const float* qkv_b, const float* qnorm_w,
+                  const float* qnorm_b, const float* knorm_w, const float* knorm_b,
+                  const float* proj_w, const float* proj_b, const float* ls1);
+
+/* Layer gating (vit_block.rs:835-839): use_qknorm = qknorm_start >= 0 && layer >=
+ * qknorm_start && q-norm weights present; use_rope = rope_start >= 0 && layer >=
+ * rope_start. */
+int va_layer_flags(const va_ctx* ctx, int layer, int* use_qknorm, int* use_rope);
+
+/* AttentionExecutor::run_attention (vit_block.rs:95-105, CUDA oracle :321-372):
+ * input = LN1 output [rows, E] (host F32), positions_yx = [rows, 2] integer-valued
+ * (y, x) as F32 or NULL (no RoPE), out = projected branch [rows, E] (host F32,
+ * proj*ls1, no residual).  One attention over all rows (the caller's n).  QK-norm
+ * follows the layer gating.  heads/head_dim must match the context. */
+int va_run_attention(va_ctx* ctx, int layer, const float* input, int64_t rows, int heads,
+                     int head_dim, const float* positions_yx, float* out);
+
+/* run_attention with positions derived in closed form (vit_block.rs:841-881):
+ * global = 1: one attention over all view_count*n rows, patch positions (1,1);
+ * global = 0: view_count independent attentions (one per view), patch p at
+ * (p/gw+1, p%gw+1).  Special tokens (0,0).  Host F32 in/out. */
+int va_attention_host(va_ctx* ctx, int layer, const float* ln1, int64_t rows, int gh, int gw,
+                      int view_count, int global, float* out);
+
+/* Same, device-resident: ln1_dev and out_dev are device F32 [rows, E]. */
+int va_attention_device(va_ctx* ctx, int layer, const float* ln1_dev, float* out_dev,
+                        int64_t rows, int gh, int gw, int view_count, int global, void* stream);
+
+/* Attention half of vit_block_with_views (vit_block.rs:1058-1091) on device:
+ * tokens += proj(attn(LN1(tokens))) * ls1, in place.  Needs norm1 weights. */
+int va_block_attention_device(va_ctx* ctx, int layer, float* tokens_dev, int64_t rows, int gh,
+                              int gw, int view_count, int global, void* stream);
+
+/* Op::Attention (graph.rs:67-105; CpuBackend arm cpu_backend.rs:198-298) on device:
+ * q, k, v, out [heads, n, 64] F32.  qn_g/qn_b/kn_g/kn_b [64] or NULL; pos_yx_host
+ * [n, 2] host F32 (rounded) or NULL.  q and k are not modified. */
+int va_op_attention_device(va_ctx* ctx, const float* q, const float* k, const float* v,
+                           int heads, int64_t n, int head_dim, const float* qn_g,
+                           const float* qn_b, const float* kn_g, const float* kn_b,
+                           float qk_norm_eps, const float* pos_yx_host, float freq, float* out,
+                           void* stream);
+
+/* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
+ * add the query-sharded global block: each rank owns an equal contiguous slice of
+ * the view-major window, forms K'/V for it, and one in-place NCCL all-gather
+ * assembles the window before the fused attention.  Local blocks need no
+ * communication when each rank's slice holds whole views. */
+/* Rank 0 creates the 128-byte communicator id and sends it to the other ranks. */
+int va_comm_unique_id(void* id_out);
+int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
+/* ln1_local/out_local: device F32 [local_rows, E], this rank's rows
+ * [rank*local_rows, (rank+1)*local_rows) of a window of nranks*local_rows tokens
+ * made of view_count views.  Collective: every rank calls it for the same layer. */
+int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
+                                float* out_local, int64_t local_rows, int gh, int gw,
+                                int view_count, int global, void* stream);
+
+/* Kernel-level entry points (each one launch; used by the parity tests). */
+/* K2 alone: q bf16 [q_count, heads*64] token-major, k and v bf16 [kv_rows, heads*64];
+ * query i is row q_offset + i of the key window.  seg_len = 0: every query attends
+ * to all kv_rows keys; seg_len > 0: independent segments of seg_len tokens (q_offset
+ * and q_count multiples of seg_len).  out bf16 [q_count, heads*64]. */
+int va_flash_attention_bf16(va_ctx* ctx, const void* q, const void* k, const void* v,
+                            int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
+                            int64_t seg_len, void* out, void* stream);
+/* K3-style GEMM: out[M,N] = (a[M,K] * w_t[N,K]^T + bias) * scale (+ residual), bf16
+ * in, F32 out; bias/scale/residual may be NULL.  N % 128 == 0, K % 64 == 0. */
+int va_linear_bf16(va_ctx* ctx, const void* a, const void* w_t, const float* bias,
+                   const float* scale, const float* residual, float* out, int64_t m, int n, int k,
+                   void* stream);
+
+/* Host-side view scheduling (backbone.rs:133-224, engine.rs:198-205). */
+/* select_reference_view_saddle: cls [views, embed] F32 -> reference view index. */
+int va_select_reference_view_saddle(const float* cls, int views, int embed, int* out_index);
+/* reference_first_order: order[0] = reference, then the other views ascending. */
+int va_reference_first_order(int views, int reference, int* order_out);
+/* restore_original_view_order as a gather: original view i = ordered view src_out[i]. */
+int va_restore_order(int views, int reference, int* src_out);
+/* Device helpers: camera-token slots (backbone.rs:746-768) and view permutation. */
+int va_camera_inject_device(float* tokens_dev, const float* camera_dev, int views,
+                            int64_t tokens_per_view, int embed, void* stream);
+int va_permute_views_device(const float* src_dev, float* dst_dev, const int* order_host,
+                            int views, int64_t view_elems, void* stream);
+
+/* Reads and clears the context's device error word (synchronises the context's
+ * device).  Returns VA_OK or VA_ERR_DEVICE with the code in va_last_error. */
+int va_check_device(va_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VESTRA_ATTN_H */

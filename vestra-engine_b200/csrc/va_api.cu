@@ -1,0 +1,815 @@
+// C-ABI layer: context, weight ownership, workspace, position tables and the
+// per-call launch sequence of the attention path.
+//
+// Per attention sub-block call (vit_block.rs:772-992), one rank:
+//   ln_cast  (LN1 when fused, F32 -> bf16)       [rows, E]
+//   qkv_gemm (K1: UMMA + bias/QK-norm/RoPE epi)  -> Q, K, V bf16 token-major [rows, E]
+//   [all-gather of K/V slices over NCCL when the window is sharded across GPUs]
+//   flash    (K2: fused attention)               -> O bf16 [rows, E]
+//   proj     (K3: UMMA + bias/ls1/residual epi)  -> F32 [rows, E]
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/vestra_attn.h"
+#include "va_comm.h"
+#include "va_internal.h"
+#include "va_ptx.cuh"
+
+using va::DevError;
+
+namespace {
+
+struct LayerWeights {
+  bool loaded = false;
+  __nv_bfloat16* w_qkv_t = nullptr;   // [3E][E]
+  __nv_bfloat16* w_proj_t = nullptr;  // [E][E]
+  float* qkv_b = nullptr;             // [3E]
+  float* proj_b = nullptr;            // [E]
+  float* ls1 = nullptr;               // [E] or null
+  float* norm1_w = nullptr;           // [E] or null
+  float* norm1_b = nullptr;
+  float* qn_g = nullptr;              // [64] or null (absent tensor)
+  float* qn_b = nullptr;
+  float* kn_g = nullptr;
+  float* kn_b = nullptr;
+};
+
+struct PosKey {
+  int64_t rows = -1;
+  int gh = 0, gw = 0, views = 0, global = 0, n_special = 0;
+  bool operator==(const PosKey& o) const {
+    return rows == o.rows && gh == o.gh && gw == o.gw && views == o.views && global == o.global &&
+           n_special == o.n_special;
+  }
+};
+
+}  // namespace
+
+struct va_ctx {
+  va_config cfg{};
+  int device = 0;
+  std::vector<LayerWeights> layers;
+  int64_t cap = 0;  // workspace rows
+  __nv_bfloat16* x = nullptr;  // [cap][E] LN1 output, bf16
+  __nv_bfloat16* q = nullptr;  // [cap][E] this rank's queries, token-major
+  __nv_bfloat16* k = nullptr;  // [cap][E] key window (all ranks' slices after the gather)
+  __nv_bfloat16* v = nullptr;  // [cap][E]
+  __nv_bfloat16* o = nullptr;  // [cap][E] attention output, token-major
+  float* in_f32 = nullptr;     // host-path staging [cap][E]
+  float* out_f32 = nullptr;
+  int2* pos = nullptr;         // [cap]
+  PosKey pos_key;
+  float2* rope_cs = nullptr;   // [rope_npos][16]
+  int rope_npos = 0;
+  int* err = nullptr;          // device error word
+  cudaStream_t stream = nullptr;
+  // Op::Attention scratch (grown on demand)
+  __nv_bfloat16* op_buf = nullptr;  // q|k|v bf16 [3][H*n*64]
+  size_t op_cap = 0;
+  int2* op_pos = nullptr;
+  size_t op_pos_cap = 0;
+  va::Comm* comm = nullptr;    // set by va_comm_init (multi-GPU global blocks)
+  std::string last_error;
+};
+
+namespace {
+
+int fail(va_ctx* c, int code, const std::string& msg) {
+  if (c) c->last_error = msg;
+  return code;
+}
+
+int cuda_fail(va_ctx* c, cudaError_t e, const char* what) {
+  return fail(c, VA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define VA_CUDA(ctx, call)                                   \
+  do {                                                       \
+    cudaError_t e_ = (call);                                 \
+    if (e_ != cudaSuccess) return cuda_fail(ctx, e_, #call); \
+  } while (0)
+
+template <class T>
+cudaError_t dmalloc(T** p, size_t count) {
+  return cudaMalloc(reinterpret_cast<void**>(p), std::max<size_t>(count, 1) * sizeof(T));
+}
+
+template <class T>
+void dfree(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return static_cast<uint16_t>((u >> 16) | ((u & 0xffff) ? 0x40 : 0));
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+// [in, out] F32 -> transposed [out][in] bf16 (K-major B operand).
+std::vector<uint16_t> transpose_to_bf16(const float* w, int in, int out) {
+  std::vector<uint16_t> t(static_cast<size_t>(in) * out);
+  for (int i = 0; i < in; ++i)
+    for (int o = 0; o < out; ++o) t[static_cast<size_t>(o) * in + i] = f32_to_bf16_rne(w[static_cast<size_t>(i) * out + o]);
+  return t;
+}
+
+int upload_vec(va_ctx* c, float** dst, const float* src, size_t n) {
+  if (!src) {
+    *dst = nullptr;
+    return VA_OK;
+  }
+  VA_CUDA(c, dmalloc(dst, n));
+  VA_CUDA(c, cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+  return VA_OK;
+}
+
+void free_layer(LayerWeights& l) {
+  dfree(l.w_qkv_t);
+  dfree(l.w_proj_t);
+  dfree(l.qkv_b);
+  dfree(l.proj_b);
+  dfree(l.ls1);
+  dfree(l.norm1_w);
+  dfree(l.norm1_b);
+  dfree(l.qn_g);
+  dfree(l.qn_b);
+  dfree(l.kn_g);
+  dfree(l.kn_b);
+  l.loaded = false;
+}
+
+bool layer_use_qknorm(const va_ctx* c, int layer) {
+  return c->cfg.qknorm_start >= 0 && layer >= c->cfg.qknorm_start && c->layers[layer].qn_g != nullptr;
+}
+bool layer_use_rope(const va_ctx* c, int layer) {
+  return c->cfg.rope_start >= 0 && layer >= c->cfg.rope_start;
+}
+
+// cos/sin table of pos * base^(-2i/32), i < 16, for pos in [0, npos).  Double on
+// the host, rounded to F32, like the CPU restatement.
+int ensure_rope_table(va_ctx* c, int npos) {
+  if (npos <= c->rope_npos) return VA_OK;
+  const int n = std::max(npos, 64);
+  std::vector<float2> t(static_cast<size_t>(n) * 16);
+  for (int p = 0; p < n; ++p)
+    for (int i = 0; i < 16; ++i) {
+      const double ang = p * std::pow(static_cast<double>(c->cfg.rope_freq), -(2.0 * i) / 32.0);
+      t[static_cast<size_t>(p) * 16 + i] = make_float2(static_cast<float>(std::cos(ang)),
+                                                      static_cast<float>(std::sin(ang)));
+    }
+  dfree(c->rope_cs);
+  VA_CUDA(c, dmalloc(&c->rope_cs, t.size()));
+  VA_CUDA(c, cudaMemcpy(c->rope_cs, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  c->rope_npos = n;
+  return VA_OK;
+}
+
+// Closed-form position table (vit_block.rs:841-881) into c->pos, cached.
+int ensure_positions(va_ctx* c, int64_t rows, int gh, int gw, int views, int global) {
+  const int n_special = 1 + c->cfg.num_register;
+  PosKey key{rows, gh, gw, views, global, n_special};
+  if (c->pos_key == key) return VA_OK;
+  const int64_t per_view = n_special + static_cast<int64_t>(gh) * gw;
+  if (views <= 0 || per_view * views != rows)
+    return fail(c, VA_ERR_INVALID, "rows must equal view_count * (1 + num_register + gh*gw)");
+  std::vector<int2> p(static_cast<size_t>(rows), make_int2(0, 0));
+  int maxp = 1;
+  for (int v = 0; v < views; ++v)
+    for (int64_t lt = n_special; lt < per_view; ++lt) {
+      const int64_t t = v * per_view + lt;
+      if (global) {
+        p[t] = make_int2(1, 1);
+      } else {
+        const int64_t q = lt - n_special;
+        p[t] = make_int2(static_cast<int>(q / gw + 1), static_cast<int>(q % gw + 1));
+        maxp = std::max(maxp, std::max(p[t].x, p[t].y));
+      }
+    }
+  // Kernels of an earlier call (on any stream) may still read the old table.
+  VA_CUDA(c, cudaDeviceSynchronize());
+  int rc = ensure_rope_table(c, maxp + 1);
+  if (rc) return rc;
+  VA_CUDA(c, cudaMemcpy(c->pos, p.data(), p.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  c->pos_key = key;
+  return VA_OK;
+}
+
+// Explicit F32 position table (AttentionExecutor seam) -> c->pos.
+int upload_positions(va_ctx* c, const float* pos_yx, int64_t rows, int2* dst) {
+  std::vector<int2> p(static_cast<size_t>(rows));
+  int maxp = 0;
+  for (int64_t t = 0; t < rows; ++t) {
+    const long long y = std::llround(pos_yx[2 * t]), x = std::llround(pos_yx[2 * t + 1]);
+    if (y < 0 || x < 0 || y > 65535 || x > 65535)
+      return fail(c, VA_ERR_INVALID, "RoPE positions must be integers in [0, 65535]");
+    p[t] = make_int2(static_cast<int>(y), static_cast<int>(x));
+    maxp = std::max(maxp, static_cast<int>(std::max(y, x)));
+  }
+  VA_CUDA(c, cudaDeviceSynchronize());  // the old table may still be in use
+  int rc = ensure_rope_table(c, maxp + 1);
+  if (rc) return rc;
+  VA_CUDA(c, cudaMemcpy(dst, p.data(), p.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  c->pos_key = PosKey{};  // the cached closed-form table was overwritten
+  return VA_OK;
+}
+
+int check_layer(va_ctx* c, int layer) {
+  if (layer < 0 || layer >= static_cast<int>(c->layers.size()))
+    return fail(c, VA_ERR_INVALID, "layer index out of range");
+  if (!c->layers[layer].loaded) return fail(c, VA_ERR_STATE, "layer weights not loaded");
+  return VA_OK;
+}
+
+// One rank's share of an attention sub-block.  The key window holds window_rows
+// tokens; this rank owns rows [row_offset, row_offset + rows) of it (single GPU:
+// row_offset 0, rows == window_rows).
+struct BranchSpec {
+  const float* in;        // F32 [rows, E]: LN1 output, or raw tokens when apply_ln1
+  bool apply_ln1;
+  float* out;             // F32 [rows, E]
+  const float* residual;  // F32 [rows, E] added in the epilogue, or nullptr
+  int64_t rows;
+  int64_t row_offset;
+  int64_t window_rows;
+  const int2* pos;        // positions of the window (nullptr: no RoPE)
+  int seg_len;            // 0: global attention over the window; > 0: per-view segments
+  bool gather;            // all-gather K/V slices of every rank before the attention
+};
+
+// In-place all-gather of this rank's K'/V slices into the window buffers.
+int gather_kv(va_ctx* c, const __nv_bfloat16* k_slice, const __nv_bfloat16* v_slice, int64_t rows,
+              cudaStream_t st) {
+  if (!c->comm) return fail(c, VA_ERR_STATE, "no communicator (va_comm_init)");
+  const size_t per_rank = static_cast<size_t>(rows) * c->cfg.embed_dim;
+  if (k_slice != c->k + per_rank * va::comm_rank(c->comm) ||
+      v_slice != c->v + per_rank * va::comm_rank(c->comm))
+    return fail(c, VA_ERR_INVALID, "sharded slices must be rank-ordered and equal");
+  std::string err;
+  if (!va::comm_allgather_inplace2(c->comm, c->k, c->v, per_rank, st, &err))
+    return fail(c, VA_ERR_NCCL, err);
+  return VA_OK;
+}
+
+int segments_for(va_ctx* c, int64_t rows, int view_count, int global, int* seg_len) {
+  if (view_count <= 0 || rows % view_count != 0)
+    return fail(c, VA_ERR_INVALID, "rows must be a multiple of view_count");
+  *seg_len = global ? 0 : static_cast<int>(rows / view_count);
+  return VA_OK;
+}
+
+// The device launch sequence of one attention sub-block (see the file header).
+int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
+  const LayerWeights& w = c->layers[layer];
+  const int E = c->cfg.embed_dim;
+  const int64_t rows = b.rows;
+  if (rows <= 0 || b.window_rows > c->cap || b.row_offset + rows > b.window_rows)
+    return fail(c, VA_ERR_INVALID, "rows exceed the context's max_rows");
+  if (b.window_rows > 0x7fffffff / 64) return fail(c, VA_ERR_INVALID, "rows too large");
+  if (b.apply_ln1 && !w.norm1_w) return fail(c, VA_ERR_STATE, "norm1 weights not loaded");
+  if (b.seg_len > 0 && (rows % b.seg_len != 0 || b.row_offset % b.seg_len != 0))
+    return fail(c, VA_ERR_INVALID, "a rank's rows must hold whole views in local blocks");
+  VA_CUDA(c, va::launch_ln_cast(b.in, b.apply_ln1 ? w.norm1_w : nullptr, w.norm1_b,
+                                c->cfg.ln_eps, static_cast<int>(rows), E, c->x, st));
+  __nv_bfloat16* k_slice = c->k + b.row_offset * E;
+  __nv_bfloat16* v_slice = c->v + b.row_offset * E;
+  va::QkvEpilogueArgs qa{};
+  qa.bias = w.qkv_b;
+  const bool qk = layer_use_qknorm(c, layer);
+  qa.q_g = qk ? w.qn_g : nullptr;
+  qa.q_b = qk ? w.qn_b : nullptr;
+  qa.k_g = qk ? w.kn_g : nullptr;
+  qa.k_b = qk ? w.kn_b : nullptr;
+  qa.qk_eps = c->cfg.qk_norm_eps;
+  qa.pos = b.pos ? b.pos + b.row_offset : nullptr;
+  qa.rope_cs = c->rope_cs;
+  qa.rope_pairing = c->cfg.rope_pairing;
+  qa.q_out = c->q;
+  qa.k_out = k_slice;
+  qa.v_out = v_slice;
+  qa.rows = static_cast<int>(rows);
+  qa.embed = E;
+  VA_CUDA(c, va::launch_qkv_gemm(c->x, w.w_qkv_t, static_cast<int>(rows), E, qa, c->err, st));
+  va::FlashArgs fa{};
+  fa.q_count = static_cast<int>(rows);
+  fa.seg_len = b.seg_len;
+  fa.heads = c->cfg.num_heads;
+  fa.scale_log2 = static_cast<float>(1.0 / std::sqrt(64.0) * 1.4426950408889634);
+  fa.out_mode = 0;
+  fa.o_tok = c->o;
+  fa.embed = E;
+  const __nv_bfloat16* kk = c->k;
+  const __nv_bfloat16* vv = c->v;
+  if (b.gather) {
+    int rc = gather_kv(c, k_slice, v_slice, rows, st);
+    if (rc) return rc;
+    fa.q_offset = static_cast<int>(b.row_offset);
+    fa.kv_rows = static_cast<int>(b.window_rows);
+  } else if (b.seg_len > 0) {
+    // Local blocks: every key a query needs lives in this rank's own slice.
+    kk = k_slice;
+    vv = v_slice;
+    fa.q_offset = 0;
+    fa.kv_rows = static_cast<int>(rows);
+  } else {
+    if (rows != b.window_rows)
+      return fail(c, VA_ERR_INVALID, "global attention over a sharded window needs the communicator");
+    fa.q_offset = 0;
+    fa.kv_rows = static_cast<int>(rows);
+  }
+  VA_CUDA(c, va::launch_flash(c->q, kk, vv, fa, c->err, st));
+  va::ProjEpilogueArgs pa{};
+  pa.bias = w.proj_b;
+  pa.ls1 = w.ls1;
+  pa.residual = b.residual;
+  pa.out = b.out;
+  pa.rows = static_cast<int>(rows);
+  pa.embed = E;
+  VA_CUDA(c, va::launch_proj_gemm(c->o, w.w_proj_t, static_cast<int>(rows), E, E, pa, c->err, st));
+  return VA_OK;
+}
+
+int read_device_error(va_ctx* c) {
+  int h = 0;
+  VA_CUDA(c, cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h != 0) {
+    cudaMemset(c->err, 0, sizeof(int));
+    char buf[128];
+    std::snprintf(buf, sizeof(buf), "device error word %d (a bounded wait timed out)", h);
+    return fail(c, VA_ERR_DEVICE, buf);
+  }
+  return VA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* va_version(void) { return "vestra_attn 0.1 sm_100a"; }
+
+void va_default_config(va_config* cfg) {
+  if (!cfg) return;
+  cfg->embed_dim = 768;
+  cfg->num_heads = 12;
+  cfg->head_dim = 64;
+  cfg->depth = 12;
+  cfg->num_register = 0;
+  cfg->rope_start = 4;
+  cfg->qknorm_start = 4;
+  cfg->rope_freq = 100.0f;
+  cfg->ln_eps = 1e-6f;
+  cfg->qk_norm_eps = 1e-5f;
+  cfg->rope_pairing = 0;
+  cfg->max_rows = 12 * 866;
+}
+
+int va_create(const va_config* cfg, int device, va_ctx** out) {
+  if (!cfg || !out) return VA_ERR_INVALID;
+  *out = nullptr;
+  if (cfg->head_dim != 64 || cfg->embed_dim != cfg->num_heads * 64 || cfg->embed_dim % 256 != 0 ||
+      cfg->depth <= 0 || cfg->max_rows <= 0 || cfg->num_register < 0 ||
+      (cfg->rope_pairing != 0 && cfg->rope_pairing != 1))
+    return VA_ERR_INVALID;
+  va_ctx* c = new (std::nothrow) va_ctx();
+  if (!c) return VA_ERR_INVALID;
+  c->cfg = *cfg;
+  c->device = device;
+  c->layers.resize(cfg->depth);
+  c->cap = cfg->max_rows;
+  auto bail = [&](cudaError_t e) {
+    va_destroy(c);
+    (void)e;
+    return VA_ERR_CUDA;
+  };
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return bail(e);
+  const size_t E = cfg->embed_dim;
+  const size_t n = static_cast<size_t>(c->cap) * E;
+  if ((e = dmalloc(&c->x, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->q, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->k, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->v, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->o, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->in_f32, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->out_f32, n)) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->pos, static_cast<size_t>(c->cap))) != cudaSuccess) return bail(e);
+  if ((e = dmalloc(&c->err, 1)) != cudaSuccess) return bail(e);
+  if ((e = cudaMemset(c->err, 0, sizeof(int))) != cudaSuccess) return bail(e);
+  if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
+  if (ensure_rope_table(c, 128) != VA_OK) return bail(cudaErrorMemoryAllocation);
+  *out = c;
+  return VA_OK;
+}
+
+void va_destroy(va_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  for (auto& l : c->layers) free_layer(l);
+  dfree(c->x);
+  dfree(c->q);
+  dfree(c->k);
+  dfree(c->v);
+  dfree(c->o);
+  dfree(c->in_f32);
+  dfree(c->out_f32);
+  dfree(c->pos);
+  dfree(c->rope_cs);
+  dfree(c->err);
+  dfree(c->op_buf);
+  dfree(c->op_pos);
+  if (c->comm) va::comm_destroy(c->comm, false);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+const char* va_last_error(const va_ctx* c) { return c ? c->last_error.c_str() : "null context"; }
+
+int va_load_layer(va_ctx* c, int layer, const float* norm1_w, const float* norm1_b,
+                  const float* qkv_w, const float* qkv_b, const float* qnorm_w,
+                  const float* qnorm_b, const float* knorm_w, const float* knorm_b,
+                  const float* proj_w, const float* proj_b, const float* ls1) {
+  if (!c) return VA_ERR_INVALID;
+  if (layer < 0 || layer >= c->cfg.depth) return fail(c, VA_ERR_INVALID, "layer index out of range");
+  if (!qkv_w || !qkv_b || !proj_w || !proj_b)
+    return fail(c, VA_ERR_INVALID, "qkv and proj weights are required");
+  if ((qnorm_w == nullptr) != (knorm_w == nullptr) || (qnorm_w && (!qnorm_b || !knorm_b)))
+    return fail(c, VA_ERR_INVALID, "q-norm and k-norm tensors must be given together");
+  if ((norm1_w == nullptr) != (norm1_b == nullptr))
+    return fail(c, VA_ERR_INVALID, "norm1 weight and bias must be given together");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  LayerWeights& l = c->layers[layer];
+  free_layer(l);
+  const int E = c->cfg.embed_dim;
+  std::vector<uint16_t> wq = transpose_to_bf16(qkv_w, E, 3 * E);
+  std::vector<uint16_t> wp = transpose_to_bf16(proj_w, E, E);
+  VA_CUDA(c, dmalloc(&l.w_qkv_t, wq.size()));
+  VA_CUDA(c, cudaMemcpy(l.w_qkv_t, wq.data(), wq.size() * 2, cudaMemcpyHostToDevice));
+  VA_CUDA(c, dmalloc(&l.w_proj_t, wp.size()));
+  VA_CUDA(c, cudaMemcpy(l.w_proj_t, wp.data(), wp.size() * 2, cudaMemcpyHostToDevice));
+  int rc;
+  if ((rc = upload_vec(c, &l.qkv_b, qkv_b, 3 * E))) return rc;
+  if ((rc = upload_vec(c, &l.proj_b, proj_b, E))) return rc;
+  if ((rc = upload_vec(c, &l.ls1, ls1, E))) return rc;
+  if ((rc = upload_vec(c, &l.norm1_w, norm1_w, E))) return rc;
+  if ((rc = upload_vec(c, &l.norm1_b, norm1_b, E))) return rc;
+  if ((rc = upload_vec(c, &l.qn_g, qnorm_w, 64))) return rc;
+  if ((rc = upload_vec(c, &l.qn_b, qnorm_b, 64))) return rc;
+  if ((rc = upload_vec(c, &l.kn_g, knorm_w, 64))) return rc;
+  if ((rc = upload_vec(c, &l.kn_b, knorm_b, 64))) return rc;
+  l.loaded = true;
+  return VA_OK;
+}
+
+int va_layer_flags(const va_ctx* c, int layer, int* use_qknorm, int* use_rope) {
+  if (!c || layer < 0 || layer >= c->cfg.depth) return VA_ERR_INVALID;
+  if (use_qknorm) *use_qknorm = layer_use_qknorm(c, layer) ? 1 : 0;
+  if (use_rope) *use_rope = layer_use_rope(c, layer) ? 1 : 0;
+  return VA_OK;
+}
+
+int va_run_attention(va_ctx* c, int layer, const float* input, int64_t rows, int heads,
+                     int head_dim, const float* positions_yx, float* out) {
+  if (!c || !input || !out) return VA_ERR_INVALID;
+  int rc = check_layer(c, layer);
+  if (rc) return rc;
+  if (heads != c->cfg.num_heads || head_dim != c->cfg.head_dim || rows <= 0)
+    return fail(c, VA_ERR_INVALID, "heads/head_dim do not match the context");
+  if (rows > c->cap) return fail(c, VA_ERR_INVALID, "rows exceed the context's max_rows");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  const int2* pos = nullptr;
+  if (positions_yx) {
+    VA_CUDA(c, cudaStreamSynchronize(c->stream));  // c->pos may still be read by a previous call
+    if ((rc = upload_positions(c, positions_yx, rows, c->pos))) return rc;
+    pos = c->pos;
+  }
+  const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
+  VA_CUDA(c, cudaMemcpyAsync(c->in_f32, input, bytes, cudaMemcpyHostToDevice, c->stream));
+  BranchSpec b{c->in_f32, false, c->out_f32, nullptr, rows, 0, rows, pos, 0, false};
+  if ((rc = run_branch(c, layer, b, c->stream))) return rc;
+  VA_CUDA(c, cudaMemcpyAsync(out, c->out_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  return read_device_error(c);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Shared body of the closed-form-position entry points.  window_rows = the whole
+// view-major window (all ranks); local_rows = this rank's slice.
+int device_call(va_ctx* c, int layer, const float* in, bool apply_ln1, float* out,
+                const float* residual, int64_t window_rows, int64_t local_rows, int64_t row_offset,
+                int gh, int gw, int view_count, int global, bool sharded, cudaStream_t st) {
+  int rc = check_layer(c, layer);
+  if (rc) return rc;
+  if (window_rows <= 0 || window_rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  int seg_len;
+  if ((rc = segments_for(c, window_rows, view_count, global, &seg_len))) return rc;
+  const int2* pos = nullptr;
+  if (layer_use_rope(c, layer)) {
+    if ((rc = ensure_positions(c, window_rows, gh, gw, view_count, global))) return rc;
+    pos = c->pos;
+  }
+  BranchSpec b{in, apply_ln1, out, residual, local_rows, row_offset, window_rows, pos, seg_len,
+               sharded && global};
+  return run_branch(c, layer, b, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int gh, int gw,
+                      int view_count, int global, float* out) {
+  if (!c || !ln1 || !out) return VA_ERR_INVALID;
+  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
+  VA_CUDA(c, cudaMemcpyAsync(c->in_f32, ln1, bytes, cudaMemcpyHostToDevice, c->stream));
+  int rc = device_call(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
+                       view_count, global, false, c->stream);
+  if (rc) return rc;
+  VA_CUDA(c, cudaMemcpyAsync(out, c->out_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  return read_device_error(c);
+}
+
+int va_attention_device(va_ctx* c, int layer, const float* ln1_dev, float* out_dev, int64_t rows,
+                        int gh, int gw, int view_count, int global, void* stream) {
+  if (!c || !ln1_dev || !out_dev) return VA_ERR_INVALID;
+  return device_call(c, layer, ln1_dev, false, out_dev, nullptr, rows, rows, 0, gh, gw, view_count,
+                     global, false, static_cast<cudaStream_t>(stream));
+}
+
+int va_block_attention_device(va_ctx* c, int layer, float* tokens_dev, int64_t rows, int gh,
+                              int gw, int view_count, int global, void* stream) {
+  if (!c || !tokens_dev) return VA_ERR_INVALID;
+  return device_call(c, layer, tokens_dev, true, tokens_dev, tokens_dev, rows, rows, 0, gh, gw,
+                     view_count, global, false, static_cast<cudaStream_t>(stream));
+}
+
+int va_comm_unique_id(void* id_out) {
+  if (!id_out) return VA_ERR_INVALID;
+  std::string err;
+  return va::comm_unique_id(id_out, &err) ? VA_OK : VA_ERR_NCCL;
+}
+
+int va_comm_init(va_ctx* c, const void* id, int nranks, int rank) {
+  if (!c || !id || nranks <= 0 || rank < 0 || rank >= nranks) return VA_ERR_INVALID;
+  VA_CUDA(c, cudaSetDevice(c->device));
+  if (c->comm) {
+    va::comm_destroy(c->comm, false);
+    c->comm = nullptr;
+  }
+  std::string err;
+  c->comm = va::comm_init(id, nranks, rank, &err);
+  return c->comm ? VA_OK : fail(c, VA_ERR_NCCL, err);
+}
+
+int va_attention_device_sharded(va_ctx* c, int layer, const float* ln1_local, float* out_local,
+                                int64_t local_rows, int gh, int gw, int view_count, int global,
+                                void* stream) {
+  if (!c || !ln1_local || !out_local) return VA_ERR_INVALID;
+  const int nranks = c->comm ? va::comm_size(c->comm) : 1;
+  const int rank = c->comm ? va::comm_rank(c->comm) : 0;
+  if (global && !c->comm) return fail(c, VA_ERR_STATE, "no communicator (va_comm_init)");
+  return device_call(c, layer, ln1_local, false, out_local, nullptr, local_rows * nranks, local_rows,
+                     local_rows * rank, gh, gw, view_count, global, true,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int va_op_attention_device(va_ctx* c, const float* q, const float* k, const float* v, int heads,
+                           int64_t n, int head_dim, const float* qn_g, const float* qn_b,
+                           const float* kn_g, const float* kn_b, float qk_norm_eps,
+                           const float* pos_yx_host, float freq, float* out, void* stream) {
+  if (!c || !q || !k || !v || !out) return VA_ERR_INVALID;
+  if (head_dim != 64) return fail(c, VA_ERR_INVALID, "Op::Attention on device needs head_dim 64");
+  if (heads <= 0 || n <= 0 || static_cast<int64_t>(heads) * n > 0x7fffffff / 64)
+    return fail(c, VA_ERR_INVALID, "bad heads/n");
+  if ((qn_g == nullptr) != (qn_b == nullptr) || (kn_g == nullptr) != (kn_b == nullptr))
+    return fail(c, VA_ERR_INVALID, "norm gamma and beta must be given together");
+  if (pos_yx_host && freq != c->cfg.rope_freq)
+    return fail(c, VA_ERR_INVALID, "RoPE base must equal the context's rope_freq");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t per = static_cast<size_t>(heads) * n * 64;
+  if (3 * per > c->op_cap) {
+    dfree(c->op_buf);
+    VA_CUDA(c, dmalloc(&c->op_buf, 3 * per));
+    c->op_cap = 3 * per;
+  }
+  int2* pos = nullptr;
+  if (pos_yx_host) {
+    if (static_cast<size_t>(n) > c->op_pos_cap) {
+      dfree(c->op_pos);
+      VA_CUDA(c, dmalloc(&c->op_pos, static_cast<size_t>(n)));
+      c->op_pos_cap = n;
+    }
+    VA_CUDA(c, cudaStreamSynchronize(st));  // op_pos may still be read by an earlier call
+    int rc = upload_positions(c, pos_yx_host, n, c->op_pos);
+    if (rc) return rc;
+    pos = c->op_pos;
+  }
+  __nv_bfloat16* qb = c->op_buf;
+  __nv_bfloat16* kb = c->op_buf + per;
+  __nv_bfloat16* vb = c->op_buf + 2 * per;
+  VA_CUDA(c, va::launch_prep_heads(q, heads, static_cast<int>(n), qn_g, qn_b, qk_norm_eps, pos,
+                                   c->rope_cs, c->cfg.rope_pairing, qb, st));
+  VA_CUDA(c, va::launch_prep_heads(k, heads, static_cast<int>(n), kn_g, kn_b, qk_norm_eps, pos,
+                                   c->rope_cs, c->cfg.rope_pairing, kb, st));
+  VA_CUDA(c, va::launch_prep_heads(v, heads, static_cast<int>(n), nullptr, nullptr, 0.f, nullptr,
+                                   nullptr, 0, vb, st));
+  va::FlashArgs fa{};
+  fa.q_count = static_cast<int>(n);
+  fa.q_offset = 0;
+  fa.kv_rows = static_cast<int>(n);
+  fa.seg_len = 0;
+  fa.heads = heads;
+  fa.scale_log2 = static_cast<float>(1.0 / 8.0 * 1.4426950408889634);
+  fa.out_mode = 1;
+  fa.o_hnd = out;
+  fa.embed = heads * 64;
+  VA_CUDA(c, va::launch_flash(qb, kb, vb, fa, c->err, st));
+  return VA_OK;
+}
+
+int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void* v,
+                            int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
+                            int64_t seg_len, void* out, void* stream) {
+  if (!c || !q || !k || !v || !out) return VA_ERR_INVALID;
+  if (q_count <= 0 || kv_rows <= 0 || heads <= 0 || seg_len < 0 || q_offset < 0 ||
+      kv_rows > 0x7fffffff / 64 / heads || q_count > kv_rows)
+    return fail(c, VA_ERR_INVALID, "bad flash shape");
+  if (seg_len > 0 && (q_count % seg_len || q_offset % seg_len || q_offset + q_count > kv_rows))
+    return fail(c, VA_ERR_INVALID, "local attention needs whole segments inside the key rows");
+  va::FlashArgs fa{};
+  fa.q_count = static_cast<int>(q_count);
+  fa.q_offset = static_cast<int>(q_offset);
+  fa.kv_rows = static_cast<int>(kv_rows);
+  fa.seg_len = static_cast<int>(seg_len);
+  fa.heads = heads;
+  fa.scale_log2 = static_cast<float>(1.0 / 8.0 * 1.4426950408889634);
+  fa.out_mode = 0;
+  fa.o_tok = static_cast<__nv_bfloat16*>(out);
+  fa.embed = heads * 64;
+  VA_CUDA(c, va::launch_flash(static_cast<const __nv_bfloat16*>(q),
+                              static_cast<const __nv_bfloat16*>(k),
+                              static_cast<const __nv_bfloat16*>(v), fa, c->err,
+                              static_cast<cudaStream_t>(stream)));
+  return VA_OK;
+}
+
+int va_linear_bf16(va_ctx* c, const void* a, const void* w_t, const float* bias, const float* scale,
+                   const float* residual, float* out, int64_t m, int n, int k, void* stream) {
+  if (!c || !a || !w_t || !out) return VA_ERR_INVALID;
+  if (m <= 0 || m > 0x7fffffff || n % 128 != 0 || k % 64 != 0 || n <= 0 || k <= 0)
+    return fail(c, VA_ERR_INVALID, "linear needs n % 128 == 0 and k % 64 == 0");
+  va::ProjEpilogueArgs pa{};
+  pa.bias = bias;
+  pa.ls1 = scale;
+  pa.residual = residual;
+  pa.out = out;
+  pa.rows = static_cast<int>(m);
+  pa.embed = n;
+  cudaError_t e = va::launch_proj_gemm(static_cast<const __nv_bfloat16*>(a),
+                                       static_cast<const __nv_bfloat16*>(w_t), static_cast<int>(m),
+                                       n, k, pa, c->err, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(c, e, "launch_proj_gemm");
+  return VA_OK;
+}
+
+int va_select_reference_view_saddle(const float* cls, int views, int embed, int* out_index) {
+  if (!cls || !out_index || views <= 0) return VA_ERR_INVALID;
+  if (views == 1) {
+    *out_index = 0;
+    return VA_OK;
+  }
+  if (embed <= 1) return VA_ERR_INVALID;
+  // backbone.rs:133-206: normalised CLS rows, mean cosine similarity to the other
+  // views, vector norm and unbiased variance of the normalised row; each min-max
+  // normalised (denominator + 1e-8); the view minimising the summed distance to
+  // 0.5 wins, ties keep the earliest view.
+  std::vector<double> norm(views), sim(views, 0.0), var(views, 0.0);
+  std::vector<double> nz(static_cast<size_t>(views) * embed);
+  for (int v = 0; v < views; ++v) {
+    double s = 0.0;
+    for (int e = 0; e < embed; ++e) {
+      const double x = cls[static_cast<size_t>(v) * embed + e];
+      s += x * x;
+    }
+    const double mag = std::sqrt(s);
+    norm[v] = mag;
+    const double inv = mag > 0.0 ? 1.0 / mag : 0.0;
+    for (int e = 0; e < embed; ++e)
+      nz[static_cast<size_t>(v) * embed + e] = static_cast<double>(cls[static_cast<size_t>(v) * embed + e]) * inv;
+  }
+  for (int v = 0; v < views; ++v) {
+    for (int o = 0; o < views; ++o) {
+      if (o == v) continue;
+      double d = 0.0;
+      for (int e = 0; e < embed; ++e) d += nz[static_cast<size_t>(v) * embed + e] * nz[static_cast<size_t>(o) * embed + e];
+      sim[v] += d;
+    }
+    sim[v] /= static_cast<double>(views - 1);
+    double mean = 0.0;
+    for (int e = 0; e < embed; ++e) mean += nz[static_cast<size_t>(v) * embed + e];
+    mean /= embed;
+    double acc = 0.0;
+    for (int e = 0; e < embed; ++e) {
+      const double d = nz[static_cast<size_t>(v) * embed + e] - mean;
+      acc += d * d;
+    }
+    var[v] = acc / static_cast<double>(embed - 1);
+  }
+  auto norm01 = [](std::vector<double>& x) {
+    double lo = INFINITY, hi = -INFINITY;
+    for (double y : x) {
+      lo = std::min(lo, y);
+      hi = std::max(hi, y);
+    }
+    const double den = hi - lo + 1e-8;
+    for (double& y : x) y = (y - lo) / den;
+  };
+  norm01(sim);
+  norm01(norm);
+  norm01(var);
+  int best = 0;
+  double best_b = INFINITY;
+  for (int v = 0; v < views; ++v) {
+    const double b = std::fabs(sim[v] - 0.5) + std::fabs(norm[v] - 0.5) + std::fabs(var[v] - 0.5);
+    if (b < best_b) {
+      best_b = b;
+      best = v;
+    }
+  }
+  *out_index = best;
+  return VA_OK;
+}
+
+int va_reference_first_order(int views, int reference, int* order_out) {
+  if (!order_out || views <= 0 || reference < 0 || reference >= views) return VA_ERR_INVALID;
+  int i = 0;
+  order_out[i++] = reference;
+  for (int v = 0; v < views; ++v)
+    if (v != reference) order_out[i++] = v;
+  return VA_OK;
+}
+
+int va_restore_order(int views, int reference, int* src_out) {
+  if (!src_out || views <= 0 || reference < 0 || reference >= views) return VA_ERR_INVALID;
+  // ordered position p holds original view order[p]; invert it.
+  std::vector<int> order(views);
+  va_reference_first_order(views, reference, order.data());
+  for (int p = 0; p < views; ++p) src_out[order[p]] = p;
+  return VA_OK;
+}
+
+int va_camera_inject_device(float* tokens_dev, const float* camera_dev, int views,
+                            int64_t tokens_per_view, int embed, void* stream) {
+  if (!tokens_dev || !camera_dev || views <= 0 || tokens_per_view <= 0 || embed <= 0 ||
+      tokens_per_view > 0x7fffffff)
+    return VA_ERR_INVALID;
+  return va::launch_camera_inject(tokens_dev, camera_dev, views, static_cast<int>(tokens_per_view),
+                                  embed, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? VA_OK
+             : VA_ERR_CUDA;
+}
+
+int va_permute_views_device(const float* src_dev, float* dst_dev, const int* order_host, int views,
+                            int64_t view_elems, void* stream) {
+  if (!src_dev || !dst_dev || !order_host || views <= 0 || view_elems <= 0 || src_dev == dst_dev)
+    return VA_ERR_INVALID;
+  std::vector<int> seen(views, 0);
+  for (int i = 0; i < views; ++i) {
+    if (order_host[i] < 0 || order_host[i] >= views || seen[order_host[i]]++) return VA_ERR_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* d_order = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&d_order), sizeof(int) * views, st) != cudaSuccess)
+    return VA_ERR_CUDA;
+  if (cudaMemcpyAsync(d_order, order_host, sizeof(int) * views, cudaMemcpyHostToDevice, st) !=
+      cudaSuccess)
+    return VA_ERR_CUDA;
+  const cudaError_t e = va::launch_permute_views(src_dev, dst_dev, d_order, views, view_elems, st);
+  cudaFreeAsync(d_order, st);
+  if (e != cudaSuccess) return VA_ERR_CUDA;
+  // order_host is pageable: the H2D copy above completed before returning.
+  return VA_OK;
+}
+
+int va_check_device(va_ctx* c) {
+  if (!c) return VA_ERR_INVALID;
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaDeviceSynchronize());
+  return read_device_error(c);
+}
+
+}  // extern "C"

@@ -1,0 +1,320 @@
+// K1 / K3: tcgen05 BF16 GEMMs with fused epilogues.
+//
+//   C[M, N] = A[M, K] * B[N, K]^T        (both operands K-major in HBM)
+//
+// K1 (QKV projection, vit_block.rs:803-831 + :895-948): A = LN1 output (bf16),
+//   B = W_qkv^T [3E, E].  Epilogue per 64-column head chunk: + bias, then for the
+//   Q and K sections per-head LayerNorm (eps 1e-5, vit_block.rs:686) and 2D RoPE,
+//   cast to bf16 and store token-major [rows][E] per section (the split_qkv layout
+//   transform: head h occupies columns [64h, 64h+64), one 128-B row per thread).
+// K3 (output projection, vit_block.rs:969-979 -> run_linear :721-761): A = attention
+//   output O (token-major bf16), B = W_proj^T [E, E].  Epilogue: + bias, * ls1 when
+//   present, + residual when asked (vit_block.rs:1090), F32 store.
+//
+// Structure: one 128 x BN output tile per CTA, 6 warps.
+//   warp 0      TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1      TMEM allocator + single-thread UMMA issuer (M=128, N=BN, K=16 steps)
+//   warps 2..5  epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (tile rows), one
+//               row per thread, 32 columns per tcgen05.ld.
+// Operands arrive through TMA with SWIZZLE_128B (64 bf16 = one 128-B row per
+// box row), which is exactly the UMMA K-major SW128 canonical layout.
+#include <math.h>
+
+#include "va_internal.h"
+#include "va_ptx.cuh"
+
+namespace va {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+__device__ __forceinline__ float ln_rsqrt(float var_eps) { return 1.0f / sqrtf(var_eps); }
+
+// LayerNorm of one 64-wide head row held in registers (torch semantics).
+__device__ __forceinline__ void head_layernorm(float* x, const float* g, const float* b, float eps) {
+  float mean = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) mean += x[i];
+  mean *= (1.0f / 64.0f);
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float d = x[i] - mean;
+    var += d * d;
+  }
+  var *= (1.0f / 64.0f);
+  const float inv = ln_rsqrt(var + eps);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) x[i] = (x[i] - mean) * inv * __ldg(g + i) + __ldg(b + i);
+}
+
+// 2D RoPE of one 64-wide head row: channels [0,32) rotate with y, [32,64) with x.
+__device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, int pairing) {
+#pragma unroll
+  for (int axis = 0; axis < 2; ++axis) {
+    const int p = axis == 0 ? pos.x : pos.y;
+    const float2* row = cs + p * 16;
+    float* seg = x + axis * 32;
+    if (pairing == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 c = __ldg(row + i);
+        const float a = seg[i], bb = seg[i + 16];
+        seg[i] = a * c.x - bb * c.y;
+        seg[i + 16] = bb * c.x + a * c.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 c = __ldg(row + i);
+        const float a = seg[2 * i], bb = seg[2 * i + 1];
+        seg[2 * i] = a * c.x - bb * c.y;
+        seg[2 * i + 1] = bb * c.x + a * c.y;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16_row64(__nv_bfloat16* dst, const float* x) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 u;
+    u.x = pack_bf16x2(x[8 * c + 0], x[8 * c + 1]);
+    u.y = pack_bf16x2(x[8 * c + 2], x[8 * c + 3]);
+    u.z = pack_bf16x2(x[8 * c + 4], x[8 * c + 5]);
+    u.w = pack_bf16x2(x[8 * c + 6], x[8 * c + 7]);
+    d[c] = u;
+  }
+}
+
+struct QkvEpilogue {
+  QkvEpilogueArgs a;
+  template <int BN>
+  __device__ __forceinline__ void run(uint32_t tmem_row, int grow, bool valid, int n0) const {
+    const int section = n0 / a.embed;         // 0 = Q, 1 = K, 2 = V
+    const int h0 = (n0 - section * a.embed) / 64;
+    __nv_bfloat16* base = section == 0 ? a.q_out : (section == 1 ? a.k_out : a.v_out);
+    const float* g = section == 0 ? a.q_g : a.k_g;
+    const float* b = section == 0 ? a.q_b : a.k_b;
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 64; ++hh) {
+      float x[64];
+      tmem_ld32(tmem_row + hh * 64, x);
+      tmem_ld32(tmem_row + hh * 64 + 32, x + 32);
+      if (!valid) continue;
+      const float* bias = a.bias + n0 + hh * 64;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) x[i] += __ldg(bias + i);
+      if (section < 2) {
+        if (g) head_layernorm(x, g, b, a.qk_eps);
+        if (a.pos) head_rope(x, a.pos[grow], a.rope_cs, a.rope_pairing);
+      }
+      store_bf16_row64(base + static_cast<size_t>(grow) * a.embed + (h0 + hh) * 64, x);
+    }
+  }
+};
+
+struct ProjEpilogue {
+  ProjEpilogueArgs a;
+  template <int BN>
+  __device__ __forceinline__ void run(uint32_t tmem_row, int grow, bool valid, int n0) const {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float x[32];
+      tmem_ld32(tmem_row + c * 32, x);
+      if (!valid) continue;
+      const int n = n0 + c * 32;
+      const size_t off = static_cast<size_t>(grow) * a.embed + n;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float y = x[i] + (a.bias ? __ldg(a.bias + n + i) : 0.f);
+        if (a.ls1) y *= __ldg(a.ls1 + n + i);
+        x[i] = y;
+      }
+      if (a.residual) {
+        const float4* r = reinterpret_cast<const float4*>(a.residual + off);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 rv = r[i];
+          x[4 * i] += rv.x;
+          x[4 * i + 1] += rv.y;
+          x[4 * i + 2] += rv.z;
+          x[4 * i + 3] += rv.w;
+        }
+      }
+      float4* d = reinterpret_cast<float4*>(a.out + off);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+    }
+  }
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t kABytes = kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarOffset = STAGES * kStageBytes;
+  static constexpr uint32_t kBytes = kBarOffset + 256;  // barriers + tmem slot + flags
+  static constexpr uint32_t kLaunchBytes = kBytes + 1024;  // slack for 1024-B alignment
+};
+
+// Waits (bounded, ignoring the abort flag) so that nothing asynchronous still
+// targets this CTA's shared memory or TMEM when it tears down after an abort.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+}
+
+template <int BN, int STAGES, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_b, int M, int K, Epi epi, int* err) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * BN;
+  const int num_kb = K / kBK;
+
+  const uint32_t bar0 = base_u32 + L::kBarOffset;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  const uint32_t accum_bar = bar0 + 8u * (2 * STAGES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kBarOffset + 8 * (2 * STAGES + 1));
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* issued = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* consumed = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* accum_seen = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  auto sA = [&](int s) { return base_u32 + s * L::kStageBytes; };
+  auto sB = [&](int s) { return base_u32 + s * L::kStageBytes + L::kABytes; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(accum_bar, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    *accum_seen = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(empty_bar(s), ph ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
+        mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
+        tma_load_2d(sA(s), &map_a, full_bar(s), kb * kBK, m0);
+        tma_load_2d(sB(s), &map_b, full_bar(s), kb * kBK, n0);
+        *issued = kb + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, false, false);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(full_bar(s), ph, abort_flag, err, kDevTimeoutMma)) break;
+        *consumed = kb + 1;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const uint64_t ad = sdesc_sw128(sA(s) + k * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(sB(s) + k * 32, 16, 1024);
+          umma_ss(tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        tc_commit(empty_bar(s));
+      }
+      tc_commit(accum_bar);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    bool ok = mbar_wait(accum_bar, 0, abort_flag, err, kDevTimeoutConsumer);
+    ok = __all_sync(0xffffffffu, ok);  // reconverge: tcgen05.ld is warp-collective
+    if (ok) {
+      if (lane == 0) *accum_seen = 1;
+      tc_fence_after();
+      epi.template run<BN>(tmem + (static_cast<uint32_t>(quad * 32) << 16), m0 + row,
+                           (m0 + row) < M, n0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // Drain TMA copies that were issued but never consumed, then the UMMAs.
+    for (int kb = *consumed; kb < *issued; ++kb) drain_wait(full_bar(kb % STAGES), (kb / STAGES) & 1);
+    if (!*accum_seen) drain_wait(accum_bar, 0);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+template <int BN, int STAGES, class Epi>
+cudaError_t launch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K,
+                        const Epi& epi, int* err, cudaStream_t st) {
+  if (M <= 0 || N % BN != 0 || K % kBK != 0) return cudaErrorInvalidValue;
+  CUtensorMap map_a, map_b;
+  if (!encode_tma_2d_bf16(&map_a, a, K, M, kBK, kBM)) return cudaErrorInvalidValue;
+  if (!encode_tma_2d_bf16(&map_b, b, K, N, kBK, BN)) return cudaErrorInvalidValue;
+  using L = GemmSmem<BN, STAGES>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       L::kLaunchBytes);
+  if (e != cudaSuccess) return e;
+  dim3 grid(N / BN, (M + kBM - 1) / kBM);
+  kern<<<grid, kGemmThreads, L::kLaunchBytes, st>>>(map_a, map_b, M, K, epi, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t, int rows,
+                            int embed, const QkvEpilogueArgs& epi, int* err, cudaStream_t st) {
+  if (embed % 256 != 0) return cudaErrorInvalidValue;
+  QkvEpilogue e{epi};
+  return launch_gemm<256, 4>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
+}
+
+cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
+                             const ProjEpilogueArgs& epi, int* err, cudaStream_t st) {
+  if (n % 128 != 0 || epi.embed != n) return cudaErrorInvalidValue;
+  ProjEpilogue e{epi};
+  return launch_gemm<128, 4>(a, w_t, m, n, k, e, err, st);
+}
+
+}  // namespace va

@@ -1,0 +1,90 @@
+// Internal launcher interface between the C-ABI layer (va_api.cu) and the
+// kernels (va_gemm.cu, va_flash.cu, va_layout.cu).  Plain pointers and sizes;
+// no torch types anywhere in the library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace va {
+
+// ---- QKV projection (K1): X[rows,E] bf16 x Wqkv^T -> Q,K,V token-major bf16 ----
+struct QkvEpilogueArgs {
+  const float* bias;                  // [3E]
+  const float* q_g; const float* q_b;  // [64] QK-norm (nullptr: no QK-norm)
+  const float* k_g; const float* k_b;
+  float qk_eps;
+  const int2* pos;                     // [rows] (y, x) integer positions (nullptr: no RoPE)
+  const float2* rope_cs;               // [n_pos][16] (cos, sin) of pos * base^(-2i/32)
+  int rope_pairing;                    // 0 rotate-half, 1 interleaved
+  __nv_bfloat16* q_out;                // [rows][E], head h at columns [64h, 64h+64)
+  __nv_bfloat16* k_out;                // [rows][E] (may be a rank's slice of a gathered buffer)
+  __nv_bfloat16* v_out;
+  int rows;
+  int embed;
+};
+
+// ---- output projection (K3): O[rows,E] bf16 x Wp^T + b (* ls1) (+ residual) -> F32 ----
+struct ProjEpilogueArgs {
+  const float* bias;      // [E]
+  const float* ls1;       // [E] or nullptr
+  const float* residual;  // [rows,E] F32 or nullptr (may alias out)
+  float* out;             // [rows,E] F32
+  int rows;
+  int embed;
+};
+
+// ---- fused flash attention (K2) ----
+// Q is [q_count][E] token-major (this rank's queries, the first of which is row
+// q_offset of the key window); K and V are [kv_rows][E] token-major.
+// seg_len == 0: global attention, every query sees all kv_rows keys.
+// seg_len  > 0: local attention over independent segments of seg_len tokens;
+//               q_offset and q_count are then multiples of seg_len.
+struct FlashArgs {
+  int q_count;
+  int q_offset;
+  int kv_rows;
+  int seg_len;
+  int heads;
+  float scale_log2;       // (1/sqrt(64)) * log2(e)
+  int out_mode;           // 0: token-major bf16 [q_count][E]; 1: head-major F32 [H][q_count][64]
+  __nv_bfloat16* o_tok;
+  float* o_hnd;
+  int embed;
+};
+
+// Tensor-map encoding through the driver entry point (no -lcuda needed).
+bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                        uint32_t box_inner, uint32_t box_outer);
+bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                        uint32_t b0, uint32_t b1, uint32_t b2);
+
+// Launchers return cudaSuccess or the launch error; kernels report device-side
+// failures through *err (see DevError in va_ptx.cuh).
+cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t, int rows,
+                            int embed, const QkvEpilogueArgs& epi, int* err, cudaStream_t st);
+// General form: out[m, n] from a[m, k] and w_t[n, k]; epi.embed is the output width n.
+cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
+                             const ProjEpilogueArgs& epi, int* err, cudaStream_t st);
+cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                         const FlashArgs& fa, int* err, cudaStream_t st);
+
+// LN1 (optional) + F32 -> bf16 cast of token rows: x[rows,E] -> y[rows,E].
+cudaError_t launch_ln_cast(const float* x, const float* g, const float* b, float eps, int rows,
+                           int embed, __nv_bfloat16* y, cudaStream_t st);
+// Op::Attention operand preparation: [H,n,64] F32 -> optional LN -> optional RoPE ->
+// token-major bf16 [n][H*64].
+cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, const float* b,
+                              float eps, const int2* pos, const float2* rope_cs, int rope_pairing,
+                              __nv_bfloat16* y, cudaStream_t st);
+// Camera-token slots (backbone.rs:746-768): token 0 of view 0 <- cam[0:E],
+// token 0 of every later view <- cam[E:2E].
+cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
+                                 int embed, cudaStream_t st);
+// View permutation: dst view i <- src view order[i] (order on the device).
+cudaError_t launch_permute_views(const float* src, float* dst, const int* order, int views,
+                                 int64_t view_elems, cudaStream_t st);
+
+}  // namespace va

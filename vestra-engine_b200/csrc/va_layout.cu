@@ -1,0 +1,241 @@
+// Bandwidth-bound layout kernels of the attention path, plus TMA map encoding.
+//
+//   ln_cast      LN1 (vit_block.rs:696-714, optional) fused with the F32 -> bf16 cast
+//                of the token rows that feed the QKV UMMA.  One warp per token row,
+//                float4 loads, warp-shuffle mean/variance, 8-byte bf16 stores.
+//   prep_heads   Op::Attention operand preparation (cpu_backend.rs:251-296): per
+//                (head, token) LayerNorm over head_dim at qk_norm_eps, then 2D RoPE,
+//                then bf16 token-major; one warp per row, two channels per lane.
+//   camera_inject  camera-token slots before block alt_start (backbone.rs:746-768).
+//   permute_views  view-order permutation (engine.rs:198-205 restore, backbone.rs:218-224).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "va_internal.h"
+#include "va_ptx.cuh"
+
+namespace va {
+
+// ---------------------------------------------------------------------------
+// TMA tensor maps
+// ---------------------------------------------------------------------------
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+}  // namespace
+
+bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                        uint32_t box_inner, uint32_t box_outer) {
+  if (!get_encode()) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (inner * 2) % 16 != 0) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                        uint32_t b0, uint32_t b1, uint32_t b2) {
+  if (!get_encode()) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (d0 * 2) % 16 != 0) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// LN1 + cast
+// ---------------------------------------------------------------------------
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// E % 128 == 0; each lane owns E/128 float4 groups of the row.
+template <int kGroups>
+__global__ void __launch_bounds__(256) ln_cast_kernel(const float* __restrict__ x,
+                                                      const float* __restrict__ g,
+                                                      const float* __restrict__ b, float eps,
+                                                      int rows, int embed,
+                                                      __nv_bfloat16* __restrict__ y) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * embed);
+  float4 v[kGroups];
+#pragma unroll
+  for (int i = 0; i < kGroups; ++i) v[i] = __ldg(xr + i * 32 + lane);
+  if (g != nullptr) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) s += v[i].x + v[i].y + v[i].z + v[i].w;
+    const float mean = warp_sum(s) / embed;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const float a = v[i].x - mean, bb = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += a * a + bb * bb + c * c + d * d;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) / embed + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+    for (int i = 0; i < kGroups; ++i) {
+      const float4 gg = __ldg(g4 + i * 32 + lane), bb = __ldg(b4 + i * 32 + lane);
+      v[i].x = (v[i].x - mean) * inv * gg.x + bb.x;
+      v[i].y = (v[i].y - mean) * inv * gg.y + bb.y;
+      v[i].z = (v[i].z - mean) * inv * gg.z + bb.z;
+      v[i].w = (v[i].w - mean) * inv * gg.w + bb.w;
+    }
+  }
+  uint2* yr = reinterpret_cast<uint2*>(y + static_cast<size_t>(row) * embed);
+#pragma unroll
+  for (int i = 0; i < kGroups; ++i)
+    yr[i * 32 + lane] = make_uint2(pack_bf16x2(v[i].x, v[i].y), pack_bf16x2(v[i].z, v[i].w));
+}
+
+// One warp per (head, token) row of 64 channels; lane owns channels 2*lane, 2*lane+1.
+__global__ void __launch_bounds__(256) prep_heads_kernel(
+    const float* __restrict__ x, int rows_total, const float* __restrict__ g,
+    const float* __restrict__ b, float eps, const int2* __restrict__ pos, int n,
+    const float2* __restrict__ cs, int pairing, __nv_bfloat16* __restrict__ y) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows_total) return;
+  const float2 v = __ldg(reinterpret_cast<const float2*>(x + static_cast<size_t>(row) * 64) + lane);
+  float a0 = v.x, a1 = v.y;
+  if (g != nullptr) {
+    const float mean = warp_sum(a0 + a1) * (1.0f / 64.0f);
+    const float d0 = a0 - mean, d1 = a1 - mean;
+    const float inv = 1.0f / sqrtf(warp_sum(d0 * d0 + d1 * d1) * (1.0f / 64.0f) + eps);
+    a0 = d0 * inv * __ldg(g + 2 * lane) + __ldg(b + 2 * lane);
+    a1 = d1 * inv * __ldg(g + 2 * lane + 1) + __ldg(b + 2 * lane + 1);
+  }
+  if (pos != nullptr) {
+    const int t = row % n;
+    const int2 p = pos[t];
+    // channel c = 2*lane + e lives in half c/32 (0 = y, 1 = x), index c%32 in it.
+    // Rotate-half partners (i, i+16) are channel c^16 = component e of lane^8.
+    const float sw0 = __shfl_xor_sync(0xffffffffu, a0, 8);
+    const float sw1 = __shfl_xor_sync(0xffffffffu, a1, 8);
+    float out[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = 2 * lane + e;
+      const int half = c >> 5;
+      const int i = c & 31;
+      const int pp = half == 0 ? p.x : p.y;
+      const float me = e == 0 ? a0 : a1;
+      float partner, sgn;
+      int f;
+      if (pairing == 0) {
+        partner = e == 0 ? sw0 : sw1;
+        f = i & 15;
+        sgn = (i < 16) ? -1.f : 1.f;
+      } else {
+        // pairs (2k, 2k+1): the partner is the other channel of this lane
+        partner = e == 0 ? a1 : a0;
+        f = i >> 1;
+        sgn = (e == 0) ? -1.f : 1.f;
+      }
+      const float2 cc = __ldg(cs + pp * 16 + f);
+      out[e] = me * cc.x + sgn * partner * cc.y;
+    }
+    a0 = out[0];
+    a1 = out[1];
+  }
+  // [H][n][64] -> token-major [n][H*64]
+  const int heads = rows_total / n;
+  const int h = row / n, t = row - h * n;
+  reinterpret_cast<uint32_t*>(y + (static_cast<size_t>(t) * heads + h) * 64)[lane] =
+      pack_bf16x2(a0, a1);
+}
+
+__global__ void camera_inject_kernel(float* tokens, const float* cam, int views,
+                                     int tokens_per_view, int embed) {
+  const int view = blockIdx.x;
+  const float* src = cam + (view > 0 ? embed : 0);
+  float* dst = tokens + static_cast<size_t>(view) * tokens_per_view * embed;
+  for (int c = threadIdx.x; c < embed; c += blockDim.x) dst[c] = src[c];
+}
+
+__global__ void permute_views_kernel(const float4* src, float4* dst, const int* order,
+                                     int64_t view_vec4) {
+  const int view = blockIdx.y;
+  const float4* s = src + static_cast<int64_t>(order[view]) * view_vec4;
+  float4* d = dst + static_cast<int64_t>(view) * view_vec4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < view_vec4;
+       i += (int64_t)gridDim.x * blockDim.x)
+    d[i] = s[i];
+}
+
+}  // namespace
+
+cudaError_t launch_ln_cast(const float* x, const float* g, const float* b, float eps, int rows,
+                           int embed, __nv_bfloat16* y, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid((rows + 7) / 8);
+  switch (embed) {
+    case 256: ln_cast_kernel<2><<<grid, 256, 0, st>>>(x, g, b, eps, rows, embed, y); break;
+    case 512: ln_cast_kernel<4><<<grid, 256, 0, st>>>(x, g, b, eps, rows, embed, y); break;
+    case 768: ln_cast_kernel<6><<<grid, 256, 0, st>>>(x, g, b, eps, rows, embed, y); break;
+    case 1024: ln_cast_kernel<8><<<grid, 256, 0, st>>>(x, g, b, eps, rows, embed, y); break;
+    case 1536: ln_cast_kernel<12><<<grid, 256, 0, st>>>(x, g, b, eps, rows, embed, y); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, const float* b,
+                              float eps, const int2* pos, const float2* rope_cs, int rope_pairing,
+                              __nv_bfloat16* y, cudaStream_t st) {
+  const int total = heads * n;
+  if (total <= 0) return cudaSuccess;
+  prep_heads_kernel<<<(total + 7) / 8, 256, 0, st>>>(x, total, g, b, eps, pos, n, rope_cs,
+                                                     rope_pairing, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
+                                 int embed, cudaStream_t st) {
+  if (views <= 0) return cudaSuccess;
+  camera_inject_kernel<<<views, 256, 0, st>>>(tokens, cam, views, tokens_per_view, embed);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute_views(const float* src, float* dst, const int* order, int views,
+                                 int64_t view_elems, cudaStream_t st) {
+  if (views <= 0 || view_elems % 4 != 0) return cudaErrorInvalidValue;
+  const int64_t v4 = view_elems / 4;
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>((v4 + 255) / 256, 1024)), views);
+  permute_views_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                             reinterpret_cast<float4*>(dst), order, v4);
+  return cudaGetLastError();
+}
+
+}  // namespace va

@@ -1,0 +1,366 @@
+"""Host-side mirror of the reference's attention executor seams over libvestra_attn.so.
+
+The reference (Rust) plugs device attention into its block loop through traits in
+crates/da-engine/src/vit_block.rs; this module offers the same shapes of calls to
+Python callers (tests, bench, smoke) through the C ABI in include/vestra_attn.h:
+
+  CudaAttentionExecutor.run_attention   AttentionExecutor::run_attention (vit_block.rs:95-105)
+  CudaAttentionExecutor.run_attention_views  run_attention with closed-form positions
+                                        (vit_block.rs:841-881) for local/global blocks
+  op_attention                          Op::Attention / GraphBuilder::attention_full
+                                        (graph.rs:67-105, 394-422)
+  select_reference_view_saddle, reference_first_order, restore_original_view_order
+                                        backbone.rs:133-224, engine.rs:198-205
+
+There is no CPU fallback: a missing library or a failing call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_build", "libvestra_attn.so")
+
+VA_OK, VA_ERR_INVALID, VA_ERR_CUDA, VA_ERR_DEVICE, VA_ERR_STATE, VA_ERR_NCCL = range(6)
+
+# Every symbol include/vestra_attn.h declares (checked by tests/test_abi.py).
+EXPORTED = [
+    "va_version", "va_default_config", "va_create", "va_destroy", "va_last_error", "va_load_layer",
+    "va_layer_flags", "va_run_attention", "va_attention_host", "va_attention_device",
+    "va_block_attention_device", "va_op_attention_device", "va_flash_attention_bf16",
+    "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
+    "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
+    "va_comm_unique_id", "va_comm_init", "va_attention_device_sharded",
+]
+
+
+class VestraError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"vestra_attn error {code}: {msg}")
+        self.code = code
+
+
+class VaConfig(ctypes.Structure):
+    """va_config: the ModelConfig fields the attention path reads (config.rs:146)."""
+
+    _fields_ = [
+        ("embed_dim", ctypes.c_int32), ("num_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("depth", ctypes.c_int32), ("num_register", ctypes.c_int32), ("rope_start", ctypes.c_int32),
+        ("qknorm_start", ctypes.c_int32), ("rope_freq", ctypes.c_float), ("ln_eps", ctypes.c_float),
+        ("qk_norm_eps", ctypes.c_float), ("rope_pairing", ctypes.c_int32), ("max_rows", ctypes.c_int32),
+    ]
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int)
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads libvestra_attn.so.  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with vestra-engine_b200/build.py")
+    lib = ctypes.CDLL(path)
+    i64, c_int, c_float = ctypes.c_int64, ctypes.c_int, ctypes.c_float
+    sig = {
+        "va_version": ([], ctypes.c_char_p),
+        "va_default_config": ([ctypes.POINTER(VaConfig)], None),
+        "va_create": ([ctypes.POINTER(VaConfig), c_int, ctypes.POINTER(_vp)], c_int),
+        "va_destroy": ([_vp], None),
+        "va_last_error": ([_vp], ctypes.c_char_p),
+        "va_load_layer": ([_vp, c_int] + [_vp] * 11, c_int),
+        "va_layer_flags": ([_vp, c_int, _i32p, _i32p], c_int),
+        "va_run_attention": ([_vp, c_int, _vp, i64, c_int, c_int, _vp, _vp], c_int),
+        "va_attention_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_attention_device": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_block_attention_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_op_attention_device": ([_vp, _vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float,
+                                    _vp, c_float, _vp, _vp], c_int),
+        "va_flash_attention_bf16": ([_vp, _vp, _vp, _vp, i64, i64, i64, c_int, i64, _vp, _vp], c_int),
+        "va_comm_unique_id": ([_vp], c_int),
+        "va_comm_init": ([_vp, _vp, c_int, c_int], c_int),
+        "va_attention_device_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_linear_bf16": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, i64, c_int, c_int, _vp], c_int),
+        "va_select_reference_view_saddle": ([_vp, c_int, c_int, _i32p], c_int),
+        "va_reference_first_order": ([c_int, c_int, _i32p], c_int),
+        "va_restore_order": ([c_int, c_int, _i32p], c_int),
+        "va_camera_inject_device": ([_vp, _vp, c_int, i64, c_int, _vp], c_int),
+        "va_permute_views_device": ([_vp, _vp, _i32p, c_int, i64, _vp], c_int),
+        "va_check_device": ([_vp], c_int),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def _ptr(x):
+    """Device/host address of a torch tensor, numpy array, int or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if isinstance(x, np.ndarray):
+        assert x.flags.c_contiguous
+        return x.ctypes.data
+    if hasattr(x, "data_ptr"):
+        assert x.is_contiguous()
+        return x.data_ptr()
+    raise TypeError(type(x))
+
+
+def _f32(a):
+    return None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+
+
+def default_config(**overrides) -> VaConfig:
+    cfg = VaConfig()
+    load_library().va_default_config(ctypes.byref(cfg))
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg
+
+
+def wname(layer_idx: int, suffix: str) -> str:
+    """Weight tensor names, vit_block.rs:30-53 / :688-690."""
+    return f"vit.blk.{layer_idx}.{suffix}"
+
+
+@dataclass
+class ModelConfig:
+    """The ModelConfig fields of the attention path (config.rs:146-...)."""
+
+    embed_dim: int = 768
+    num_heads: int = 12
+    head_dim: int = 64
+    depth: int = 12
+    num_register: int = 0
+    rope_start: int = 4
+    qknorm_start: int = 4
+    rope_freq: float = 100.0
+    ln_eps: float = 1e-6
+    alt_start: int = 4
+
+    def to_va(self, max_rows: int, qk_norm_eps: float = 1e-5, rope_pairing: int = 0) -> VaConfig:
+        return default_config(embed_dim=self.embed_dim, num_heads=self.num_heads, head_dim=self.head_dim,
+                              depth=self.depth, num_register=self.num_register, rope_start=self.rope_start,
+                              qknorm_start=self.qknorm_start, rope_freq=self.rope_freq, ln_eps=self.ln_eps,
+                              qk_norm_eps=qk_norm_eps, rope_pairing=rope_pairing, max_rows=max_rows)
+
+    def is_global(self, layer_idx: int) -> bool:
+        """backbone.rs:459-460 / :770-771."""
+        return self.alt_start >= 0 and layer_idx >= self.alt_start and layer_idx % 2 == 1
+
+
+class Context:
+    """Owns one va_ctx (one device, serial calls)."""
+
+    def __init__(self, cfg: VaConfig, device: int = 0):
+        self.lib = load_library()
+        self.cfg = cfg
+        h = _vp()
+        rc = self.lib.va_create(ctypes.byref(cfg), device, ctypes.byref(h))
+        if rc != VA_OK:
+            raise VestraError(rc, "va_create failed")
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.va_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, rc: int):
+        if rc != VA_OK:
+            raise VestraError(rc, self.lib.va_last_error(self.h).decode())
+
+    def load_layer(self, layer: int, p: dict):
+        """p: qkv_w [E,3E], qkv_b, proj_w [E,E], proj_b, optional norm1_w/b, q_g/q_b/k_g/k_b, ls1."""
+        keep = {k: _f32(v) for k, v in p.items() if v is not None}
+        g = lambda k: _ptr(keep.get(k))  # noqa: E731
+        self.check(self.lib.va_load_layer(self.h, layer, g("norm1_w"), g("norm1_b"), g("qkv_w"), g("qkv_b"),
+                                          g("q_g"), g("q_b"), g("k_g"), g("k_b"), g("proj_w"), g("proj_b"),
+                                          g("ls1")))
+
+    def layer_flags(self, layer: int):
+        a, b = ctypes.c_int(), ctypes.c_int()
+        self.check(self.lib.va_layer_flags(self.h, layer, ctypes.byref(a), ctypes.byref(b)))
+        return bool(a.value), bool(b.value)
+
+    def attention_host(self, layer, ln1, gh, gw, view_count, global_, out=None):
+        ln1 = ln1 if hasattr(ln1, "data_ptr") else _f32(ln1)
+        rows = ln1.shape[0]
+        if out is None:
+            out = np.empty_like(ln1) if isinstance(ln1, np.ndarray) else ln1.new_empty(ln1.shape)
+        self.check(self.lib.va_attention_host(self.h, layer, _ptr(ln1), rows, gh, gw, view_count,
+                                              int(bool(global_)), _ptr(out)))
+        return out
+
+    def attention_device(self, layer, ln1_dev, out_dev, gh, gw, view_count, global_, stream=0):
+        self.check(self.lib.va_attention_device(self.h, layer, _ptr(ln1_dev), _ptr(out_dev), ln1_dev.shape[0],
+                                                gh, gw, view_count, int(bool(global_)), stream))
+
+    def block_attention_device(self, layer, tokens_dev, gh, gw, view_count, global_, stream=0):
+        self.check(self.lib.va_block_attention_device(self.h, layer, _ptr(tokens_dev), tokens_dev.shape[0],
+                                                      gh, gw, view_count, int(bool(global_)), stream))
+
+    def run_attention(self, layer, inp, rows, heads, head_dim, positions_yx):
+        inp = _f32(inp)
+        out = np.empty_like(inp)
+        pos = _f32(positions_yx)
+        self.check(self.lib.va_run_attention(self.h, layer, _ptr(inp), rows, heads, head_dim, _ptr(pos),
+                                             _ptr(out)))
+        return out
+
+    def flash_bf16(self, q, k, v, heads, out, seg_len=0, q_offset=0, stream=0):
+        """q [q_count, heads*64], k/v [kv_rows, heads*64] bf16 token-major; seg_len 0 = global."""
+        self.check(self.lib.va_flash_attention_bf16(self.h, _ptr(q), _ptr(k), _ptr(v), q.shape[0], q_offset,
+                                                    k.shape[0], heads, seg_len, _ptr(out), stream))
+
+    def comm_init(self, comm_id: bytes, nranks: int, rank: int):
+        buf = ctypes.create_string_buffer(bytes(comm_id), 128)
+        self.check(self.lib.va_comm_init(self.h, buf, nranks, rank))
+
+    def attention_device_sharded(self, layer, ln1_local, out_local, gh, gw, view_count, global_, stream=0):
+        self.check(self.lib.va_attention_device_sharded(self.h, layer, _ptr(ln1_local), _ptr(out_local),
+                                                        ln1_local.shape[0], gh, gw, view_count,
+                                                        int(bool(global_)), stream))
+
+    def linear_bf16(self, a, w_t, out, bias=None, scale=None, residual=None, stream=0):
+        m, k = a.shape
+        n = w_t.shape[0]
+        self.check(self.lib.va_linear_bf16(self.h, _ptr(a), _ptr(w_t), _ptr(bias), _ptr(scale), _ptr(residual),
+                                           _ptr(out), m, n, k, stream))
+
+    def op_attention(self, q, k, v, out, qnorm=None, knorm=None, qk_norm_eps=1e-5, rope=None, stream=0):
+        heads, n, d = q.shape
+        pos = None if rope is None else _f32(rope[0])
+        freq = 100.0 if rope is None else float(rope[1])
+        qg, qb = (None, None) if qnorm is None else qnorm
+        kg, kb = (None, None) if knorm is None else knorm
+        self.check(self.lib.va_op_attention_device(self.h, _ptr(q), _ptr(k), _ptr(v), heads, n, d, _ptr(qg),
+                                                   _ptr(qb), _ptr(kg), _ptr(kb), qk_norm_eps, _ptr(pos), freq,
+                                                   _ptr(out), stream))
+
+    def check_device(self):
+        self.check(self.lib.va_check_device(self.h))
+
+
+class CudaAttentionExecutor:
+    """AttentionExecutor (vit_block.rs:95-105) backed by the sm_100a path.
+
+    Built from the reference's `Weights` naming (dict name -> F32 array, linear
+    weights [in, out]); uploads every layer once, like CudaAttentionExecutor::new
+    (vit_block.rs:239-318).  run_attention raises instead of returning None: the
+    reference's silent CPU fallback does not exist here.
+    """
+
+    def __init__(self, cfg: ModelConfig, weights: dict, device: int = 0, max_rows: int = 12 * 866):
+        self.cfg = cfg
+        self.ctx = Context(cfg.to_va(max_rows), device)
+        for i in range(cfg.depth):
+            if weights.get(wname(i, "attn_qkv.weight")) is None:
+                continue
+            self.ctx.load_layer(i, layer_params_from_weights(weights, i))
+
+    def run_attention(self, layer_idx, input, rows, heads, head_dim, positions_yx):
+        return self.ctx.run_attention(layer_idx, input, rows, heads, head_dim, positions_yx)
+
+    def run_attention_views(self, layer_idx, ln1, gh, gw, view_count, global_):
+        return self.ctx.attention_host(layer_idx, ln1, gh, gw, view_count, global_)
+
+
+def layer_params_from_weights(weights: dict, i: int) -> dict:
+    g = lambda s: weights.get(wname(i, s))  # noqa: E731
+    return {"norm1_w": g("norm1.weight"), "norm1_b": g("norm1.bias"), "qkv_w": g("attn_qkv.weight"),
+            "qkv_b": g("attn_qkv.bias"), "q_g": g("attn_qnorm.weight"), "q_b": g("attn_qnorm.bias"),
+            "k_g": g("attn_knorm.weight"), "k_b": g("attn_knorm.bias"), "proj_w": g("attn_proj.weight"),
+            "proj_b": g("attn_proj.bias"), "ls1": g("ls1")}
+
+
+def positions_yx(rows: int, view_count: int, n_special: int, gh: int, gw: int, global_: bool) -> np.ndarray:
+    """RoPE position table of run_attention (vit_block.rs:841-881), [rows, 2] F32."""
+    per_view = n_special + gh * gw
+    if view_count <= 0 or per_view * view_count != rows:
+        raise ValueError("token count must equal tokens_per_view * view_count")
+    p = np.zeros((view_count, per_view, 2), np.float32)
+    if global_:
+        p[:, n_special:, :] = 1.0
+    else:
+        idx = np.arange(gh * gw)
+        p[:, n_special:, 0] = idx // gw + 1
+        p[:, n_special:, 1] = idx % gw + 1
+    return p.reshape(rows, 2)
+
+
+def comm_unique_id() -> bytes:
+    """128-byte communicator id, made on rank 0 and shared with the other ranks."""
+    buf = ctypes.create_string_buffer(128)
+    rc = load_library().va_comm_unique_id(buf)
+    if rc != VA_OK:
+        raise VestraError(rc, "va_comm_unique_id failed (NCCL unavailable?)")
+    return buf.raw
+
+
+def shard_rows(window_rows: int, nranks: int, rank: int) -> tuple[int, int]:
+    """(row_offset, local_rows) of a rank's equal contiguous slice of the window."""
+    if window_rows % nranks:
+        raise ValueError(f"window of {window_rows} tokens does not split into {nranks} equal slices")
+    local = window_rows // nranks
+    return rank * local, local
+
+
+def select_reference_view_saddle(cls) -> int:
+    cls = _f32(cls)
+    out = ctypes.c_int()
+    rc = load_library().va_select_reference_view_saddle(_ptr(cls), cls.shape[0], cls.shape[1], ctypes.byref(out))
+    if rc != VA_OK:
+        raise VestraError(rc, "select_reference_view_saddle")
+    return out.value
+
+
+def reference_first_order(view_count: int, reference: int) -> list[int]:
+    buf = (ctypes.c_int * view_count)()
+    rc = load_library().va_reference_first_order(view_count, reference, buf)
+    if rc != VA_OK:
+        raise VestraError(rc, "reference_first_order")
+    return list(buf)
+
+
+def restore_original_view_order(ordered: list, reference_view_index: int) -> list:
+    """engine.rs:198-205: caller order from reference-first order."""
+    n = len(ordered)
+    buf = (ctypes.c_int * n)()
+    rc = load_library().va_restore_order(n, reference_view_index, buf)
+    if rc != VA_OK:
+        raise VestraError(rc, "restore_order")
+    return [ordered[i] for i in buf]
+
+
+def camera_inject_device(tokens_dev, camera_dev, views, tokens_per_view, embed, stream=0):
+    rc = load_library().va_camera_inject_device(_ptr(tokens_dev), _ptr(camera_dev), views, tokens_per_view,
+                                                embed, stream)
+    if rc != VA_OK:
+        raise VestraError(rc, "camera_inject_device")
+
+
+def permute_views_device(src_dev, dst_dev, order, views, view_elems, stream=0):
+    buf = (ctypes.c_int * views)(*order)
+    rc = load_library().va_permute_views_device(_ptr(src_dev), _ptr(dst_dev), buf, views, view_elems, stream)
+    if rc != VA_OK:
+        raise VestraError(rc, "permute_views_device")
