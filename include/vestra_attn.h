@@ -38,6 +38,7 @@ extern "C" {
 #define VA_ERR_DEVICE 3  /* a kernel gave up on a bounded wait and set the error word */
 #define VA_ERR_STATE 4   /* e.g. layer weights not loaded */
 #define VA_ERR_NCCL 5    /* communicator failure */
+#define VA_ERR_CAPACITY 6 /* request larger than a fixed-size buffer (va_op_attention_noalloc) */
 
 typedef struct va_ctx va_ctx;
 
@@ -122,6 +123,23 @@ int va_op_attention_device(va_ctx* ctx, const float* q, const float* k, const fl
                            const float* qn_b, const float* kn_g, const float* kn_b,
                            float qk_norm_eps, const float* pos_yx_host, float freq, float* out,
                            void* stream);
+
+/* No counterpart in the reference: Op::Attention for callers that cannot allocate
+ * device memory (a process whose allocator owns the whole GPU, or a block loop that
+ * must not stall on cudaMalloc/cudaFree or fail on one).  Needs no context and
+ * allocates nothing; its bf16 operand scratch is a fixed array of 12 MiB inside the
+ * library, held on every GPU that loads it until exit.  All pointers are device
+ * pointers: q, k, v, out [heads, n, 64] F32; norm vectors [64] or NULL; pos_yx_dev
+ * [n, 2] F32 (rounded) or NULL; rope_pairing as in va_config.  Limit: heads * n * 64
+ * <= 2,097,152, else VA_ERR_CAPACITY.  The first call on a device looks up the
+ * scratch address with that device current and should come before any stream
+ * capture.  Calls share the scratch: calls that overlap on the GPU race.  The call
+ * waits for `stream` and returns VA_ERR_DEVICE if a kernel gave up on a bounded wait. */
+int va_op_attention_noalloc(const float* q, const float* k, const float* v, int heads,
+                            int64_t n, int head_dim, const float* qn_g, const float* qn_b,
+                            const float* kn_g, const float* kn_b, float qk_norm_eps,
+                            const float* pos_yx_dev, float freq, int rope_pairing, float* out,
+                            void* stream);
 
 /* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
  * add the query-sharded global block: each rank owns an equal contiguous slice of

@@ -25,7 +25,8 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_build", "libvestra_attn.so")
 
-VA_OK, VA_ERR_INVALID, VA_ERR_CUDA, VA_ERR_DEVICE, VA_ERR_STATE, VA_ERR_NCCL = range(6)
+VA_OK, VA_ERR_INVALID, VA_ERR_CUDA, VA_ERR_DEVICE, VA_ERR_STATE, VA_ERR_NCCL, VA_ERR_CAPACITY = range(7)
+NOALLOC_MAX_ELEMS = 1 << 21  # heads * n * 64 limit of va_op_attention_noalloc
 
 # Every symbol include/vestra_attn.h declares (checked by tests/test_abi.py).
 EXPORTED = [
@@ -34,7 +35,7 @@ EXPORTED = [
     "va_block_attention_device", "va_op_attention_device", "va_flash_attention_bf16",
     "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
-    "va_comm_unique_id", "va_comm_init", "va_attention_device_sharded",
+    "va_comm_unique_id", "va_comm_init", "va_attention_device_sharded", "va_op_attention_noalloc",
 ]
 
 
@@ -88,6 +89,8 @@ def load_library(path: str = LIB_PATH):
         "va_comm_unique_id": ([_vp], c_int),
         "va_comm_init": ([_vp, _vp, c_int, c_int], c_int),
         "va_attention_device_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_op_attention_noalloc": ([_vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float, _vp, c_float,
+                                     c_int, _vp, _vp], c_int),
         "va_linear_bf16": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, i64, c_int, c_int, _vp], c_int),
         "va_select_reference_view_saddle": ([_vp, c_int, c_int, _i32p], c_int),
         "va_reference_first_order": ([c_int, c_int, _i32p], c_int),
@@ -306,6 +309,18 @@ def positions_yx(rows: int, view_count: int, n_special: int, gh: int, gw: int, g
         p[:, n_special:, 0] = idx // gw + 1
         p[:, n_special:, 1] = idx % gw + 1
     return p.reshape(rows, 2)
+
+
+def op_attention_noalloc(q, k, v, out, qnorm=None, knorm=None, qk_norm_eps=1e-5, pos_yx_dev=None,
+                         freq=100.0, rope_pairing=0, stream=0) -> int:
+    """Op::Attention without any device allocation (for callers that cannot call
+    cudaMalloc); all arguments are device tensors.  Returns the raw status code."""
+    heads, n, d = q.shape
+    qg, qb = (None, None) if qnorm is None else qnorm
+    kg, kb = (None, None) if knorm is None else knorm
+    return load_library().va_op_attention_noalloc(_ptr(q), _ptr(k), _ptr(v), heads, n, d, _ptr(qg), _ptr(qb),
+                                                  _ptr(kg), _ptr(kb), qk_norm_eps, _ptr(pos_yx_dev), freq,
+                                                  rope_pairing, _ptr(out), stream)
 
 
 def comm_unique_id() -> bytes:
