@@ -50,6 +50,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the CPU-baseline sample (seconds of CPU work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--variants", action="store_true",
+                    help="also time the attention kernel's exponential-split and f16-P variants")
     return ap.parse_args()
 
 
@@ -323,27 +325,39 @@ def run_ours(args):
     value = flops / (ms_per_step * 1e-3) / 1e12
 
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
+    # Q/K ~ N(0,1) per channel like QK-normalised rows; V bf16 (production path).
     g = torch.Generator(device="cuda").manual_seed(rank)
-    qk_scale = 1.0
-    q = (qk_scale * torch.randn(local, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
+    q = torch.randn(local, wl.embed, device="cuda", generator=g).to(torch.bfloat16)
     kw = torch.randn(wl.rows, wl.embed, device="cuda", generator=g).to(torch.bfloat16)
-    vw = torch.randn(wl.rows, wl.embed, device="cuda", generator=g).to(torch.bfloat16)
+    vw = (0.5 * torch.randn(wl.rows, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
     o = torch.empty(local, wl.embed, device="cuda", dtype=torch.bfloat16)
-    for _ in range(3):
-        ctx.flash_bf16(q, kw, vw, wl.heads, o, q_offset=row0, stream=sp)
-    k_ms = []
-    barrier()
-    for _ in range(args.steps):
-        flush_buf.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        ctx.flash_bf16(q, kw, vw, wl.heads, o, q_offset=row0, stream=sp)
-        b.record(stream)
-        k_ms.append((a, b))
-    barrier()
-    ctx.check_device()
-    flash_ms = statistics.mean(a.elapsed_time(b) for a, b in k_ms)
+
+    def time_flash(v_tensor, poly=-1):
+        for _ in range(3):
+            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, poly_per8=poly)
+        evs = []
+        barrier()
+        for _ in range(args.steps):
+            flush_buf.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, poly_per8=poly)
+            b.record(stream)
+            evs.append((a, b))
+        barrier()
+        ctx.check_device()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
     flash_flops = 4.0 * local * wl.rows * 64 * wl.heads
+    flash_ms = time_flash(vw)
+    variants = {}
+    if args.variants:
+        to_tf = lambda ms: round(flash_flops / (ms * 1e-3) / 1e12, 2)  # noqa: E731
+        for form in (2, 3, 5):
+            for p in range(3):
+                name = {3: f"w20_poly{p}", 5: f"w20ord_poly{p}"}.get(form, f"form{form}_poly{p}")
+                variants[name] = to_tf(time_flash(vw, p + 8 * form))
+        variants["f16_p"] = to_tf(time_flash(vw.to(torch.float16)))
     peak_tflops, _, peak_kind = load_peaks()
     achieved = flash_flops / (flash_ms * 1e-3) / 1e12
 
@@ -400,6 +414,7 @@ def run_ours(args):
                          "peak": peak_tflops, "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
                          "peak_kind": f"bf16 burst ({peak_kind})", "flops_per_launch": flash_flops,
                          "ms_per_launch": round(flash_ms, 4),
+                         **({"variants_tflops": variants} if variants else {}),
                          "traffic": FLASH_DRAM_BYTES_PER_LAUNCH},
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
                     "h2d_bytes_per_step": int(wl.rows * wl.embed * 4), "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),

@@ -65,26 +65,51 @@ def test_linear_bf16_matches_torch(ctx, m, n, k):
 
 
 # ---------------------------------------------------------------- K2 alone
-def _tok(x):
-    """[heads, rows, 64] -> token-major bf16 CUDA [rows, heads*64]."""
+def _tok(x, dtype=None):
+    """[heads, rows, 64] -> token-major CUDA [rows, heads*64] (bf16 unless dtype given)."""
     h, n, d = x.shape
-    return torch.from_numpy(np.ascontiguousarray(x.transpose(1, 0, 2).reshape(n, h * d))).to(torch.bfloat16).cuda()
+    t = torch.from_numpy(np.ascontiguousarray(x.transpose(1, 0, 2).reshape(n, h * d)))
+    return t.to(dtype or torch.bfloat16).cuda()
 
 
+def f16_round(x):
+    return x.astype(np.float16).astype(np.float32)
+
+
+@pytest.mark.parametrize("v_dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 127, 1), (2, 128, 1), (2, 129, 1), (3, 256, 1),
                                             (2, 300, 1), (12, 866, 1), (4, 865, 3), (12, 1732, 1)])
-def test_flash_bf16_matches_oracle_core(ctx, oracle_mod, heads, seg, segs):
+def test_flash_bf16_matches_oracle_core(ctx, oracle_mod, heads, seg, segs, v_dtype):
     rows = seg * segs
     rng = np.random.default_rng(heads * 1000 + seg)
     q, k, v = (rng.standard_normal((heads, rows, 64)).astype(np.float32) for _ in range(3))
-    q, k, v = bf16_round(q), bf16_round(k), bf16_round(v)
+    q, k = bf16_round(q), bf16_round(k)
+    v = f16_round(v) if v_dtype == "f16" else bf16_round(v)
     out = torch.zeros(rows, heads * 64, dtype=torch.bfloat16, device="cuda")
-    ctx.flash_bf16(_tok(q), _tok(k), _tok(v), heads, out, seg_len=seg if segs > 1 else 0)
+    tv = _tok(v, torch.float16 if v_dtype == "f16" else torch.bfloat16)
+    ctx.flash_bf16(_tok(q), _tok(k), tv, heads, out, seg_len=seg if segs > 1 else 0)
     torch.cuda.synchronize()
     ctx.check_device()
     got = out.float().cpu().numpy().reshape(rows, heads, 64).transpose(1, 0, 2)
     ref = oracle_mod.attention_core(q, k, v, seg_len=seg)
     assert_close(got, ref, what=f"flash h{heads} n{seg}x{segs}")
+
+
+@pytest.mark.parametrize("variant", [1, 16, 24, 25, 26, 32, 40, 41])
+@pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 129, 1), (12, 866, 1), (4, 865, 3), (12, 1732, 1)])
+def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, segs, variant):
+    # variant = (pairs of every 8 exponentials on the FMA pipe) + 8 * layout/formulation;
+    # 24..26 are the 20-warp layout with 4 threads per row.
+    rows = seg * segs
+    rng = np.random.default_rng(heads * 7 + seg)
+    q, k, v = (bf16_round(rng.standard_normal((heads, rows, 64)).astype(np.float32)) for _ in range(3))
+    out = torch.zeros(rows, heads * 64, dtype=torch.bfloat16, device="cuda")
+    ctx.flash_bf16(_tok(q), _tok(k), _tok(v), heads, out, seg_len=seg if segs > 1 else 0, poly_per8=variant)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    got = out.float().cpu().numpy().reshape(rows, heads, 64).transpose(1, 0, 2)
+    ref = oracle_mod.attention_core(q, k, v, seg_len=seg)
+    assert_close(got, ref, what=f"flash variant {variant} h{heads} n{seg}x{segs}")
 
 
 @pytest.mark.parametrize("nranks", [2, 8])
@@ -93,9 +118,10 @@ def test_flash_query_slices_of_a_window(ctx, oracle_mod, nranks):
     # whole gathered key window.  The slices together must equal the full attention.
     heads, window = 4, 1736 if nranks == 8 else 1732
     rng = np.random.default_rng(nranks)
-    q, k, v = (bf16_round(rng.standard_normal((heads, window, 64)).astype(np.float32)) for _ in range(3))
+    q, k = (bf16_round(rng.standard_normal((heads, window, 64)).astype(np.float32)) for _ in range(2))
+    v = f16_round(rng.standard_normal((heads, window, 64)).astype(np.float32))
     ref = oracle_mod.attention_core(q, k, v)
-    tq, tk, tv = _tok(q), _tok(k), _tok(v)
+    tq, tk, tv = _tok(q), _tok(k), _tok(v, torch.float16)
     local = window // nranks
     for r in range(nranks):
         out = torch.zeros(local, heads * 64, dtype=torch.bfloat16, device="cuda")

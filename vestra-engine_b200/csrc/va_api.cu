@@ -296,6 +296,9 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
   qa.v_out = v_slice;
   qa.rows = static_cast<int>(rows);
   qa.embed = E;
+  // V (and so P) stay bf16: measured faster on B200 than an f16 P formed with
+  // packed ex2.f16x2 (584 vs 511 TFLOP/s for the S=12 window).
+  qa.v_f16 = 0;
   VA_CUDA(c, va::launch_qkv_gemm(c->x, w.w_qkv_t, static_cast<int>(rows), E, qa, c->err, st));
   va::FlashArgs fa{};
   fa.q_count = static_cast<int>(rows);
@@ -305,6 +308,7 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
   fa.out_mode = 0;
   fa.o_tok = c->o;
   fa.embed = E;
+  fa.v_f16 = 0;
   const __nv_bfloat16* kk = c->k;
   const __nv_bfloat16* vv = c->v;
   if (b.gather) {
@@ -637,13 +641,15 @@ int va_op_attention_device(va_ctx* c, const float* q, const float* k, const floa
   fa.out_mode = 1;
   fa.o_hnd = out;
   fa.embed = heads * 64;
+  fa.v_f16 = 0;
   VA_CUDA(c, va::launch_flash(qb, kb, vb, fa, c->err, st));
   return VA_OK;
 }
 
 int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void* v,
                             int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
-                            int64_t seg_len, void* out, void* stream) {
+                            int64_t seg_len, int v_f16, int poly_per8, void* out,
+                            void* stream) {
   if (!c || !q || !k || !v || !out) return VA_ERR_INVALID;
   if (q_count <= 0 || kv_rows <= 0 || heads <= 0 || seg_len < 0 || q_offset < 0 ||
       kv_rows > 0x7fffffff / 64 / heads || q_count > kv_rows)
@@ -660,6 +666,12 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   fa.out_mode = 0;
   fa.o_tok = static_cast<__nv_bfloat16*>(out);
   fa.embed = heads * 64;
+  fa.v_f16 = v_f16 ? 1 : 0;
+  if (poly_per8 >= 0) {
+    if ((poly_per8 & 7) > 2 || (poly_per8 >> 3) > 5)
+      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..3)");
+    fa.poly_per8 = poly_per8;
+  }
   VA_CUDA(c, va::launch_flash(static_cast<const __nv_bfloat16*>(q),
                               static_cast<const __nv_bfloat16*>(k),
                               static_cast<const __nv_bfloat16*>(v), fa, c->err,

@@ -6,30 +6,36 @@
 // view-major sequence (global blocks: one segment of S*n tokens) or over each
 // view (local blocks batched: S segments of n tokens, block-diagonal).
 // Q and K arrive already QK-normalised and rotated (K1 epilogue, or the
-// Op::Attention prep kernel).  All operands are bf16 token-major [rows][E]; the
-// TMA box of head h is the 64-column slab [64h, 64h+64) (128 B per row), so a
-// rank's queries can run against a key window gathered from other ranks.
+// Op::Attention prep kernel).  All operands are token-major [rows][E]; the TMA
+// box of head h is the 64-column slab [64h, 64h+64) (128 B per row), so a rank's
+// queries can run against a key window gathered from other ranks.
 //
-// CTA = one (segment, head, pair of 128-query tiles).  10 warps:
-//   warp 0      TMA producer: Q0/Q1 once, then K_j/V_j into a STAGES-deep ring
-//   warp 1      TMEM owner + single-thread UMMA issuer
-//   warps 2..5  softmax warpgroup for query tile 0 (thread = query row)
-//   warps 6..9  softmax warpgroup for query tile 1
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384).
-// P_t (bf16x2-packed probabilities) overwrites the first 64 columns of S_t and
-// feeds the PV UMMA straight from TMEM (A operand in TMEM), so P never touches
-// shared memory.  The two query tiles ping-pong: while one warpgroup runs the
-// softmax of KV tile j, the tensor core runs the other tile's PV(j) and QK(j+1).
+// CTA = one (segment, head, pair of 128-query tiles).
+//   warp 0   TMA producer: Q0/Q1 once, then K_j/V_j into a STAGES-deep ring
+//   warp 1   TMEM owner + single-thread UMMA issuer
+//   softmax warps (two layouts, selected at launch):
+//     "rows"  10 warps: warps 2..5 / 6..9 own query tile 0 / 1, one row per thread
+//     "w20"   20 warps: warps 4..11 / 12..19 own tile 0 / 1; two warps share a TMEM
+//             lane quadrant (16 lanes each, 16x256b loads, 4 threads per row), so
+//             every SM sub-partition keeps 4 softmax warps in flight; setmaxnreg
+//             moves registers from warps 0..3 to the softmax warpgroups.
+// TMEM (512 columns), per query tile t: S_t (128 fp32 columns), P_t (64 columns
+// of packed bf16x2 probabilities), O_t (64 fp32 columns):
+//   S0 [0,128) P0 [128,192) O0 [192,256) S1 [256,384) P1 [384,448) O1 [448,512).
+// QK^T is an SS UMMA (M=128, N=128, K=16 x4); PV is a TS UMMA that reads P_t
+// straight from TMEM (M=128, N=64, K=16 x8, V as MN-major SW128 B operand).
 //
-// Per KV tile j and query tile t the issue order is PV_t(j-1) then QK_t(j); the
-// commit that signals S_t(j) therefore also covers PV_t(j-1), so when a softmax
-// warpgroup sees S_t(j) ready, O_t holds every earlier contribution and the
-// columns of P_t(j-1) may be overwritten.  O_t is rescaled in TMEM by its own
-// warpgroup when the running row max grows.
+// Pipeline per query tile t and KV tile j:
+//   softmax_t loads S_t(j) into registers and releases it at once (s_free), so
+//   the UMMA warp issues QK_t(j+1) while the exponentials of tile j run; it then
+//   waits for PV_t(j-1) (pv_done) before writing P_t(j) and, when the running
+//   max grew by more than 2^8, rescaling O_t in TMEM; p_full hands P_t(j) to PV_t(j).
+// The two query tiles ping-pong on the tensor core.
 #include <math.h>
 
 #include "va_internal.h"
 #include "va_ptx.cuh"
+#include "va_tmem16.cuh"
 
 namespace va {
 
@@ -38,19 +44,35 @@ namespace {
 constexpr int kTileQ = 128;
 constexpr int kTileK = 128;
 constexpr int kHeadDim = 64;
-constexpr int kStages = 3;
-constexpr int kFlashThreads = 320;
-constexpr uint32_t kTileBytes = kTileQ * kHeadDim * 2;  // 16 KB, one bf16 [128][64] tile
+constexpr int kStages = 4;
+constexpr int kRowsThreads = 320;  // "rows" layout
+constexpr int kW20Threads = 640;   // "w20" layout
+// setmaxnreg split of the w20 layout: warpgroup 0 (producer, UMMA, 2 idle warps)
+// drops to kW20LowRegs, the four softmax warpgroups rise to kW20HighRegs.  The
+// launch must give every thread at least kW20MinLaunchRegs registers, checked on
+// the host (cudaFuncGetAttributes) before each launch: 128*low + 512*high must
+// not exceed 640 * launch registers, or setmaxnreg.inc would wait forever.
+constexpr int kW20LowRegs = 40;
+constexpr int kW20HighRegs = 104;
+constexpr int kW20MinLaunchRegs = (128 * kW20LowRegs + 512 * kW20HighRegs + 639) / 640;
+constexpr uint32_t kTileBytes = kTileQ * kHeadDim * 2;  // 16 KB, one 2-byte [128][64] tile
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO0 = 256;
+__host__ __device__ constexpr uint32_t col_s(int t) { return t * 256; }
+__host__ __device__ constexpr uint32_t col_p(int t) { return t * 256 + 128; }
+__host__ __device__ constexpr uint32_t col_o(int t) { return t * 256 + 192; }
+// A softmax thread rescales O (in TMEM) only when a tile raises a row's running
+// maximum by more than 2^8; until then it keeps exponentiating against the older,
+// smaller maximum, so probabilities stay <= 256 (exact enough in bf16, F32 sums).
+constexpr float kRescaleLog2 = 8.0f;
 
 struct FlashSmem {
   static constexpr uint32_t kQ = 0;                              // Q0, Q1
   static constexpr uint32_t kK = 2 * kTileBytes;                 // K ring
   static constexpr uint32_t kV = kK + kStages * kTileBytes;      // V ring
   static constexpr uint32_t kBar = kV + kStages * kTileBytes;
-  // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_final[2]
-  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 6;
+  // barriers: q_full, kv_full[S], kv_empty[S], then per tile s_full, s_free,
+  // p_full, pv_done, o_final, ex_done
+  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 12;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kBytes = kMisc + 64;
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;
@@ -69,268 +91,602 @@ __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
   }
 }
 
-__global__ void __launch_bounds__(kFlashThreads, 1)
-    flash_fwd_d64_kernel(const __grid_constant__ CUtensorMap map_q,
-                         const __grid_constant__ CUtensorMap map_k,
-                         const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
-  using L = FlashSmem;
+// Per-CTA geometry: the query rows of this CTA (local Q buffer) and its keys.
+struct Geom {
+  int q0, q_end, k0, klen, nq, num_kv, col, head;
+  bool tail_mask;
+};
+
+__device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
+  Geom g;
+  const bool global = fa.seg_len == 0;
+  const int seg = blockIdx.z;
+  const int q_seg0 = global ? 0 : seg * fa.seg_len;
+  g.q_end = global ? fa.q_count : q_seg0 + fa.seg_len;
+  g.q0 = q_seg0 + blockIdx.x * 2 * kTileQ;
+  g.k0 = global ? 0 : fa.q_offset + q_seg0;
+  g.klen = global ? fa.kv_rows : fa.seg_len;
+  g.nq = (g.q_end - g.q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
+  g.num_kv = (g.klen + kTileK - 1) / kTileK;
+  g.tail_mask = (g.num_kv * kTileK) != g.klen;
+  g.head = blockIdx.y;
+  g.col = g.head * kHeadDim;
+  return g;
+}
+
+// Shared-memory handles of one CTA.
+struct Ctl {
+  uint32_t base;
+  uint8_t* smem;
+  __device__ uint32_t bar(int i) const { return base + FlashSmem::kBar + 8u * i; }
+  __device__ uint32_t q_full() const { return bar(0); }
+  __device__ uint32_t kv_full(int s) const { return bar(1 + s); }
+  __device__ uint32_t kv_empty(int s) const { return bar(1 + kStages + s); }
+  __device__ uint32_t s_full(int t) const { return bar(1 + 2 * kStages + t); }
+  __device__ uint32_t s_free(int t) const { return bar(3 + 2 * kStages + t); }
+  __device__ uint32_t p_full(int t) const { return bar(5 + 2 * kStages + t); }
+  __device__ uint32_t pv_done(int t) const { return bar(7 + 2 * kStages + t); }
+  __device__ uint32_t o_final(int t) const { return bar(9 + 2 * kStages + t); }
+  __device__ uint32_t ex_done(int t) const { return bar(11 + 2 * kStages + t); }
+  __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(smem + FlashSmem::kMisc); }
+  __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 4); }
+  __device__ volatile int* kv_issued() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 8); }
+  __device__ volatile int* kv_consumed() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 12); }
+  __device__ volatile int* mma_done() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 16); }
+  __device__ uint32_t sQ(int t) const { return base + FlashSmem::kQ + t * kTileBytes; }
+  __device__ uint32_t sK(int s) const { return base + FlashSmem::kK + s * kTileBytes; }
+  __device__ uint32_t sV(int s) const { return base + FlashSmem::kV + s * kTileBytes; }
+};
+
+__device__ __forceinline__ Ctl make_ctl() {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
-  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
-  uint8_t* smem = smem_raw + (base - raw_u32);
+  Ctl c;
+  c.base = (raw_u32 + 1023u) & ~1023u;
+  c.smem = smem_raw + (c.base - raw_u32);
+  return c;
+}
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int pair = blockIdx.x;
-  const int head = blockIdx.y;
-  const int seg = blockIdx.z;
-  const bool global = fa.seg_len == 0;
-  // Query rows of this CTA (in the local Q buffer) and the key range they see.
-  const int q_seg0 = global ? 0 : seg * fa.seg_len;
-  const int q_end = global ? fa.q_count : q_seg0 + fa.seg_len;
-  const int q0 = q_seg0 + pair * 2 * kTileQ;
-  const int k0 = global ? 0 : fa.q_offset + q_seg0;
-  const int klen = global ? fa.kv_rows : fa.seg_len;
-  const int nq = (q_end - q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
-  const int num_kv = (klen + kTileK - 1) / kTileK;
-  const bool tail_mask = (num_kv * kTileK) != klen;
-  const int col = head * kHeadDim;
-
-  const uint32_t bar_q = base + L::kBar;
-  auto bar_kv_full = [&](int s) { return base + L::kBar + 8u * (1 + s); };
-  auto bar_kv_empty = [&](int s) { return base + L::kBar + 8u * (1 + kStages + s); };
-  auto bar_s_full = [&](int t) { return base + L::kBar + 8u * (1 + 2 * kStages + t); };
-  auto bar_p_full = [&](int t) { return base + L::kBar + 8u * (3 + 2 * kStages + t); };
-  auto bar_o_final = [&](int t) { return base + L::kBar + 8u * (5 + 2 * kStages + t); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
-  volatile int* kv_issued = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
-  volatile int* kv_consumed = reinterpret_cast<volatile int*>(smem + L::kMisc + 12);
-  volatile int* mma_done = reinterpret_cast<volatile int*>(smem + L::kMisc + 16);
-  auto sQ = [&](int t) { return base + L::kQ + t * kTileBytes; };
-  auto sK = [&](int s) { return base + L::kK + s * kTileBytes; };
-  auto sV = [&](int s) { return base + L::kV + s * kTileBytes; };
-
+// Barrier init (thread 0) and TMEM allocation (warp 1); every thread returns the
+// TMEM base after the CTA-wide barrier.  softmax_threads = arrivals per tile.
+__device__ __forceinline__ uint32_t cta_setup(const Ctl& c, int softmax_threads,
+                                              const CUtensorMap* mq, const CUtensorMap* mk,
+                                              const CUtensorMap* mv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1);
+    mbar_init(c.q_full(), 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar_kv_full(s), 1);
-      mbar_init(bar_kv_empty(s), 1);
+      mbar_init(c.kv_full(s), 1);
+      mbar_init(c.kv_empty(s), 1);
     }
     for (int t = 0; t < 2; ++t) {
-      mbar_init(bar_s_full(t), 1);
-      mbar_init(bar_p_full(t), 128);
-      mbar_init(bar_o_final(t), 1);
+      mbar_init(c.s_full(t), 1);
+      mbar_init(c.s_free(t), softmax_threads);
+      mbar_init(c.p_full(t), softmax_threads);
+      mbar_init(c.pv_done(t), 1);
+      mbar_init(c.o_final(t), 1);
+      mbar_init(c.ex_done(t), softmax_threads);
     }
-    *abort_flag = 0;
-    *kv_issued = 0;
-    *kv_consumed = 0;
-    *mma_done = 0;
+    *c.abort_flag() = 0;
+    *c.kv_issued() = 0;
+    *c.kv_consumed() = 0;
+    *c.mma_done() = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&map_q);
-    tma_prefetch_desc(&map_k);
-    tma_prefetch_desc(&map_v);
+    tma_prefetch_desc(mq);
+    tma_prefetch_desc(mk);
+    tma_prefetch_desc(mv);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_alloc(smem_u32(c.tmem_slot()), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  return *c.tmem_slot();
+}
+
+// TMA producer (one thread).
+__device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const CUtensorMap* mq,
+                                             const CUtensorMap* mk, const CUtensorMap* mv,
+                                             int* err) {
+  // Every box starts inside the tensor; rows past its end are zero-filled.
+  mbar_arrive_expect_tx(c.q_full(), g.nq * kTileBytes);
+  tma_load_2d(c.sQ(0), mq, c.q_full(), g.col, g.q0);
+  if (g.nq == 2) tma_load_2d(c.sQ(1), mq, c.q_full(), g.col, g.q0 + kTileQ);
+  for (int j = 0; j < g.num_kv; ++j) {
+    const int s = j % kStages;
+    const uint32_t ph = (j / kStages) & 1;
+    if (!mbar_wait(c.kv_empty(s), ph ^ 1, c.abort_flag(), err, kDevTimeoutProducer)) break;
+    mbar_arrive_expect_tx(c.kv_full(s), 2 * kTileBytes);
+    tma_load_2d(c.sK(s), mk, c.kv_full(s), g.col, g.k0 + j * kTileK);
+    tma_load_2d(c.sV(s), mv, c.kv_full(s), g.col, g.k0 + j * kTileK);
+    *c.kv_issued() = j + 1;
+  }
+}
+
+// Single-thread UMMA issuer.
+template <bool kF16>
+__device__ __forceinline__ void run_mma(const Ctl& c, const Geom& g, uint32_t tmem, int* err) {
+  constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
+  constexpr uint32_t idesc_pv = kF16 ? idesc_f16_f32(kTileQ, kHeadDim, false, true)
+                                     : idesc_bf16_f32(kTileQ, kHeadDim, false, true);
+  volatile int* abort_flag = c.abort_flag();
+  auto issue_qk = [&](int t, int s) {
+#pragma unroll
+    for (int k = 0; k < kHeadDim / 16; ++k) {
+      const uint64_t ad = sdesc_sw128(c.sQ(t) + k * 32, 16, 1024);
+      const uint64_t bd = sdesc_sw128(c.sK(s) + k * 32, 16, 1024);
+      umma_ss(tmem + col_s(t), ad, bd, idesc_qk, k != 0 ? 1u : 0u);
+    }
+  };
+  auto issue_pv = [&](int t, int s, bool acc) {
+#pragma unroll
+    for (int k = 0; k < kTileK / 16; ++k) {
+      // B = V tile, MN-major: 16 keys per step = 16 rows of 128 B.
+      const uint64_t bd = sdesc_sw128(c.sV(s) + k * 16 * 128, 8192, 1024);
+      umma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, bd, idesc_pv, (acc || k != 0) ? 1u : 0u);
+    }
+  };
+  // QK_t(jj) for jj >= 1 needs K(jj) (waited for once, by t == 0) and S_t free,
+  // i.e. softmax_t holding S_t(jj-1) in registers.
+  auto next_qk = [&](int t, int jj) {
+    bool r = true;
+    if (t == 0) {
+      r = mbar_wait(c.kv_full(jj % kStages), (jj / kStages) & 1, abort_flag, err, kDevTimeoutMma);
+      if (r) *c.kv_consumed() = jj + 1;
+    }
+    if (r) r = mbar_wait(c.s_free(t), (jj - 1) & 1, abort_flag, err, kDevTimeoutMma);
+    if (r) {
+      tc_fence_after();
+      issue_qk(t, jj % kStages);
+      tc_commit(c.s_full(t));
+    }
+    return r;
+  };
+  bool ok = mbar_wait(c.q_full(), 0, abort_flag, err, kDevTimeoutMma);
+  if (ok) ok = mbar_wait(c.kv_full(0), 0, abort_flag, err, kDevTimeoutMma);
+  if (ok) {
+    *c.kv_consumed() = 1;
+    tc_fence_after();
+    for (int t = 0; t < g.nq; ++t) {
+      issue_qk(t, 0);
+      tc_commit(c.s_full(t));
+    }
+  }
+  for (int t = 0; ok && t < g.nq && g.num_kv > 1; ++t) ok = next_qk(t, 1);
+  // Issue order follows the order the softmax warpgroups finish in: PV_0(j),
+  // QK_0(j+2), PV_1(j), QK_1(j+2); the S tile of step j+2 is ready a whole step
+  // before its warpgroup needs it.
+  for (int j = 0; ok && j < g.num_kv; ++j) {
+    const int s = j % kStages;
+    for (int t = 0; t < g.nq && ok; ++t) {
+      ok = mbar_wait(c.p_full(t), j & 1, abort_flag, err, kDevTimeoutMma);
+      if (!ok) break;
+      tc_fence_after();
+      issue_pv(t, s, j > 0);
+      tc_commit(c.pv_done(t));
+      if (j + 2 < g.num_kv) ok = next_qk(t, j + 2);
+    }
+    tc_commit(c.kv_empty(s));
+  }
+  for (int t = 0; t < 2; ++t) tc_commit(c.o_final(t));
+  *c.mma_done() = 1;
+}
+
+// Drains in-flight copies/UMMAs after an abort, then frees TMEM (warp 1).
+__device__ __forceinline__ void cta_teardown(const Ctl& c, uint32_t tmem) {
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *c.abort_flag()) {
+    if (*c.kv_consumed() == 0) drain(c.q_full(), 0);
+    for (int j = *c.kv_consumed(); j < *c.kv_issued(); ++j) drain(c.kv_full(j % kStages), (j / kStages) & 1);
+    if (*c.mma_done()) drain(c.o_final(0), 0);
+  }
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+__device__ __forceinline__ void store_o_row_bf16(__nv_bfloat16* dst, const float* o, float inv) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 w;
+    w.x = pack_bf16x2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+    w.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+    w.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+    w.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+    d[c] = w;
+  }
+}
+
+// ============================================================== "rows" layout
+// P = 2^(s*scale - m) for 128 keys of one row as 64 bf16x2 pairs; returns the F32
+// row sum.  In every group of 8 pairs, the last kPoly pairs are exponentiated on
+// the FMA pipe (exp2_fma_x2) and the others on MUFU (ex2.approx).
+// kForm selects the instruction formulation (measured against each other):
+//   0: x via packed f32x2 FMA, row sum in 8 scalar accumulators
+//   1: x via scalar FFMA, row sum in 4 packed f32x2 accumulators
+//   2: x via packed f32x2 FMA, row sum in 4 packed f32x2 accumulators
+//   4: as 2, with the bf16 pack done by integer rounding + byte permute instead of
+//      the F32->bf16x2 conversion instruction (round half up at the bf16 boundary)
+template <int kPoly, int kForm>
+__device__ __forceinline__ float softmax_pairs_bf16(const float* s, uint64_t sc2, uint64_t neg2,
+                                                   uint32_t* pk) {
+  float acc[8];
+  uint64_t acc2[4];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    float x0, x1, p0, p1;
+    if (kForm == 1) {
+      float sl, nm;
+      f32x2_unpack(sc2, sl, nm);
+      f32x2_unpack(neg2, nm, nm);
+      x0 = fmaf(s[2 * i], sl, nm);
+      x1 = fmaf(s[2 * i + 1], sl, nm);
+    } else {
+      f32x2_unpack(f32x2_fma(f32x2_pack(s[2 * i], s[2 * i + 1]), sc2, neg2), x0, x1);
+    }
+    if ((i & 7) >= 8 - kPoly) {
+      exp2_fma_x2(x0, x1, p0, p1);
+    } else {
+      p0 = ex2(x0);
+      p1 = ex2(x1);
+    }
+    if (kForm == 0) {
+      acc[i & 7] = (i < 8) ? p0 + p1 : acc[i & 7] + (p0 + p1);
+    } else {
+      const uint64_t pp = f32x2_pack(p0, p1);
+      acc2[i & 3] = (i < 4) ? pp : f32x2_add(acc2[i & 3], pp);
+    }
+    if (kForm == 4)
+      pk[i] = pack_bf16x2_round_prmt(p0, p1);
+    else
+      pk[i] = pack_bf16x2(p0, p1);
+  }
+  if (kForm == 0)
+    return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+  const uint64_t a = f32x2_add(f32x2_add(acc2[0], acc2[1]), f32x2_add(acc2[2], acc2[3]));
+  float lo, hi;
+  f32x2_unpack(a, lo, hi);
+  return lo + hi;
+}
+
+// The f16 variant: x in packed F32, one cvt and one MUFU ex2.f16x2 per pair, P and
+// V in f16.  Measured slower than the bf16 path on B200; kept for comparison.
+__device__ __forceinline__ float softmax_pairs_f16(const float* s, uint64_t sc2, uint64_t neg2,
+                                                  uint32_t* pk) {
+  uint32_t acc[8];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    float x0, x1;
+    f32x2_unpack(f32x2_fma(f32x2_pack(s[2 * i], s[2 * i + 1]), sc2, neg2), x0, x1);
+    pk[i] = f16x2_ex2(f16x2_from_f32(x0, x1));
+    acc[i & 7] = (i < 8) ? pk[i] : f16x2_add(acc[i & 7], pk[i]);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum += f16x2_sum_to_f32(acc[i]);
+  return sum;
+}
+
+// kF16: V and P are f16; otherwise V and P are bf16 and kPoly of every 8
+// exponential pairs run on the FMA pipe.  Q and K are bf16.
+template <bool kF16, int kPoly, int kForm>
+__global__ void __launch_bounds__(kRowsThreads, 1)
+    flash_fwd_d64_kernel(const __grid_constant__ CUtensorMap map_q,
+                         const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  const Ctl c = make_ctl();
+  const Geom g = make_geom(fa);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t tmem = cta_setup(c, 128, &map_q, &map_k, &map_v);
+  volatile int* abort_flag = c.abort_flag();
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      // Every box starts inside the tensor; rows past its end are zero-filled.
-      mbar_arrive_expect_tx(bar_q, nq * kTileBytes);
-      tma_load_2d(sQ(0), &map_q, bar_q, col, q0);
-      if (nq == 2) tma_load_2d(sQ(1), &map_q, bar_q, col, q0 + kTileQ);
-      for (int j = 0; j < num_kv; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(bar_kv_empty(s), ph ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
-        mbar_arrive_expect_tx(bar_kv_full(s), 2 * kTileBytes);
-        tma_load_2d(sK(s), &map_k, bar_kv_full(s), col, k0 + j * kTileK);
-        tma_load_2d(sV(s), &map_v, bar_kv_full(s), col, k0 + j * kTileK);
-        *kv_issued = j + 1;
-      }
-    }
+    if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
   } else if (warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileQ, kHeadDim, false, true);
-      bool ok = mbar_wait(bar_q, 0, abort_flag, err, kDevTimeoutMma);
-      auto issue_qk = [&](int t, int s) {
-#pragma unroll
-        for (int k = 0; k < kHeadDim / 16; ++k) {
-          const uint64_t ad = sdesc_sw128(sQ(t) + k * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(sK(s) + k * 32, 16, 1024);
-          umma_ss(tmem + kColS0 + t * 128, ad, bd, idesc_qk, k != 0 ? 1u : 0u);
-        }
-      };
-      auto issue_pv = [&](int t, int s, bool acc) {
-#pragma unroll
-        for (int k = 0; k < kTileK / 16; ++k) {
-          // B = V tile, MN-major: 16 keys per step = 16 rows of 128 B.
-          const uint64_t bd = sdesc_sw128(sV(s) + k * 16 * 128, 8192, 1024);
-          umma_ts(tmem + kColO0 + t * 64, tmem + kColS0 + t * 128 + k * 8, bd, idesc_pv,
-                  (acc || k != 0) ? 1u : 0u);
-        }
-      };
-      if (ok) ok = mbar_wait(bar_kv_full(0), 0, abort_flag, err, kDevTimeoutMma);
-      if (ok) {
-        *kv_consumed = 1;
-        tc_fence_after();
-        for (int t = 0; t < nq; ++t) {
-          issue_qk(t, 0);
-          tc_commit(bar_s_full(t));
-        }
-      }
-      for (int j = 0; ok && j < num_kv; ++j) {
-        const int s = j % kStages;
-        for (int t = 0; t < nq && ok; ++t) {
-          ok = mbar_wait(bar_p_full(t), j & 1, abort_flag, err, kDevTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(t, s, j > 0);
-          if (j + 1 < num_kv) {
-            const int s1 = (j + 1) % kStages;
-            if (t == 0) {
-              ok = mbar_wait(bar_kv_full(s1), ((j + 1) / kStages) & 1, abort_flag, err,
-                             kDevTimeoutMma);
-              if (!ok) break;
-              *kv_consumed = j + 2;
-              tc_fence_after();
-            }
-            issue_qk(t, s1);
-            tc_commit(bar_s_full(t));
-          }
-        }
-        tc_commit(bar_kv_empty(s));
-      }
-      for (int t = 0; t < 2; ++t) tc_commit(bar_o_final(t));
-      *mma_done = 1;
-    }
+    if (lane == 0) run_mma<kF16>(c, g, tmem, err);
   } else {
-    // ------------------------------------------------------------ softmax
     const int t = (warp - 2) >> 2;              // query tile of this warpgroup
     const int quad = warp & 3;                  // TMEM lane quadrant
     const int r = quad * 32 + lane;             // row inside the query tile
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off + kColS0 + t * 128;
-    const uint32_t tO = tmem + lane_off + kColO0 + t * 64;
+    const uint32_t tS = tmem + lane_off + col_s(t);
+    const uint32_t tP = tmem + lane_off + col_p(t);
+    const uint32_t tO = tmem + lane_off + col_o(t);
     const float sl2 = fa.scale_log2;
-    if (t < nq) {
+    if (t < g.nq) {
       float m = -INFINITY;  // running max, log2 domain (already multiplied by scale_log2)
       float l = 0.f;
       bool ok = true;
-      for (int j = 0; j < num_kv; ++j) {
-        ok = mbar_wait(bar_s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
+      for (int j = 0; j < g.num_kv; ++j) {
+        ok = mbar_wait(c.s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
         float s[128];
+        tmem_ld128(tS, s);
+        tc_fence_before();
+        mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
+        const bool tail = g.tail_mask && j == g.num_kv - 1;
+        if (tail) {
+          const int valid = g.klen - j * kTileK;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s + c * 32);
-        if (tail_mask && j == num_kv - 1) {
-          const int valid = klen - j * kTileK;
-#pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (c >= valid) s[c] = -INFINITY;
+          for (int q = 0; q < 128; ++q)
+            if (q >= valid) s[q] = -INFINITY;
         }
-        float mx = s[0];
+        // Row maximum as a tree of 3-input maxima (no 128-long dependency chain).
+        float mx8[8];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
-        const float m_new = fmaxf(m, mx * sl2);
-        const float alpha = ex2(m - m_new);  // 0 on the first tile (m = -inf)
-        const float neg = -m_new;
-        float sum = 0.f;
+        for (int i = 0; i < 8; ++i) mx8[i] = max3f(s[i], s[8 + i], s[16 + i]);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
+        for (int q = 24; q < 120; q += 16)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = ex2(fmaf(s[c * 32 + 2 * i], sl2, neg));
-            const float p1 = ex2(fmaf(s[c * 32 + 2 * i + 1], sl2, neg));
-            sum += p0 + p1;
-            pk[i] = pack_bf16x2(p0, p1);
-          }
-          tmem_st16(tS + c * 16, pk);
+          for (int i = 0; i < 8; ++i) mx8[i] = max3f(mx8[i], s[q + i], s[q + 8 + i]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], s[120 + i]);
+        const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7])) * sl2;
+        // Conditional rescale: keep the running max unless the tile raises it by
+        // more than kRescaleLog2 (probabilities then stay <= 2^kRescaleLog2).
+        const bool grow = mx > m + kRescaleLog2;
+        const float m_new = grow ? mx : m;
+        const float alpha = grow ? ex2(m - m_new) : 1.0f;  // 0 on the first tile (m = -inf)
+        const uint64_t sc2 = f32x2_pack(sl2, sl2);
+        const uint64_t neg2 = f32x2_pack(-m_new, -m_new);
+        uint32_t pk[64];
+        float sum;
+        // The two warpgroups take turns in the exponential section (tile 0 of step
+        // j, tile 1 of step j, tile 0 of step j+1, ...): MUFU then serves one of
+        // them at a time while the other does its loads, maxima and stores.
+        if (g.nq == 2 && (t == 1 || j > 0)) {
+          ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
+                         kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
         }
-        if (j > 0 && __any_sync(0xffffffffu, alpha < 1.0f)) {
+        if constexpr (kF16) {
+          sum = softmax_pairs_f16(s, sc2, neg2, pk);
+        } else {
+          // Masked keys (-inf) only occur on the tail tile, which stays on MUFU so
+          // they contribute exactly 0.
+          if (tail)
+            sum = softmax_pairs_bf16<0, kForm>(s, sc2, neg2, pk);
+          else
+            sum = softmax_pairs_bf16<kPoly, kForm>(s, sc2, neg2, pk);
+        }
+        if (g.nq == 2) mbar_arrive(c.ex_done(t));
+        if (j > 0) {
+          // PV_t(j-1) has finished reading P_t and adding into O_t.
+          ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tmem_st64(tP, pk);
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
           float o[64];
           tmem_ld32(tO, o);
           tmem_ld32(tO + 32, o + 32);
-          uint32_t u[16];
+          uint32_t u[64];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(o[c * 16 + i] * alpha);
-            tmem_st16(tO + c * 16, u);
-          }
+          for (int i = 0; i < 64; ++i) u[i] = __float_as_uint(o[i] * alpha);
+          tmem_st64(tO, u);
         }
         tmem_wait_st();
         l = l * alpha + sum;
         m = m_new;
         tc_fence_before();
-        mbar_arrive(bar_p_full(t));
+        mbar_arrive(c.p_full(t));
       }
-      bool fin = ok && mbar_wait(bar_o_final(t), 0, abort_flag, err, kDevTimeoutConsumer);
+      bool fin = ok && mbar_wait(c.o_final(t), 0, abort_flag, err, kDevTimeoutConsumer);
       fin = __all_sync(0xffffffffu, fin);
       if (fin) {
         tc_fence_after();
         float o[64];
         tmem_ld32(tO, o);
         tmem_ld32(tO + 32, o + 32);
-        const int token = q0 + t * kTileQ + r;  // row of the local Q / O buffers
-        if (token < q_end) {
+        const int token = g.q0 + t * kTileQ + r;  // row of the local Q / O buffers
+        if (token < g.q_end) {
           const float inv = 1.0f / l;
           if (fa.out_mode == 0) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i) o[i] *= inv;
-            uint4* d = reinterpret_cast<uint4*>(fa.o_tok + static_cast<size_t>(token) * fa.embed +
-                                                head * kHeadDim);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              uint4 w;
-              w.x = pack_bf16x2(o[8 * c + 0], o[8 * c + 1]);
-              w.y = pack_bf16x2(o[8 * c + 2], o[8 * c + 3]);
-              w.z = pack_bf16x2(o[8 * c + 4], o[8 * c + 5]);
-              w.w = pack_bf16x2(o[8 * c + 6], o[8 * c + 7]);
-              d[c] = w;
-            }
+            store_o_row_bf16(fa.o_tok + static_cast<size_t>(token) * fa.embed + g.col, o, inv);
           } else {
             float4* d = reinterpret_cast<float4*>(
-                fa.o_hnd + (static_cast<size_t>(head) * fa.q_count + token) * kHeadDim);
+                fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim);
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-              d[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv,
-                                 o[4 * c + 3] * inv);
+            for (int q = 0; q < 16; ++q)
+              d[q] = make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv,
+                                 o[4 * q + 3] * inv);
           }
         }
       }
     }
   }
+  cta_teardown(c, tmem);
+}
 
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) {
-    // Drain copies and UMMAs still in flight before TMEM is released.
-    if (*kv_consumed == 0) drain(bar_q, 0);
-    for (int j = *kv_consumed; j < *kv_issued; ++j) drain(bar_kv_full(j % kStages), (j / kStages) & 1);
-    if (*mma_done) drain(bar_o_final(0), 0);
+// ============================================================== "w20" layout
+// 4 threads per row: thread i of a softmax warp owns rows (i/4) and (i/4 + 8) of
+// its 16-lane slice and, of every 8 key columns, the pair (2*(i%4), 2*(i%4)+1).
+// kOrder: the two query tiles take turns in the exponential section, as in the
+// "rows" layout.
+template <int kPoly, bool kOrder>
+__global__ void __launch_bounds__(kW20Threads, 1)
+    flash_fwd_d64_w20_kernel(const __grid_constant__ CUtensorMap map_q,
+                             const __grid_constant__ CUtensorMap map_k,
+                             const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  const Ctl c = make_ctl();
+  const Geom g = make_geom(fa);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t tmem = cta_setup(c, 256, &map_q, &map_k, &map_v);
+  volatile int* abort_flag = c.abort_flag();
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kW20LowRegs));
+    if (warp == 0) {
+      if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
+    } else if (warp == 1) {
+      if (lane == 0) run_mma<false>(c, g, tmem, err);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));
+    const int sw = warp - 4;                    // 0..15
+    const int t = sw >> 3;                      // query tile
+    const int quad = warp & 3;                  // TMEM lane quadrant of this warp
+    const int lane_base = quad * 32 + ((sw >> 2) & 1) * 16;
+    const uint32_t lane_off = static_cast<uint32_t>(lane_base) << 16;
+    const uint32_t tS = tmem + lane_off + col_s(t);
+    const uint32_t tP = tmem + lane_off + col_p(t);
+    const uint32_t tO = tmem + lane_off + col_o(t);
+    const int c0 = 2 * (lane & 3);              // first of my key pair in each 8-column block
+    const float sl2 = fa.scale_log2;
+    const uint64_t sc2 = f32x2_pack(sl2, sl2);
+    if (t < g.nq) {
+      float m0 = -INFINITY, m1 = -INFINITY;     // rows lane/4 and lane/4 + 8
+      float l0 = 0.f, l1 = 0.f;                 // partial sums over my columns
+      bool ok = true;
+      for (int j = 0; j < g.num_kv; ++j) {
+        ok = mbar_wait(c.s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        float s[64];  // block k: s[4k..4k+1] row 0 cols 8k+c0, +1; s[4k+2..4k+3] row 1
+        tmem_ld_16x256b_x16(tS, s);
+        tc_fence_before();
+        mbar_arrive(c.s_free(t));
+        const bool tail = g.tail_mask && j == g.num_kv - 1;
+        if (tail) {
+          const int valid = g.klen - j * kTileK;
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (8 * k + c0 + (e & 1) >= valid) s[4 * k + e] = -INFINITY;
+        }
+        float a0 = max3f(s[0], s[1], s[4]), a1 = max3f(s[2], s[3], s[6]);
+        float b0 = max3f(s[5], s[8], s[9]), b1 = max3f(s[7], s[10], s[11]);
+#pragma unroll
+        for (int k = 3; k < 16; k += 2) {
+          a0 = max3f(a0, s[4 * k], s[4 * k + 1]);
+          a1 = max3f(a1, s[4 * k + 2], s[4 * k + 3]);
+          if (k + 1 < 16) {
+            b0 = max3f(b0, s[4 * k + 4], s[4 * k + 5]);
+            b1 = max3f(b1, s[4 * k + 6], s[4 * k + 7]);
+          }
+        }
+        float mx0 = fmaxf(a0, b0), mx1 = fmaxf(a1, b1);
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * sl2;
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * sl2;
+        const bool grow0 = mx0 > m0 + kRescaleLog2, grow1 = mx1 > m1 + kRescaleLog2;
+        const float mn0 = grow0 ? mx0 : m0, mn1 = grow1 ? mx1 : m1;
+        const float al0 = grow0 ? ex2(m0 - mn0) : 1.0f, al1 = grow1 ? ex2(m1 - mn1) : 1.0f;
+        const uint64_t ng0 = f32x2_pack(-mn0, -mn0), ng1 = f32x2_pack(-mn1, -mn1);
+        if (kOrder && g.nq == 2 && (t == 1 || j > 0)) {
+          ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
+                         kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+        }
+        uint32_t pk[32];  // 16x128b order: block k: (row 0 pair k), (row 1 pair k)
+        uint64_t acc0 = 0, acc1 = 0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          float x0, x1, x2, x3, p0, p1, p2, p3;
+          f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k], s[4 * k + 1]), sc2, ng0), x0, x1);
+          f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k + 2], s[4 * k + 3]), sc2, ng1), x2, x3);
+          if (!tail && (k & 7) >= 8 - kPoly) {
+            exp2_fma_x2(x0, x1, p0, p1);
+            exp2_fma_x2(x2, x3, p2, p3);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+            p2 = ex2(x2);
+            p3 = ex2(x3);
+          }
+          const uint64_t q0 = f32x2_pack(p0, p1), q1 = f32x2_pack(p2, p3);
+          acc0 = (k == 0) ? q0 : f32x2_add(acc0, q0);
+          acc1 = (k == 0) ? q1 : f32x2_add(acc1, q1);
+          pk[2 * k] = pack_bf16x2(p0, p1);
+          pk[2 * k + 1] = pack_bf16x2(p2, p3);
+        }
+        if (kOrder && g.nq == 2) mbar_arrive(c.ex_done(t));
+        float u0, u1, v0, v1;
+        f32x2_unpack(acc0, u0, u1);
+        f32x2_unpack(acc1, v0, v1);
+        if (j > 0) {
+          ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tmem_st_16x128b_x16(tP, pk);
+        if (j > 0 && __any_sync(0xffffffffu, grow0 || grow1)) {
+          float o[32];  // block k: o[4k..4k+1] row 0, o[4k+2..4k+3] row 1
+          tmem_ld_16x256b_x8(tO, o);
+          uint32_t w[32];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            w[4 * k] = __float_as_uint(o[4 * k] * al0);
+            w[4 * k + 1] = __float_as_uint(o[4 * k + 1] * al0);
+            w[4 * k + 2] = __float_as_uint(o[4 * k + 2] * al1);
+            w[4 * k + 3] = __float_as_uint(o[4 * k + 3] * al1);
+          }
+          tmem_st_16x256b_x8(tO, w);
+        }
+        tmem_wait_st();
+        l0 = l0 * al0 + (u0 + u1);
+        l1 = l1 * al1 + (v0 + v1);
+        m0 = mn0;
+        m1 = mn1;
+        tc_fence_before();
+        mbar_arrive(c.p_full(t));
+      }
+      bool fin = ok && mbar_wait(c.o_final(t), 0, abort_flag, err, kDevTimeoutConsumer);
+      fin = __all_sync(0xffffffffu, fin);
+      if (fin) {
+        tc_fence_after();
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        float o[32];
+        tmem_ld_16x256b_x8(tO, o);
+        const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const int token = g.q0 + t * kTileQ + lane_base + (lane >> 2) + 8 * rr;
+          if (token >= g.q_end) continue;
+          const float inv = rr ? inv1 : inv0;
+          if (fa.out_mode == 0) {
+            uint32_t* d = reinterpret_cast<uint32_t*>(fa.o_tok + static_cast<size_t>(token) * fa.embed +
+                                                      g.col + c0);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              d[4 * k] = pack_bf16x2(o[4 * k + 2 * rr] * inv, o[4 * k + 2 * rr + 1] * inv);
+          } else {
+            float2* d = reinterpret_cast<float2*>(
+                fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim + c0);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              d[4 * k] = make_float2(o[4 * k + 2 * rr] * inv, o[4 * k + 2 * rr + 1] * inv);
+          }
+        }
+      }
+    }
   }
-  __syncthreads();
-  if (warp == 1) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
-  }
+  cta_teardown(c, tmem);
 }
 
 }  // namespace
@@ -349,18 +705,55 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
       return cudaErrorInvalidValue;
     segs = fa.q_count / fa.seg_len;
   }
+  // V is bf16 or f16; TMA copies 2-byte elements either way (zero fill is 0x0000
+  // in both types), so one bf16 map description serves both.
   CUtensorMap mq, mk, mv;
   if (!encode_tma_2d_bf16(&mq, q, fa.embed, fa.q_count, kHeadDim, kTileQ) ||
       !encode_tma_2d_bf16(&mk, k, fa.embed, fa.kv_rows, kHeadDim, kTileK) ||
       !encode_tma_2d_bf16(&mv, v, fa.embed, fa.kv_rows, kHeadDim, kTileK))
     return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(flash_fwd_d64_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+  // Variant = poly + 8 * form: form 0..2 = "rows" layout formulations, form 3 = w20.
+  using Kern = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, FlashArgs, int*);
+  static const Kern rows[5][3] = {
+      {flash_fwd_d64_kernel<false, 0, 0>, flash_fwd_d64_kernel<false, 1, 0>,
+       flash_fwd_d64_kernel<false, 2, 0>},
+      {flash_fwd_d64_kernel<false, 0, 1>, flash_fwd_d64_kernel<false, 1, 1>,
+       flash_fwd_d64_kernel<false, 2, 1>},
+      {flash_fwd_d64_kernel<false, 0, 2>, flash_fwd_d64_kernel<false, 1, 2>,
+       flash_fwd_d64_kernel<false, 2, 2>},
+      {nullptr, nullptr, nullptr},
+      {flash_fwd_d64_kernel<false, 0, 4>, flash_fwd_d64_kernel<false, 1, 4>,
+       flash_fwd_d64_kernel<false, 2, 4>}};
+  static const Kern w20[2][3] = {
+      {flash_fwd_d64_w20_kernel<0, false>, flash_fwd_d64_w20_kernel<1, false>,
+       flash_fwd_d64_w20_kernel<2, false>},
+      {flash_fwd_d64_w20_kernel<0, true>, flash_fwd_d64_w20_kernel<1, true>,
+       flash_fwd_d64_w20_kernel<2, true>}};
+  Kern kern;
+  int threads = kRowsThreads;
+  if (fa.v_f16) {
+    kern = flash_fwd_d64_kernel<true, 0, 0>;
+  } else {
+    const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
+    if (fa.poly_per8 < 0 || poly > 2 || form > 5) return cudaErrorInvalidValue;
+    if (form == 3 || form == 5) {
+      kern = w20[form == 5][poly];
+      threads = kW20Threads;
+      // setmaxnreg.inc draws on the registers the CTA launched with.
+      cudaFuncAttributes attr;
+      cudaError_t e = cudaFuncGetAttributes(&attr, kern);
+      if (e != cudaSuccess) return e;
+      if (attr.numRegs < kW20MinLaunchRegs) return cudaErrorInvalidConfiguration;
+    } else {
+      kern = rows[form][poly];
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        FlashSmem::kLaunchBytes);
   if (e != cudaSuccess) return e;
   const int span = fa.seg_len > 0 ? fa.seg_len : fa.q_count;
   dim3 grid((span + 2 * kTileQ - 1) / (2 * kTileQ), fa.heads, segs);
-  flash_fwd_d64_kernel<<<grid, kFlashThreads, FlashSmem::kLaunchBytes, st>>>(mq, mk, mv, fa, err);
+  kern<<<grid, threads, FlashSmem::kLaunchBytes, st>>>(mq, mk, mv, fa, err);
   return cudaGetLastError();
 }
 

@@ -91,6 +91,19 @@ __device__ __forceinline__ void store_bf16_row64(__nv_bfloat16* dst, const float
   }
 }
 
+__device__ __forceinline__ void store_f16_row64(__nv_bfloat16* dst, const float* x) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 u;
+    u.x = f16x2_from_f32(x[8 * c + 0], x[8 * c + 1]);
+    u.y = f16x2_from_f32(x[8 * c + 2], x[8 * c + 3]);
+    u.z = f16x2_from_f32(x[8 * c + 4], x[8 * c + 5]);
+    u.w = f16x2_from_f32(x[8 * c + 6], x[8 * c + 7]);
+    d[c] = u;
+  }
+}
+
 struct QkvEpilogue {
   QkvEpilogueArgs a;
   template <int BN>
@@ -113,7 +126,11 @@ struct QkvEpilogue {
         if (g) head_layernorm(x, g, b, a.qk_eps);
         if (a.pos) head_rope(x, a.pos[grow], a.rope_cs, a.rope_pairing);
       }
-      store_bf16_row64(base + static_cast<size_t>(grow) * a.embed + (h0 + hh) * 64, x);
+      __nv_bfloat16* dst = base + static_cast<size_t>(grow) * a.embed + (h0 + hh) * 64;
+      if (section == 2 && a.v_f16)
+        store_f16_row64(dst, x);
+      else
+        store_bf16_row64(dst, x);
     }
   }
 };

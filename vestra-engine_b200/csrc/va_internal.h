@@ -21,9 +21,10 @@ struct QkvEpilogueArgs {
   int rope_pairing;                    // 0 rotate-half, 1 interleaved
   __nv_bfloat16* q_out;                // [rows][E], head h at columns [64h, 64h+64)
   __nv_bfloat16* k_out;                // [rows][E] (may be a rank's slice of a gathered buffer)
-  __nv_bfloat16* v_out;
+  __nv_bfloat16* v_out;               // bf16, or f16 bits when v_f16
   int rows;
   int embed;
+  int v_f16;                           // store V as f16 (the PV UMMA then runs in f16)
 };
 
 // ---- output projection (K3): O[rows,E] bf16 x Wp^T + b (* ls1) (+ residual) -> F32 ----
@@ -37,6 +38,7 @@ struct ProjEpilogueArgs {
 };
 
 // ---- fused flash attention (K2) ----
+constexpr int kDefaultPolyPer8 = 1;
 // Q is [q_count][E] token-major (this rank's queries, the first of which is row
 // q_offset of the key window); K and V are [kv_rows][E] token-major.
 // seg_len == 0: global attention, every query sees all kv_rows keys.
@@ -53,6 +55,8 @@ struct FlashArgs {
   __nv_bfloat16* o_tok;
   float* o_hnd;
   int embed;
+  int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
+  int poly_per8 = kDefaultPolyPer8;  // bf16 path: exponential pairs of every 8 done on the FMA pipe (0..4)
 };
 
 // Tensor-map encoding through the driver entry point (no -lcuda needed).
@@ -78,7 +82,7 @@ cudaError_t launch_ln_cast(const float* x, const float* g, const float* b, float
 // token-major bf16 [n][H*64].
 cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, const float* b,
                               float eps, const int2* pos, const float2* rope_cs, int rope_pairing,
-                              __nv_bfloat16* y, cudaStream_t st);
+                              __nv_bfloat16* y, cudaStream_t st, bool out_f16 = false);
 // Camera-token slots (backbone.rs:746-768): token 0 of view 0 <- cam[0:E],
 // token 0 of every later view <- cam[E:2E].
 cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(256) ln_cast_kernel(const float* __restrict__ 
 __global__ void __launch_bounds__(256) prep_heads_kernel(
     const float* __restrict__ x, int rows_total, const float* __restrict__ g,
     const float* __restrict__ b, float eps, const int2* __restrict__ pos, int n,
-    const float2* __restrict__ cs, int pairing, __nv_bfloat16* __restrict__ y) {
+    const float2* __restrict__ cs, int pairing, __nv_bfloat16* __restrict__ y, bool out_f16) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows_total) return;
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(256) prep_heads_kernel(
   const int heads = rows_total / n;
   const int h = row / n, t = row - h * n;
   reinterpret_cast<uint32_t*>(y + (static_cast<size_t>(t) * heads + h) * 64)[lane] =
-      pack_bf16x2(a0, a1);
+      out_f16 ? f16x2_from_f32(a0, a1) : pack_bf16x2(a0, a1);
 }
 
 __global__ void camera_inject_kernel(float* tokens, const float* cam, int views,
@@ -213,11 +213,11 @@ cudaError_t launch_ln_cast(const float* x, const float* g, const float* b, float
 
 cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, const float* b,
                               float eps, const int2* pos, const float2* rope_cs, int rope_pairing,
-                              __nv_bfloat16* y, cudaStream_t st) {
+                              __nv_bfloat16* y, cudaStream_t st, bool out_f16) {
   const int total = heads * n;
   if (total <= 0) return cudaSuccess;
   prep_heads_kernel<<<(total + 7) / 8, 256, 0, st>>>(x, total, g, b, eps, pos, n, rope_cs,
-                                                     rope_pairing, y);
+                                                     rope_pairing, y, out_f16);
   return cudaGetLastError();
 }
 

@@ -85,7 +85,8 @@ def load_library(path: str = LIB_PATH):
         "va_block_attention_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_op_attention_device": ([_vp, _vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float,
                                     _vp, c_float, _vp, _vp], c_int),
-        "va_flash_attention_bf16": ([_vp, _vp, _vp, _vp, i64, i64, i64, c_int, i64, _vp, _vp], c_int),
+        "va_flash_attention_bf16": ([_vp, _vp, _vp, _vp, i64, i64, i64, c_int, i64, c_int, c_int, _vp, _vp],
+                                    c_int),
         "va_comm_unique_id": ([_vp], c_int),
         "va_comm_init": ([_vp, _vp, c_int, c_int], c_int),
         "va_attention_device_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
@@ -230,10 +231,13 @@ class Context:
                                              _ptr(out)))
         return out
 
-    def flash_bf16(self, q, k, v, heads, out, seg_len=0, q_offset=0, stream=0):
-        """q [q_count, heads*64], k/v [kv_rows, heads*64] bf16 token-major; seg_len 0 = global."""
+    def flash_bf16(self, q, k, v, heads, out, seg_len=0, q_offset=0, stream=0, poly_per8=-1):
+        """q [q_count, heads*64], k [kv_rows, heads*64] bf16 token-major; v bf16 (production)
+        or f16 (torch dtype decides); seg_len 0 = global; poly_per8 < 0 = library default."""
+        v_f16 = int(str(getattr(v, "dtype", "")) == "torch.float16")
         self.check(self.lib.va_flash_attention_bf16(self.h, _ptr(q), _ptr(k), _ptr(v), q.shape[0], q_offset,
-                                                    k.shape[0], heads, seg_len, _ptr(out), stream))
+                                                    k.shape[0], heads, seg_len, v_f16, poly_per8, _ptr(out),
+                                                    stream))
 
     def comm_init(self, comm_id: bytes, nranks: int, rank: int):
         buf = ctypes.create_string_buffer(bytes(comm_id), 128)
