@@ -334,14 +334,14 @@ def run_ours(args):
 
     def time_flash(v_tensor, poly=-1):
         for _ in range(3):
-            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, poly_per8=poly)
+            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, variant=poly)
         evs = []
         barrier()
         for _ in range(args.steps):
             flush_buf.zero_()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, poly_per8=poly)
+            ctx.flash_bf16(q, kw, v_tensor, wl.heads, o, q_offset=row0, stream=sp, variant=poly)
             b.record(stream)
             evs.append((a, b))
         barrier()
@@ -353,7 +353,7 @@ def run_ours(args):
     variants = {}
     if args.variants:
         to_tf = lambda ms: round(flash_flops / (ms * 1e-3) / 1e12, 2)  # noqa: E731
-        for form in (2, 3, 5):
+        for form in (0, 2, 3, 5):
             for p in range(3):
                 name = {3: f"w20_poly{p}", 5: f"w20ord_poly{p}"}.get(form, f"form{form}_poly{p}")
                 variants[name] = to_tf(time_flash(vw, p + 8 * form))

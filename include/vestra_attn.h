@@ -159,14 +159,17 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
 /* Kernel-level entry points (each one launch; used by the parity tests). */
 /* K2 alone: q bf16 [q_count, heads*64] token-major, k bf16 and v [kv_rows, heads*64];
  * v is bf16 (the production path) or, with v_f16 != 0, f16 (P is then formed in
- * f16).  poly_per8 (bf16 path) = how many of every 8 exponential pairs run on the
- * FMA pipe instead of MUFU, 0..4, or < 0 for the library default.  Query i is row
+ * f16).  variant (bf16 path) = poly + 8 * form, or < 0 for the library default
+ * (24): poly 0..2 = how many of every 8 exponential pairs run on the FMA pipe
+ * instead of MUFU; form 0, 1, 2, 4 = one softmax row per thread (instruction
+ * formulations), form 3 = four threads per row (20 warps), form 5 = form 3 with
+ * the two query tiles taking turns in the exponential section.  Query i is row
  * q_offset + i of the key window.  seg_len = 0: every query attends to all kv_rows
  * keys; seg_len > 0: independent segments of seg_len tokens (q_offset and q_count
  * multiples of seg_len).  out bf16 [q_count, heads*64]. */
 int va_flash_attention_bf16(va_ctx* ctx, const void* q, const void* k, const void* v,
                             int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
-                            int64_t seg_len, int v_f16, int poly_per8, void* out,
+                            int64_t seg_len, int v_f16, int variant, void* out,
                             void* stream);
 /* K3-style GEMM: out[M,N] = (a[M,K] * w_t[N,K]^T + bias) * scale (+ residual), bf16
  * in, F32 out; bias/scale/residual may be NULL.  N % 128 == 0, K % 64 == 0. */

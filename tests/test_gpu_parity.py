@@ -104,7 +104,7 @@ def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, se
     rng = np.random.default_rng(heads * 7 + seg)
     q, k, v = (bf16_round(rng.standard_normal((heads, rows, 64)).astype(np.float32)) for _ in range(3))
     out = torch.zeros(rows, heads * 64, dtype=torch.bfloat16, device="cuda")
-    ctx.flash_bf16(_tok(q), _tok(k), _tok(v), heads, out, seg_len=seg if segs > 1 else 0, poly_per8=variant)
+    ctx.flash_bf16(_tok(q), _tok(k), _tok(v), heads, out, seg_len=seg if segs > 1 else 0, variant=variant)
     torch.cuda.synchronize()
     ctx.check_device()
     got = out.float().cpu().numpy().reshape(rows, heads, 64).transpose(1, 0, 2)

@@ -648,7 +648,7 @@ int va_op_attention_device(va_ctx* c, const float* q, const float* k, const floa
 
 int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void* v,
                             int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
-                            int64_t seg_len, int v_f16, int poly_per8, void* out,
+                            int64_t seg_len, int v_f16, int variant, void* out,
                             void* stream) {
   if (!c || !q || !k || !v || !out) return VA_ERR_INVALID;
   if (q_count <= 0 || kv_rows <= 0 || heads <= 0 || seg_len < 0 || q_offset < 0 ||
@@ -667,10 +667,10 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   fa.o_tok = static_cast<__nv_bfloat16*>(out);
   fa.embed = heads * 64;
   fa.v_f16 = v_f16 ? 1 : 0;
-  if (poly_per8 >= 0) {
-    if ((poly_per8 & 7) > 2 || (poly_per8 >> 3) > 5)
-      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..3)");
-    fa.poly_per8 = poly_per8;
+  if (variant >= 0) {
+    if ((variant & 7) > 2 || (variant >> 3) > 5)
+      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..5)");
+    fa.poly_per8 = variant;
   }
   VA_CUDA(c, va::launch_flash(static_cast<const __nv_bfloat16*>(q),
                               static_cast<const __nv_bfloat16*>(k),

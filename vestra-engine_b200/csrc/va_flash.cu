@@ -12,9 +12,10 @@
 //
 // CTA = one (segment, head, pair of 128-query tiles).
 //   warp 0   TMA producer: Q0/Q1 once, then K_j/V_j into a STAGES-deep ring
-//   warp 1   TMEM owner + single-thread UMMA issuer
+//   warp 1   TMEM owner + UMMA issuer of query tile 0 (one thread)
+//   warp 2   UMMA issuer of query tile 1 (one thread); warp 3 idle
 //   softmax warps (two layouts, selected at launch):
-//     "rows"  10 warps: warps 2..5 / 6..9 own query tile 0 / 1, one row per thread
+//     "rows"  12 warps: warps 4..7 / 8..11 own query tile 0 / 1, one row per thread
 //     "w20"   20 warps: warps 4..11 / 12..19 own tile 0 / 1; two warps share a TMEM
 //             lane quadrant (16 lanes each, 16x256b loads, 4 threads per row), so
 //             every SM sub-partition keeps 4 softmax warps in flight; setmaxnreg
@@ -27,10 +28,11 @@
 //
 // Pipeline per query tile t and KV tile j:
 //   softmax_t loads S_t(j) into registers and releases it at once (s_free), so
-//   the UMMA warp issues QK_t(j+1) while the exponentials of tile j run; it then
+//   issuer_t issues QK_t(j+1) while the exponentials of tile j run; it then
 //   waits for PV_t(j-1) (pv_done) before writing P_t(j) and, when the running
 //   max grew by more than 2^8, rescaling O_t in TMEM; p_full hands P_t(j) to PV_t(j).
-// The two query tiles ping-pong on the tensor core.
+// The two query tiles ping-pong on the tensor core.  A K/V stage is released when
+// both issuers have committed the UMMAs that read it.
 #include <math.h>
 
 #include "va_internal.h"
@@ -45,7 +47,7 @@ constexpr int kTileQ = 128;
 constexpr int kTileK = 128;
 constexpr int kHeadDim = 64;
 constexpr int kStages = 4;
-constexpr int kRowsThreads = 320;  // "rows" layout
+constexpr int kRowsThreads = 384;  // "rows" layout
 constexpr int kW20Threads = 640;   // "w20" layout
 // setmaxnreg split of the w20 layout: warpgroup 0 (producer, UMMA, 2 idle warps)
 // drops to kW20LowRegs, the four softmax warpgroups rise to kW20HighRegs.  The
@@ -132,7 +134,9 @@ struct Ctl {
   __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 4); }
   __device__ volatile int* kv_issued() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 8); }
   __device__ volatile int* kv_consumed() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 12); }
-  __device__ volatile int* mma_done() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 16); }
+  __device__ volatile int* mma_done(int t) const {
+    return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 16 + 4 * t);
+  }
   __device__ uint32_t sQ(int t) const { return base + FlashSmem::kQ + t * kTileBytes; }
   __device__ uint32_t sK(int s) const { return base + FlashSmem::kK + s * kTileBytes; }
   __device__ uint32_t sV(int s) const { return base + FlashSmem::kV + s * kTileBytes; }
@@ -148,8 +152,9 @@ __device__ __forceinline__ Ctl make_ctl() {
 }
 
 // Barrier init (thread 0) and TMEM allocation (warp 1); every thread returns the
-// TMEM base after the CTA-wide barrier.  softmax_threads = arrivals per tile.
-__device__ __forceinline__ uint32_t cta_setup(const Ctl& c, int softmax_threads,
+// TMEM base after the CTA-wide barrier.  softmax_threads = arrivals per tile;
+// each of the g.nq UMMA issuers releases every K/V stage once.
+__device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int softmax_threads,
                                               const CUtensorMap* mq, const CUtensorMap* mk,
                                               const CUtensorMap* mv) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -157,7 +162,7 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, int softmax_threads,
     mbar_init(c.q_full(), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(c.kv_full(s), 1);
-      mbar_init(c.kv_empty(s), 1);
+      mbar_init(c.kv_empty(s), g.nq);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(c.s_full(t), 1);
@@ -170,7 +175,8 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, int softmax_threads,
     *c.abort_flag() = 0;
     *c.kv_issued() = 0;
     *c.kv_consumed() = 0;
-    *c.mma_done() = 0;
+    *c.mma_done(0) = 0;
+    *c.mma_done(1) = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -207,73 +213,57 @@ __device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const 
   }
 }
 
-// Single-thread UMMA issuer.
+// UMMA issuer of query tile t (one thread; tile 0 and tile 1 have their own warps,
+// on different SM sub-partitions).  Each issuer drives one chain:
+//   QK_t(0), QK_t(1), then per KV step j: PV_t(j), QK_t(j+2).
+// The shared-memory descriptors are built once; every step only adds constants,
+// and each group of 4 (QK) or 8 (PV) UMMAs is issued from one asm block, so the
+// issuing thread spends few instructions per UMMA while the softmax warps of its
+// sub-partition compete for issue slots.
 template <bool kF16>
-__device__ __forceinline__ void run_mma(const Ctl& c, const Geom& g, uint32_t tmem, int* err) {
+__device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32_t tmem, int t,
+                                             int* err) {
   constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
   constexpr uint32_t idesc_pv = kF16 ? idesc_f16_f32(kTileQ, kHeadDim, false, true)
                                      : idesc_bf16_f32(kTileQ, kHeadDim, false, true);
+  constexpr uint64_t kStageStep = kTileBytes >> 4;  // descriptor start-field step per stage
   volatile int* abort_flag = c.abort_flag();
-  auto issue_qk = [&](int t, int s) {
-#pragma unroll
-    for (int k = 0; k < kHeadDim / 16; ++k) {
-      const uint64_t ad = sdesc_sw128(c.sQ(t) + k * 32, 16, 1024);
-      const uint64_t bd = sdesc_sw128(c.sK(s) + k * 32, 16, 1024);
-      umma_ss(tmem + col_s(t), ad, bd, idesc_qk, k != 0 ? 1u : 0u);
-    }
-  };
-  auto issue_pv = [&](int t, int s, bool acc) {
-#pragma unroll
-    for (int k = 0; k < kTileK / 16; ++k) {
-      // B = V tile, MN-major: 16 keys per step = 16 rows of 128 B.
-      const uint64_t bd = sdesc_sw128(c.sV(s) + k * 16 * 128, 8192, 1024);
-      umma_ts(tmem + col_o(t), tmem + col_p(t) + k * 8, bd, idesc_pv, (acc || k != 0) ? 1u : 0u);
-    }
-  };
-  // QK_t(jj) for jj >= 1 needs K(jj) (waited for once, by t == 0) and S_t free,
-  // i.e. softmax_t holding S_t(jj-1) in registers.
-  auto next_qk = [&](int t, int jj) {
-    bool r = true;
-    if (t == 0) {
-      r = mbar_wait(c.kv_full(jj % kStages), (jj / kStages) & 1, abort_flag, err, kDevTimeoutMma);
-      if (r) *c.kv_consumed() = jj + 1;
-    }
-    if (r) r = mbar_wait(c.s_free(t), (jj - 1) & 1, abort_flag, err, kDevTimeoutMma);
+  const uint64_t dq = sdesc_sw128(c.sQ(t), 16, 1024);
+  const uint64_t dk0 = sdesc_sw128(c.sK(0), 16, 1024);
+  // B = V tile, MN-major: 16 keys per K step = 16 rows of 128 B.
+  const uint64_t dv0 = sdesc_sw128(c.sV(0), 8192, 1024);
+  const uint32_t tS = tmem + col_s(t), tP = tmem + col_p(t), tO = tmem + col_o(t);
+  // QK_t(jj) needs K(jj) and, for jj >= 1, S_t free (softmax_t holds S_t(jj-1) in
+  // registers).
+  auto qk = [&](int jj) {
+    bool r = mbar_wait(c.kv_full(jj % kStages), (jj / kStages) & 1, abort_flag, err, kDevTimeoutMma);
+    if (r && t == 0) *c.kv_consumed() = jj + 1;
+    if (r && jj > 0) r = mbar_wait(c.s_free(t), (jj - 1) & 1, abort_flag, err, kDevTimeoutMma);
     if (r) {
       tc_fence_after();
-      issue_qk(t, jj % kStages);
+      umma_ss_k64(tS, dq, dk0 + (jj % kStages) * kStageStep, idesc_qk, 0u);
       tc_commit(c.s_full(t));
     }
     return r;
   };
   bool ok = mbar_wait(c.q_full(), 0, abort_flag, err, kDevTimeoutMma);
-  if (ok) ok = mbar_wait(c.kv_full(0), 0, abort_flag, err, kDevTimeoutMma);
-  if (ok) {
-    *c.kv_consumed() = 1;
-    tc_fence_after();
-    for (int t = 0; t < g.nq; ++t) {
-      issue_qk(t, 0);
-      tc_commit(c.s_full(t));
-    }
-  }
-  for (int t = 0; ok && t < g.nq && g.num_kv > 1; ++t) ok = next_qk(t, 1);
-  // Issue order follows the order the softmax warpgroups finish in: PV_0(j),
-  // QK_0(j+2), PV_1(j), QK_1(j+2); the S tile of step j+2 is ready a whole step
-  // before its warpgroup needs it.
+  if (ok) ok = qk(0);
+  if (ok && g.num_kv > 1) ok = qk(1);
   for (int j = 0; ok && j < g.num_kv; ++j) {
     const int s = j % kStages;
-    for (int t = 0; t < g.nq && ok; ++t) {
-      ok = mbar_wait(c.p_full(t), j & 1, abort_flag, err, kDevTimeoutMma);
-      if (!ok) break;
-      tc_fence_after();
-      issue_pv(t, s, j > 0);
-      tc_commit(c.pv_done(t));
-      if (j + 2 < g.num_kv) ok = next_qk(t, j + 2);
-    }
-    tc_commit(c.kv_empty(s));
+    ok = mbar_wait(c.p_full(t), j & 1, abort_flag, err, kDevTimeoutMma);
+    if (!ok) break;
+    tc_fence_after();
+    umma_ts_k128_mn(tO, tP, dv0 + s * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
+    tc_commit(c.pv_done(t));
+    tc_commit(c.kv_empty(s));  // K(j) and V(j) read by this tile's UMMAs
+    if (j + 2 < g.num_kv) ok = qk(j + 2);
   }
-  for (int t = 0; t < 2; ++t) tc_commit(c.o_final(t));
-  *c.mma_done() = 1;
+  // Always committed, also after an abort: o_final(t) then marks the moment every
+  // UMMA of this issuer has finished, which the teardown waits for before it frees
+  // TMEM.
+  tc_commit(c.o_final(t));
+  *c.mma_done(t) = 1;
 }
 
 // Drains in-flight copies/UMMAs after an abort, then frees TMEM (warp 1).
@@ -283,7 +273,8 @@ __device__ __forceinline__ void cta_teardown(const Ctl& c, uint32_t tmem) {
   if (threadIdx.x == 0 && *c.abort_flag()) {
     if (*c.kv_consumed() == 0) drain(c.q_full(), 0);
     for (int j = *c.kv_consumed(); j < *c.kv_issued(); ++j) drain(c.kv_full(j % kStages), (j / kStages) & 1);
-    if (*c.mma_done()) drain(c.o_final(0), 0);
+    for (int t = 0; t < 2; ++t)
+      if (*c.mma_done(t)) drain(c.o_final(t), 0);
   }
   __syncthreads();
   if ((threadIdx.x >> 5) == 1) {
@@ -387,15 +378,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   const Geom g = make_geom(fa);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t tmem = cta_setup(c, 128, &map_q, &map_k, &map_v);
+  const uint32_t tmem = cta_setup(c, g, 128, &map_q, &map_k, &map_v);
   volatile int* abort_flag = c.abort_flag();
 
   if (warp == 0) {
     if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
-  } else if (warp == 1) {
-    if (lane == 0) run_mma<kF16>(c, g, tmem, err);
-  } else {
-    const int t = (warp - 2) >> 2;              // query tile of this warpgroup
+  } else if (warp < 3) {
+    if (lane == 0 && warp - 1 < g.nq) run_mma_tile<kF16>(c, g, tmem, warp - 1, err);
+  } else if (warp >= 4) {
+    const int t = (warp - 4) >> 2;              // query tile of this warpgroup
     const int quad = warp & 3;                  // TMEM lane quadrant
     const int r = quad * 32 + lane;             // row inside the query tile
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
@@ -528,15 +519,15 @@ __global__ void __launch_bounds__(kW20Threads, 1)
   const Geom g = make_geom(fa);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t tmem = cta_setup(c, 256, &map_q, &map_k, &map_v);
+  const uint32_t tmem = cta_setup(c, g, 256, &map_q, &map_k, &map_v);
   volatile int* abort_flag = c.abort_flag();
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kW20LowRegs));
     if (warp == 0) {
       if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
-    } else if (warp == 1) {
-      if (lane == 0) run_mma<false>(c, g, tmem, err);
+    } else if (warp < 3) {
+      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false>(c, g, tmem, warp - 1, err);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));

@@ -38,7 +38,9 @@ struct ProjEpilogueArgs {
 };
 
 // ---- fused flash attention (K2) ----
-constexpr int kDefaultPolyPer8 = 1;
+// Default softmax variant (poly + 8 * form): form 3 (four threads per row, 20
+// warps), every exponential on MUFU.
+constexpr int kDefaultPolyPer8 = 24;
 // Q is [q_count][E] token-major (this rank's queries, the first of which is row
 // q_offset of the key window); K and V are [kv_rows][E] token-major.
 // seg_len == 0: global attention, every query sees all kv_rows keys.
@@ -56,7 +58,7 @@ struct FlashArgs {
   float* o_hnd;
   int embed;
   int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
-  int poly_per8 = kDefaultPolyPer8;  // bf16 path: exponential pairs of every 8 done on the FMA pipe (0..4)
+  int poly_per8 = kDefaultPolyPer8;  // bf16 path: variant = poly + 8 * form (see launch_flash)
 };
 
 // Tensor-map encoding through the driver entry point (no -lcuda needed).

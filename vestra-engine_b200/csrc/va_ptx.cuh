@@ -168,6 +168,62 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// Four SS UMMAs stepping K by 16 elements (32 B) in both K-major SW128 operands:
+// D (+)= A[:, 0:64] * B[:, 0:64].  Only the descriptors' 14-bit start field moves
+// (by 2 per step, in 16-byte units), and shared memory stays below 256 KB, so a
+// 32-bit add on the low word is exact.  `accumulate` applies to the first step;
+// the other three always accumulate.
+__device__ __forceinline__ void umma_ss_k64(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b32 alo, ahi, blo, bhi, t0, t1;\n\t.reg .b64 a, b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "mov.b64 {alo, ahi}, %1;\n\t"
+      "mov.b64 {blo, bhi}, %2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "add.u32 t0, alo, 2;\n\tadd.u32 t1, blo, 2;\n\t"
+      "mov.b64 a, {t0, ahi};\n\tmov.b64 b, {t1, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, q;\n\t"
+      "add.u32 t0, alo, 4;\n\tadd.u32 t1, blo, 4;\n\t"
+      "mov.b64 a, {t0, ahi};\n\tmov.b64 b, {t1, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, q;\n\t"
+      "add.u32 t0, alo, 6;\n\tadd.u32 t1, blo, 6;\n\t"
+      "mov.b64 a, {t0, ahi};\n\tmov.b64 b, {t1, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, q;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Eight TS UMMAs stepping K by 16: A from TMEM (8 columns of packed pairs per step),
+// B an MN-major SW128 operand whose 16-row K step is 2048 B (128 in the start
+// field).  `accumulate` applies to the first step; the others always accumulate.
+__device__ __forceinline__ void umma_ts_k128_mn(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b32 blo, bhi, ta, tb;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "mov.b64 {blo, bhi}, %2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.u32 ta, %1, 8;\n\tadd.u32 tb, blo, 128;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 16;\n\tadd.u32 tb, blo, 256;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 24;\n\tadd.u32 tb, blo, 384;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 32;\n\tadd.u32 tb, blo, 512;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 40;\n\tadd.u32 tb, blo, 640;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 48;\n\tadd.u32 tb, blo, 768;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 56;\n\tadd.u32 tb, blo, 896;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B and f32 D.
 //   [4,6) D fmt (1 = f32)  [7,10) A fmt (1 = bf16)  [10,13) B fmt (1 = bf16)
 //   [15] A MN-major  [16] B MN-major  [17,23) N>>3  [24,29) M>>4

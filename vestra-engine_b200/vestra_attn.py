@@ -231,12 +231,13 @@ class Context:
                                              _ptr(out)))
         return out
 
-    def flash_bf16(self, q, k, v, heads, out, seg_len=0, q_offset=0, stream=0, poly_per8=-1):
+    def flash_bf16(self, q, k, v, heads, out, seg_len=0, q_offset=0, stream=0, variant=-1):
         """q [q_count, heads*64], k [kv_rows, heads*64] bf16 token-major; v bf16 (production)
-        or f16 (torch dtype decides); seg_len 0 = global; poly_per8 < 0 = library default."""
+        or f16 (torch dtype decides); seg_len 0 = global; variant = poly + 8 * form of the
+        softmax (< 0 = library default)."""
         v_f16 = int(str(getattr(v, "dtype", "")) == "torch.float16")
         self.check(self.lib.va_flash_attention_bf16(self.h, _ptr(q), _ptr(k), _ptr(v), q.shape[0], q_offset,
-                                                    k.shape[0], heads, seg_len, v_f16, poly_per8, _ptr(out),
+                                                    k.shape[0], heads, seg_len, v_f16, variant, _ptr(out),
                                                     stream))
 
     def comm_init(self, comm_id: bytes, nranks: int, rank: int):
