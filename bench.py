@@ -35,9 +35,10 @@ import synthetic as syn  # noqa: E402
 
 LAYER = 5           # a global block of the DA3-BASE schedule (alt_start 4: globals 5,7,9,11)
 L2_FLUSH_BYTES = 256 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one flash launch, from the ncu
-# capture summarised in profiles/flash_fwd_d64_cfg3.md (None until captured).
-FLASH_DRAM_BYTES_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one flash launch on cfg3 (47.92 MB
+# + 0.74 MB), from the ncu capture summarised in profiles/flash_fwd_d64_cfg3.md;
+# used for the roofline's `traffic` when the bench runs that workload.
+FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 48.66e6}
 
 
 def parse_args():
@@ -410,12 +411,12 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, QK-norm gamma 1 beta 0)",
             "config": workload_config(wl, world),
-            "roofline": {"bound": "tensor", "kernel": "flash_fwd_d64_kernel", "achieved": round(achieved, 2),
+            "roofline": {"bound": "tensor", "kernel": "flash_fwd_d64_w20_kernel", "achieved": round(achieved, 2),
                          "peak": peak_tflops, "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
                          "peak_kind": f"bf16 burst ({peak_kind})", "flops_per_launch": flash_flops,
                          "ms_per_launch": round(flash_ms, 4),
                          **({"variants_tflops": variants} if variants else {}),
-                         "traffic": FLASH_DRAM_BYTES_PER_LAUNCH},
+                         "traffic": FLASH_DRAM_BYTES_PER_LAUNCH.get(args.workload) if world == 1 else None},
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
                     "h2d_bytes_per_step": int(wl.rows * wl.embed * 4), "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
