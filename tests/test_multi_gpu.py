@@ -1,0 +1,101 @@
+"""Query-sharded global attention on N GPUs (va_attention_device_sharded).
+
+One child process per GPU; rank 0 creates the NCCL unique id and hands it to the
+others through a multiprocessing queue, every rank then projects K'/V for its own
+equal token slice, all-gathers them in place and attends its queries to the whole
+window.  The concatenated rank outputs must equal the single-GPU sub-block
+(same kernels, same per-row arithmetic) and meet the oracle gates on a row sample.
+Skipped when fewer GPUs than ranks are visible.
+"""
+import multiprocessing as mp
+import queue
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+import synthetic as syn  # noqa: E402
+import vestra_attn as va  # noqa: E402
+
+LAYER = 5
+WORKLOAD = "cfg3_s12_global"
+TIMEOUT_S = 240
+
+
+def _config(wl):
+    return va.default_config(embed_dim=wl.embed, num_heads=wl.heads, num_register=wl.n_special - 1,
+                             max_rows=wl.rows, depth=12, rope_start=4, qknorm_start=4)
+
+
+def _rank_main(rank, nranks, ids, results):
+    try:
+        torch.cuda.set_device(rank)
+        wl = syn.CONFIGS[WORKLOAD]
+        row0, local = va.shard_rows(wl.rows, nranks, rank)
+        ctx = va.Context(_config(wl), rank)
+        ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=3, layer=LAYER, bias=True, perturb_norm=True))
+        if rank == 0:
+            uid = va.comm_unique_id()
+            for _ in range(nranks - 1):
+                ids.put(uid)
+        else:
+            uid = ids.get(timeout=TIMEOUT_S / 2)
+        ctx.comm_init(uid, nranks, rank)
+        x = syn.hidden_states(wl.rows, wl.embed, seed=3)[row0:row0 + local]
+        ln1 = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        out = torch.empty_like(ln1)
+        for _ in range(2):  # the second call reuses the communicator and workspace
+            ctx.attention_device_sharded(LAYER, ln1, out, wl.gh, wl.gw, wl.views, True, stream=0)
+        torch.cuda.synchronize()
+        ctx.check_device()
+        results.put((rank, "ok", out.cpu().numpy()))
+        ctx.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        results.put((rank, f"error: {e!r}", None))
+
+
+@pytest.mark.parametrize("nranks", [2, 4, 8])
+def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks):
+    if torch.cuda.device_count() < nranks:
+        pytest.skip(f"needs {nranks} GPUs")
+    wl = syn.CONFIGS[WORKLOAD]
+    mpc = mp.get_context("spawn")
+    ids, results = mpc.Queue(), mpc.Queue()
+    procs = [mpc.Process(target=_rank_main, args=(r, nranks, ids, results)) for r in range(nranks)]
+    for p in procs:
+        p.start()
+    outs = {}
+    try:
+        for _ in range(nranks):
+            rank, status, arr = results.get(timeout=TIMEOUT_S)
+            assert status == "ok", f"rank {rank}: {status}"
+            outs[rank] = arr
+    except queue.Empty:
+        pytest.fail("a rank did not report within the time limit")
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    sharded = np.concatenate([outs[r] for r in range(nranks)], axis=0)
+
+    # Single GPU, same inputs and weights.
+    ctx = va.Context(_config(wl), 0)
+    p = syn.layer_weights(wl.embed, seed=3, layer=LAYER, bias=True, perturb_norm=True)
+    ctx.load_layer(LAYER, p)
+    x = syn.hidden_states(wl.rows, wl.embed, seed=3)
+    single = ctx.attention_host(LAYER, x, wl.gh, wl.gw, wl.views, True)
+    ctx.close()
+    assert np.array_equal(sharded, single), float(np.abs(sharded - single).max())
+
+    rows = np.sort(np.random.default_rng(nranks).choice(wl.rows, 96, replace=False)).astype(np.int64)
+    pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, True)
+    ref = oracle_mod.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=0, q_rows=rows)
+    got = sharded[rows]
+    err = float(np.abs(got - ref).max())
+    a, b = got.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
+    cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+    assert err <= 2e-2 and cos >= 0.9999, (err, cos)
