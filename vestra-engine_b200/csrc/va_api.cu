@@ -39,6 +39,8 @@ struct LayerWeights {
   float* kn_b = nullptr;
 };
 
+constexpr int kMaxHostChunks = 32;
+
 struct PosKey {
   int64_t rows = -1;
   int gh = 0, gw = 0, views = 0, global = 0, n_special = 0;
@@ -68,6 +70,11 @@ struct va_ctx {
   int rope_npos = 0;
   int* err = nullptr;          // device error word
   cudaStream_t stream = nullptr;
+  // host path (va_attention_host): copy streams and per-chunk events
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_in[kMaxHostChunks] = {};
+  cudaEvent_t ev_out[kMaxHostChunks] = {};
+  int sms = 148;
   // Op::Attention scratch (grown on demand)
   __nv_bfloat16* op_buf = nullptr;  // q|k|v bf16 [3][H*n*64]
   size_t op_cap = 0;
@@ -265,21 +272,28 @@ int segments_for(va_ctx* c, int64_t rows, int view_count, int global, int* seg_l
   return VA_OK;
 }
 
-// The device launch sequence of one attention sub-block (see the file header).
-int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
+int validate_branch(va_ctx* c, int layer, const BranchSpec& b) {
   const LayerWeights& w = c->layers[layer];
-  const int E = c->cfg.embed_dim;
-  const int64_t rows = b.rows;
-  if (rows <= 0 || b.window_rows > c->cap || b.row_offset + rows > b.window_rows)
+  if (b.rows <= 0 || b.window_rows > c->cap || b.row_offset + b.rows > b.window_rows)
     return fail(c, VA_ERR_INVALID, "rows exceed the context's max_rows");
   if (b.window_rows > 0x7fffffff / 64) return fail(c, VA_ERR_INVALID, "rows too large");
   if (b.apply_ln1 && !w.norm1_w) return fail(c, VA_ERR_STATE, "norm1 weights not loaded");
-  if (b.seg_len > 0 && (rows % b.seg_len != 0 || b.row_offset % b.seg_len != 0))
+  if (b.seg_len > 0 && (b.rows % b.seg_len != 0 || b.row_offset % b.seg_len != 0))
     return fail(c, VA_ERR_INVALID, "a rank's rows must hold whole views in local blocks");
-  VA_CUDA(c, va::launch_ln_cast(b.in, b.apply_ln1 ? w.norm1_w : nullptr, w.norm1_b,
-                                c->cfg.ln_eps, static_cast<int>(rows), E, c->x, st));
-  __nv_bfloat16* k_slice = c->k + b.row_offset * E;
-  __nv_bfloat16* v_slice = c->v + b.row_offset * E;
+  if (b.seg_len == 0 && !b.gather && b.rows != b.window_rows)
+    return fail(c, VA_ERR_INVALID, "global attention over a sharded window needs the communicator");
+  return VA_OK;
+}
+
+// Projection stage for rows [r0, r1) of this rank's slice: LN1 / bf16 cast, then
+// the QKV GEMM with its bias + QK-norm + RoPE epilogue; Q' goes to c->q, K' and V
+// to the rank's rows of the key window.
+int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1, cudaStream_t st) {
+  const LayerWeights& w = c->layers[layer];
+  const int E = c->cfg.embed_dim;
+  const int n = static_cast<int>(r1 - r0);
+  VA_CUDA(c, va::launch_ln_cast(b.in + r0 * E, b.apply_ln1 ? w.norm1_w : nullptr, w.norm1_b,
+                                c->cfg.ln_eps, n, E, c->x + r0 * E, st));
   va::QkvEpilogueArgs qa{};
   qa.bias = w.qkv_b;
   const bool qk = layer_use_qknorm(c, layer);
@@ -288,56 +302,71 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
   qa.k_g = qk ? w.kn_g : nullptr;
   qa.k_b = qk ? w.kn_b : nullptr;
   qa.qk_eps = c->cfg.qk_norm_eps;
-  qa.pos = b.pos ? b.pos + b.row_offset : nullptr;
+  qa.pos = b.pos ? b.pos + b.row_offset + r0 : nullptr;
   qa.rope_cs = c->rope_cs;
   qa.rope_pairing = c->cfg.rope_pairing;
-  qa.q_out = c->q;
-  qa.k_out = k_slice;
-  qa.v_out = v_slice;
-  qa.rows = static_cast<int>(rows);
+  qa.q_out = c->q + r0 * E;
+  qa.k_out = c->k + (b.row_offset + r0) * E;
+  qa.v_out = c->v + (b.row_offset + r0) * E;
+  qa.rows = n;
   qa.embed = E;
   // V (and so P) stay bf16: measured faster on B200 than an f16 P formed with
   // packed ex2.f16x2 (584 vs 511 TFLOP/s for the S=12 window).
   qa.v_f16 = 0;
-  VA_CUDA(c, va::launch_qkv_gemm(c->x, w.w_qkv_t, static_cast<int>(rows), E, qa, c->err, st));
+  VA_CUDA(c, va::launch_qkv_gemm(c->x + r0 * E, w.w_qkv_t, n, E, qa, c->err, st));
+  return VA_OK;
+}
+
+// Attention stage for this rank's queries [q0, q1): fused flash attention against
+// the key window (global) or the queries' own views (local; the range then holds
+// whole views), then the output projection with its bias/ls1/residual epilogue.
+int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1, cudaStream_t st) {
+  const LayerWeights& w = c->layers[layer];
+  const int E = c->cfg.embed_dim;
+  const int n = static_cast<int>(q1 - q0);
   va::FlashArgs fa{};
-  fa.q_count = static_cast<int>(rows);
+  fa.q_count = n;
   fa.seg_len = b.seg_len;
   fa.heads = c->cfg.num_heads;
   fa.scale_log2 = static_cast<float>(1.0 / std::sqrt(64.0) * 1.4426950408889634);
   fa.out_mode = 0;
-  fa.o_tok = c->o;
+  fa.o_tok = c->o + q0 * E;
   fa.embed = E;
   fa.v_f16 = 0;
   const __nv_bfloat16* kk = c->k;
   const __nv_bfloat16* vv = c->v;
-  if (b.gather) {
-    int rc = gather_kv(c, k_slice, v_slice, rows, st);
-    if (rc) return rc;
-    fa.q_offset = static_cast<int>(b.row_offset);
-    fa.kv_rows = static_cast<int>(b.window_rows);
-  } else if (b.seg_len > 0) {
-    // Local blocks: every key a query needs lives in this rank's own slice.
-    kk = k_slice;
-    vv = v_slice;
+  if (b.seg_len > 0) {
+    // Local blocks: every key a query needs lives in its own view.
+    kk = c->k + (b.row_offset + q0) * E;
+    vv = c->v + (b.row_offset + q0) * E;
     fa.q_offset = 0;
-    fa.kv_rows = static_cast<int>(rows);
+    fa.kv_rows = n;
   } else {
-    if (rows != b.window_rows)
-      return fail(c, VA_ERR_INVALID, "global attention over a sharded window needs the communicator");
-    fa.q_offset = 0;
-    fa.kv_rows = static_cast<int>(rows);
+    fa.q_offset = static_cast<int>(b.row_offset + q0);
+    fa.kv_rows = static_cast<int>(b.window_rows);
   }
-  VA_CUDA(c, va::launch_flash(c->q, kk, vv, fa, c->err, st));
+  VA_CUDA(c, va::launch_flash(c->q + q0 * E, kk, vv, fa, c->err, st));
   va::ProjEpilogueArgs pa{};
   pa.bias = w.proj_b;
   pa.ls1 = w.ls1;
-  pa.residual = b.residual;
-  pa.out = b.out;
-  pa.rows = static_cast<int>(rows);
+  pa.residual = b.residual ? b.residual + q0 * E : nullptr;
+  pa.out = b.out + q0 * E;
+  pa.rows = n;
   pa.embed = E;
-  VA_CUDA(c, va::launch_proj_gemm(c->o, w.w_proj_t, static_cast<int>(rows), E, E, pa, c->err, st));
+  VA_CUDA(c, va::launch_proj_gemm(c->o + q0 * E, w.w_proj_t, n, E, E, pa, c->err, st));
   return VA_OK;
+}
+
+// The device launch sequence of one attention sub-block (see the file header).
+int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
+  int rc = validate_branch(c, layer, b);
+  if (rc) return rc;
+  if ((rc = stage_qkv(c, layer, b, 0, b.rows, st))) return rc;
+  if (b.gather) {
+    const int E = c->cfg.embed_dim;
+    if ((rc = gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st))) return rc;
+  }
+  return stage_attn(c, layer, b, 0, b.rows, st);
 }
 
 int read_device_error(va_ctx* c) {
@@ -407,6 +436,14 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   if ((e = dmalloc(&c->err, 1)) != cudaSuccess) return bail(e);
   if ((e = cudaMemset(c->err, 0, sizeof(int))) != cudaSuccess) return bail(e);
   if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
+  if ((e = cudaStreamCreateWithFlags(&c->h2d, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
+  if ((e = cudaStreamCreateWithFlags(&c->d2h, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
+  for (int i = 0; i < kMaxHostChunks; ++i) {
+    if ((e = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
+    if ((e = cudaEventCreateWithFlags(&c->ev_out[i], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
+  }
+  if ((e = cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+    return bail(e);
   if (ensure_rope_table(c, 128) != VA_OK) return bail(cudaErrorMemoryAllocation);
   *out = c;
   return VA_OK;
@@ -416,6 +453,8 @@ void va_destroy(va_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->h2d) cudaStreamSynchronize(c->h2d);
+  if (c->d2h) cudaStreamSynchronize(c->d2h);
   for (auto& l : c->layers) free_layer(l);
   dfree(c->x);
   dfree(c->q);
@@ -431,6 +470,12 @@ void va_destroy(va_ctx* c) {
   dfree(c->op_pos);
   if (c->comm) va::comm_destroy(c->comm, false);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->h2d) cudaStreamDestroy(c->h2d);
+  if (c->d2h) cudaStreamDestroy(c->d2h);
+  for (int i = 0; i < kMaxHostChunks; ++i) {
+    if (c->ev_in[i]) cudaEventDestroy(c->ev_in[i]);
+    if (c->ev_out[i]) cudaEventDestroy(c->ev_out[i]);
+  }
   delete c;
 }
 
@@ -507,11 +552,11 @@ int va_run_attention(va_ctx* c, int layer, const float* input, int64_t rows, int
 
 namespace {
 
-// Shared body of the closed-form-position entry points.  window_rows = the whole
-// view-major window (all ranks); local_rows = this rank's slice.
-int device_call(va_ctx* c, int layer, const float* in, bool apply_ln1, float* out,
+// Checks a closed-form-position call and builds its BranchSpec.  window_rows = the
+// whole view-major window (all ranks); local_rows = this rank's slice.
+int make_branch(va_ctx* c, int layer, const float* in, bool apply_ln1, float* out,
                 const float* residual, int64_t window_rows, int64_t local_rows, int64_t row_offset,
-                int gh, int gw, int view_count, int global, bool sharded, cudaStream_t st) {
+                int gh, int gw, int view_count, int global, bool sharded, BranchSpec* b) {
   int rc = check_layer(c, layer);
   if (rc) return rc;
   if (window_rows <= 0 || window_rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
@@ -522,9 +567,57 @@ int device_call(va_ctx* c, int layer, const float* in, bool apply_ln1, float* ou
     if ((rc = ensure_positions(c, window_rows, gh, gw, view_count, global))) return rc;
     pos = c->pos;
   }
-  BranchSpec b{in, apply_ln1, out, residual, local_rows, row_offset, window_rows, pos, seg_len,
-               sharded && global};
+  *b = BranchSpec{in, apply_ln1, out, residual, local_rows, row_offset, window_rows, pos, seg_len,
+                  sharded && global};
+  return validate_branch(c, layer, *b);
+}
+
+// Shared body of the closed-form-position device entry points.
+int device_call(va_ctx* c, int layer, const float* in, bool apply_ln1, float* out,
+                const float* residual, int64_t window_rows, int64_t local_rows, int64_t row_offset,
+                int gh, int gw, int view_count, int global, bool sharded, cudaStream_t st) {
+  BranchSpec b;
+  int rc = make_branch(c, layer, in, apply_ln1, out, residual, window_rows, local_rows, row_offset,
+                       gh, gw, view_count, global, sharded, &b);
+  if (rc) return rc;
   return run_branch(c, layer, b, st);
+}
+
+// Row ranges [bounds[i], bounds[i+1]) of the host path's chunks.
+using Bounds = std::vector<int64_t>;
+
+Bounds split_rows(int64_t rows, int64_t step) {
+  Bounds r;
+  for (int64_t a = 0; a < rows; a += step) r.push_back(a);
+  r.push_back(rows);
+  return r;
+}
+
+// Chunking of the host path (va_attention_host).  Local blocks: groups of whole
+// views, each copied in, projected, attended, projected out and copied back on its
+// own, so the two copy directions overlap each other and the compute.  Global
+// blocks: the input in ~8 chunks of 128-row multiples (their LN/QKV overlaps the
+// later copies in), then the queries in chunks of about one wave of attention CTAs
+// (sms / heads CTAs of 256 queries each), so the copy out of one chunk overlaps the
+// attention of the next; no query can finish before the last key has arrived.
+void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Bounds* in,
+                      Bounds* out) {
+  const int64_t rows = b.rows;
+  if (b.seg_len > 0) {
+    const int64_t views = rows / b.seg_len;
+    const int64_t per = std::max<int64_t>(1, (views + 5) / 6);
+    *in = split_rows(rows, per * b.seg_len);
+    *out = *in;
+    (void)view_count;
+    return;
+  }
+  const int64_t step_in = std::max<int64_t>(128, ((rows + 7) / 8 + 127) / 128 * 128);
+  *in = split_rows(rows, step_in);
+  const int64_t pairs = (rows + 255) / 256;
+  const int64_t per_wave = std::max<int64_t>(1, c->sms / std::max(1, c->cfg.num_heads));
+  const int64_t n_out = std::min<int64_t>(kMaxHostChunks, (pairs + per_wave - 1) / per_wave);
+  const int64_t per_chunk = (pairs + n_out - 1) / n_out;
+  *out = split_rows(rows, per_chunk * 256);
 }
 
 }  // namespace
@@ -536,13 +629,55 @@ int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int 
   if (!c || !ln1 || !out) return VA_ERR_INVALID;
   if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
   VA_CUDA(c, cudaSetDevice(c->device));
-  const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
-  VA_CUDA(c, cudaMemcpyAsync(c->in_f32, ln1, bytes, cudaMemcpyHostToDevice, c->stream));
-  int rc = device_call(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
-                       view_count, global, false, c->stream);
+  BranchSpec b;
+  int rc = make_branch(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
+                       view_count, global, false, &b);
   if (rc) return rc;
-  VA_CUDA(c, cudaMemcpyAsync(out, c->out_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
-  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  Bounds in, outb;
+  plan_host_chunks(c, b, view_count, &in, &outb);
+  const int E = c->cfg.embed_dim;
+  const size_t row_bytes = static_cast<size_t>(E) * sizeof(float);
+  // Every stream is drained before returning, also on an error, so no copy still
+  // reads or writes the caller's buffers afterwards.
+  auto finish = [&](int code) {
+    cudaStreamSynchronize(c->h2d);
+    cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->d2h);
+    return code;
+  };
+#define VA_HOST(call)                                                          \
+  do {                                                                         \
+    cudaError_t e_ = (call);                                                   \
+    if (e_ != cudaSuccess) return finish(cuda_fail(c, e_, #call));             \
+  } while (0)
+  const int n_in = static_cast<int>(in.size()) - 1, n_out = static_cast<int>(outb.size()) - 1;
+  for (int i = 0; i < n_in; ++i) {
+    VA_HOST(cudaMemcpyAsync(c->in_f32 + in[i] * E, ln1 + in[i] * E, (in[i + 1] - in[i]) * row_bytes,
+                            cudaMemcpyHostToDevice, c->h2d));
+    VA_HOST(cudaEventRecord(c->ev_in[i], c->h2d));
+  }
+  for (int i = 0; i < n_in; ++i) {
+    VA_HOST(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
+    if ((rc = stage_qkv(c, layer, b, in[i], in[i + 1], c->stream))) return finish(rc);
+    if (b.seg_len > 0) {  // local: the chunk's views are complete
+      if ((rc = stage_attn(c, layer, b, in[i], in[i + 1], c->stream))) return finish(rc);
+      VA_HOST(cudaEventRecord(c->ev_out[i], c->stream));
+    }
+  }
+  if (b.seg_len == 0) {
+    for (int j = 0; j < n_out; ++j) {
+      if ((rc = stage_attn(c, layer, b, outb[j], outb[j + 1], c->stream))) return finish(rc);
+      VA_HOST(cudaEventRecord(c->ev_out[j], c->stream));
+    }
+  }
+  for (int j = 0; j < n_out; ++j) {
+    VA_HOST(cudaStreamWaitEvent(c->d2h, c->ev_out[j], 0));
+    VA_HOST(cudaMemcpyAsync(out + outb[j] * E, c->out_f32 + outb[j] * E,
+                            (outb[j + 1] - outb[j]) * row_bytes, cudaMemcpyDeviceToHost, c->d2h));
+  }
+#undef VA_HOST
+  VA_CUDA(c, cudaStreamSynchronize(c->d2h));
+  finish(VA_OK);
   return read_device_error(c);
 }
 
