@@ -390,11 +390,15 @@ def run_ours(args):
     barrier()
     e2e_s = max_over_ranks(e2e_s)
     e2e_value = flops / (e2e_s / args.steps) / 1e12
-    # parity of the host path against the device path on this input
+    # parity of the host path against the device path on this input.  The host path
+    # attends its queries in wave-sized chunks, the device path in one launch whose
+    # partial last wave is split over key ranges, so the two agree to rounding.
+    e2e_diff = None
     if world == 1:
         ref_dev = out.cpu().numpy()
-        if not np.array_equal(ref_dev, h_out.numpy()):
-            raise SystemExit("e2e output differs from the device-path output")
+        e2e_diff = float(np.abs(ref_dev - h_out.numpy()).max())
+        if not np.isfinite(e2e_diff) or e2e_diff > 2e-2:
+            raise SystemExit(f"e2e output differs from the device-path output (max abs {e2e_diff})")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -420,7 +424,8 @@ def run_ours(args):
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
                     "h2d_bytes_per_step": int(wl.rows * wl.embed * 4), "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
-                    "pinned H2D + va_attention_device_sharded + D2H per rank"},
+                    "pinned H2D + va_attention_device_sharded + D2H per rank",
+                    "max_abs_vs_device_path": e2e_diff},
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -3,8 +3,9 @@
 One child process per GPU; rank 0 creates the NCCL unique id and hands it to the
 others through a multiprocessing queue, every rank then projects K'/V for its own
 equal token slice, all-gathers them in place and attends its queries to the whole
-window.  The concatenated rank outputs must equal the single-GPU sub-block
-(same kernels, same per-row arithmetic) and meet the oracle gates on a row sample.
+window.  The concatenated rank outputs must match the single-GPU sub-block (same
+kernels; only the split of the single launch's last wave rounds differently) and
+meet the oracle gates on a row sample.
 Skipped when fewer GPUs than ranks are visible.
 """
 import multiprocessing as mp
@@ -89,7 +90,10 @@ def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks):
     x = syn.hidden_states(wl.rows, wl.embed, seed=3)
     single = ctx.attention_host(LAYER, x, wl.gh, wl.gw, wl.views, True)
     ctx.close()
-    assert np.array_equal(sharded, single), float(np.abs(sharded - single).max())
+    # A rank's query slice is attended in one launch without a split key range; the
+    # single-GPU launch splits the key range of its partial last wave, so the two
+    # agree to rounding (bitwise wherever neither splits).
+    assert float(np.abs(sharded - single).max()) <= 2e-3, float(np.abs(sharded - single).max())
 
     rows = np.sort(np.random.default_rng(nranks).choice(wl.rows, 96, replace=False)).astype(np.int64)
     pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, True)

@@ -75,6 +75,10 @@ struct va_ctx {
   cudaEvent_t ev_in[kMaxHostChunks] = {};
   cudaEvent_t ev_out[kMaxHostChunks] = {};
   int sms = 148;
+  // split-key tail of the attention kernel: partial rows and arrival counters
+  float* part_o = nullptr;     // [2*sms][128][64]
+  float* part_ml = nullptr;    // [2*sms][128][2]
+  int* part_count = nullptr;   // [2*sms]
   // Op::Attention scratch (grown on demand)
   __nv_bfloat16* op_buf = nullptr;  // q|k|v bf16 [3][H*n*64]
   size_t op_cap = 0;
@@ -272,6 +276,15 @@ int segments_for(va_ctx* c, int64_t rows, int view_count, int global, int* seg_l
   return VA_OK;
 }
 
+// Hands the context's partial-result workspace to a flash launch (split tail).
+void set_split_workspace(const va_ctx* c, va::FlashArgs* fa) {
+  fa->sms = c->sms;
+  fa->part_o = c->part_o;
+  fa->part_ml = c->part_ml;
+  fa->counters = c->part_count;
+  fa->part_slots = va::flash_part_slots(c->sms);
+}
+
 int validate_branch(va_ctx* c, int layer, const BranchSpec& b) {
   const LayerWeights& w = c->layers[layer];
   if (b.rows <= 0 || b.window_rows > c->cap || b.row_offset + b.rows > b.window_rows)
@@ -345,6 +358,7 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
     fa.q_offset = static_cast<int>(b.row_offset + q0);
     fa.kv_rows = static_cast<int>(b.window_rows);
   }
+  set_split_workspace(c, &fa);
   VA_CUDA(c, va::launch_flash(c->q + q0 * E, kk, vv, fa, c->err, st));
   va::ProjEpilogueArgs pa{};
   pa.bias = w.proj_b;
@@ -374,6 +388,8 @@ int read_device_error(va_ctx* c) {
   VA_CUDA(c, cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost));
   if (h != 0) {
     cudaMemset(c->err, 0, sizeof(int));
+    // An aborted split-tail CTA may have left an arrival counter behind.
+    cudaMemset(c->part_count, 0, static_cast<size_t>(va::flash_part_slots(c->sms)) * sizeof(int));
     char buf[128];
     std::snprintf(buf, sizeof(buf), "device error word %d (a bounded wait timed out)", h);
     return fail(c, VA_ERR_DEVICE, buf);
@@ -444,6 +460,13 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   }
   if ((e = cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
     return bail(e);
+  {
+    const size_t slots = static_cast<size_t>(va::flash_part_slots(c->sms));
+    if ((e = dmalloc(&c->part_o, slots * 128 * 64)) != cudaSuccess) return bail(e);
+    if ((e = dmalloc(&c->part_ml, slots * 128 * 2)) != cudaSuccess) return bail(e);
+    if ((e = dmalloc(&c->part_count, slots)) != cudaSuccess) return bail(e);
+    if ((e = cudaMemset(c->part_count, 0, slots * sizeof(int))) != cudaSuccess) return bail(e);
+  }
   if (ensure_rope_table(c, 128) != VA_OK) return bail(cudaErrorMemoryAllocation);
   *out = c;
   return VA_OK;
@@ -468,6 +491,9 @@ void va_destroy(va_ctx* c) {
   dfree(c->err);
   dfree(c->op_buf);
   dfree(c->op_pos);
+  dfree(c->part_o);
+  dfree(c->part_ml);
+  dfree(c->part_count);
   if (c->comm) va::comm_destroy(c->comm, false);
   if (c->stream) cudaStreamDestroy(c->stream);
   if (c->h2d) cudaStreamDestroy(c->h2d);
@@ -777,6 +803,7 @@ int va_op_attention_device(va_ctx* c, const float* q, const float* k, const floa
   fa.o_hnd = out;
   fa.embed = heads * 64;
   fa.v_f16 = 0;
+  set_split_workspace(c, &fa);
   VA_CUDA(c, va::launch_flash(qb, kb, vb, fa, c->err, st));
   return VA_OK;
 }
@@ -807,6 +834,7 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
       return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..5)");
     fa.poly_per8 = variant;
   }
+  set_split_workspace(c, &fa);
   VA_CUDA(c, va::launch_flash(static_cast<const __nv_bfloat16*>(q),
                               static_cast<const __nv_bfloat16*>(k),
                               static_cast<const __nv_bfloat16*>(v), fa, c->err,

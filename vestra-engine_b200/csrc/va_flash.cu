@@ -35,6 +35,8 @@
 // both issuers have committed the UMMAs that read it.
 #include <math.h>
 
+#include <algorithm>
+
 #include "va_internal.h"
 #include "va_ptx.cuh"
 #include "va_tmem16.cuh"
@@ -54,7 +56,7 @@ constexpr int kW20Threads = 640;   // "w20" layout
 // launch must give every thread at least kW20MinLaunchRegs registers, checked on
 // the host (cudaFuncGetAttributes) before each launch: 128*low + 512*high must
 // not exceed 640 * launch registers, or setmaxnreg.inc would wait forever.
-constexpr int kW20LowRegs = 40;
+constexpr int kW20LowRegs = 56;
 constexpr int kW20HighRegs = 104;
 constexpr int kW20MinLaunchRegs = (128 * kW20LowRegs + 512 * kW20HighRegs + 639) / 640;
 constexpr uint32_t kTileBytes = kTileQ * kHeadDim * 2;  // 16 KB, one 2-byte [128][64] tile
@@ -66,6 +68,8 @@ __host__ __device__ constexpr uint32_t col_o(int t) { return t * 256 + 192; }
 // maximum by more than 2^8; until then it keeps exponentiating against the older,
 // smaller maximum, so probabilities stay <= 256 (exact enough in bf16, F32 sums).
 constexpr float kRescaleLog2 = 8.0f;
+// Most key ranges one unit of the split tail is cut into.
+constexpr int kMaxSplits = 4;
 
 struct FlashSmem {
   static constexpr uint32_t kQ = 0;                              // Q0, Q1
@@ -86,6 +90,11 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
@@ -95,23 +104,56 @@ __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
 
 // Per-CTA geometry: the query rows of this CTA (local Q buffer) and its keys.
 struct Geom {
-  int q0, q_end, k0, klen, nq, num_kv, col, head;
-  bool tail_mask;
+  int q0, q_end, k0, nq, num_kv, col, head;
+  int last_valid;  // keys of the last 128-key tile inside the range (128: no masking)
 };
 
+// This CTA's place in the split tail of a global launch: key range `split` of
+// `nsplit` (nsplit 1 = the whole key range) of tail unit `tail_unit`.  Recomputed
+// from blockIdx where needed rather than kept live through the main loop.
+struct SplitPos {
+  int unit, split, nsplit, tail_unit;
+};
+
+__device__ __forceinline__ SplitPos split_pos(const FlashArgs& fa) {
+  SplitPos p{static_cast<int>(blockIdx.x), 0, 1, 0};
+  if (fa.seg_len == 0 && p.unit >= fa.n_full) {
+    const int r = p.unit - fa.n_full;
+    p.unit = fa.n_full + r / fa.splits;
+    p.split = r % fa.splits;
+    p.nsplit = fa.splits;
+    p.tail_unit = p.unit - fa.n_full;
+  }
+  return p;
+}
+
+// Global attention: a 1-D grid of units (head, query pair), query pair fastest so
+// the CTAs of one head (same K/V) run together; units >= n_full are split over
+// `splits` key ranges of whole 128-key tiles.  Local attention: grid (query pairs
+// of a segment, heads, segments), never split.
 __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
   Geom g;
-  const bool global = fa.seg_len == 0;
-  const int seg = blockIdx.z;
-  const int q_seg0 = global ? 0 : seg * fa.seg_len;
-  g.q_end = global ? fa.q_count : q_seg0 + fa.seg_len;
-  g.q0 = q_seg0 + blockIdx.x * 2 * kTileQ;
-  g.k0 = global ? 0 : fa.q_offset + q_seg0;
-  g.klen = global ? fa.kv_rows : fa.seg_len;
+  if (fa.seg_len == 0) {
+    const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
+    const SplitPos sp = split_pos(fa);
+    g.head = sp.unit / qpairs;
+    g.q0 = (sp.unit % qpairs) * 2 * kTileQ;
+    g.q_end = fa.q_count;
+    const int total = (fa.kv_rows + kTileK - 1) / kTileK;
+    const int t0 = sp.split * total / sp.nsplit, t1 = (sp.split + 1) * total / sp.nsplit;
+    g.k0 = t0 * kTileK;
+    g.last_valid = min(fa.kv_rows, t1 * kTileK) - (t1 - 1) * kTileK;
+    g.num_kv = t1 - t0;
+  } else {
+    const int q_seg0 = blockIdx.z * fa.seg_len;
+    g.q_end = q_seg0 + fa.seg_len;
+    g.q0 = q_seg0 + blockIdx.x * 2 * kTileQ;
+    g.k0 = fa.q_offset + q_seg0;
+    g.num_kv = (fa.seg_len + kTileK - 1) / kTileK;
+    g.last_valid = fa.seg_len - (g.num_kv - 1) * kTileK;
+    g.head = blockIdx.y;
+  }
   g.nq = (g.q_end - g.q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
-  g.num_kv = (g.klen + kTileK - 1) / kTileK;
-  g.tail_mask = (g.num_kv * kTileK) != g.klen;
-  g.head = blockIdx.y;
   g.col = g.head * kHeadDim;
   return g;
 }
@@ -136,6 +178,10 @@ struct Ctl {
   __device__ volatile int* kv_consumed() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 12); }
   __device__ volatile int* mma_done(int t) const {
     return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 16 + 4 * t);
+  }
+  // Split tail: 1 when this CTA merges query tile t.
+  __device__ volatile int* merge_flag(int t) const {
+    return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 24 + 4 * t);
   }
   __device__ uint32_t sQ(int t) const { return base + FlashSmem::kQ + t * kTileBytes; }
   __device__ uint32_t sK(int s) const { return base + FlashSmem::kK + s * kTileBytes; }
@@ -407,9 +453,9 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         tmem_ld128(tS, s);
         tc_fence_before();
         mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
-        const bool tail = g.tail_mask && j == g.num_kv - 1;
+        const bool tail = j == g.num_kv - 1 && g.last_valid < kTileK;
         if (tail) {
-          const int valid = g.klen - j * kTileK;
+          const int valid = g.last_valid;
 #pragma unroll
           for (int q = 0; q < 128; ++q)
             if (q >= valid) s[q] = -INFINITY;
@@ -555,9 +601,9 @@ __global__ void __launch_bounds__(kW20Threads, 1)
         tmem_ld_16x256b_x16(tS, s);
         tc_fence_before();
         mbar_arrive(c.s_free(t));
-        const bool tail = g.tail_mask && j == g.num_kv - 1;
+        const bool tail = j == g.num_kv - 1 && g.last_valid < kTileK;
         if (tail) {
-          const int valid = g.klen - j * kTileK;
+          const int valid = g.last_valid;
 #pragma unroll
           for (int k = 0; k < 16; ++k)
 #pragma unroll
@@ -646,14 +692,81 @@ __global__ void __launch_bounds__(kW20Threads, 1)
       }
       bool fin = ok && mbar_wait(c.o_final(t), 0, abort_flag, err, kDevTimeoutConsumer);
       fin = __all_sync(0xffffffffu, fin);
+      float o[32];  // block k: o[4k..4k+1] row 0, o[4k+2..4k+3] row 1 (unnormalised)
       if (fin) {
         tc_fence_after();
         l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
         l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
         l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-        float o[32];
         tmem_ld_16x256b_x8(tO, o);
+      }
+      const SplitPos sp = split_pos(fa);
+      if (sp.nsplit > 1) {
+        // Split tail: publish this key range's partial rows, count the arrival, and
+        // let the CTA that arrives last merge every split.  All 8 warps of the tile
+        // get here (each wait above is bounded), so both named barriers complete.
+        const int r0 = lane_base + (lane >> 2);  // rows r0 and r0 + 8 of the tile
+        const int slot = (sp.tail_unit * sp.nsplit + sp.split) * 2 + t;
+        if (fin) {
+          float* po = fa.part_o + static_cast<size_t>(slot) * kTileQ * kHeadDim;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+              *reinterpret_cast<float2*>(po + (r0 + 8 * rr) * kHeadDim + 8 * k + c0) =
+                  make_float2(o[4 * k + 2 * rr], o[4 * k + 2 * rr + 1]);
+          if ((lane & 3) == 0) {
+            float2* pm = reinterpret_cast<float2*>(fa.part_ml + static_cast<size_t>(slot) * kTileQ * 2);
+            pm[r0] = make_float2(m0, l0);
+            pm[r0 + 8] = make_float2(m1, l1);
+          }
+        }
+        __threadfence();
+        named_bar_sync(1 + t, 256);
+        if ((sw & 7) == 0 && lane == 0) {
+          const int old = atomicAdd(fa.counters + sp.tail_unit * 2 + t, 1);
+          const bool last = old == sp.nsplit - 1;
+          if (last) atomicExch(fa.counters + sp.tail_unit * 2 + t, 0);  // ready for the next launch
+          *c.merge_flag(t) = last ? 1 : 0;
+        }
+        named_bar_sync(1 + t, 256);
+        if (*c.merge_flag(t) == 0) {
+          fin = false;  // another split's CTA merges this tile
+        } else if (fin) {
+          __threadfence();
+          float mx0 = -INFINITY, mx1 = -INFINITY;
+          for (int s = 0; s < sp.nsplit; ++s) {
+            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+            const float2* pm = reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2);
+            mx0 = fmaxf(mx0, __ldcg(pm + r0).x);
+            mx1 = fmaxf(mx1, __ldcg(pm + r0 + 8).x);
+          }
+          l0 = 0.f;
+          l1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          for (int s = 0; s < sp.nsplit; ++s) {
+            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+            const float2* pm = reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2);
+            const float* po = fa.part_o + static_cast<size_t>(sl) * kTileQ * kHeadDim;
+            const float2 a = __ldcg(pm + r0), b = __ldcg(pm + r0 + 8);
+            const float w0 = ex2(a.x - mx0), w1 = ex2(b.x - mx1);
+            l0 += w0 * a.y;
+            l1 += w1 * b.y;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float2 u = __ldcg(reinterpret_cast<const float2*>(po + r0 * kHeadDim + 8 * k + c0));
+              const float2 v = __ldcg(reinterpret_cast<const float2*>(po + (r0 + 8) * kHeadDim + 8 * k + c0));
+              o[4 * k] += w0 * u.x;
+              o[4 * k + 1] += w0 * u.y;
+              o[4 * k + 2] += w1 * v.x;
+              o[4 * k + 3] += w1 * v.y;
+            }
+          }
+        }
+      }
+      if (fin) {
         const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
 #pragma unroll
         for (int rr = 0; rr < 2; ++rr) {
@@ -683,7 +796,8 @@ __global__ void __launch_bounds__(kW20Threads, 1)
 }  // namespace
 
 cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                         const FlashArgs& fa, int* err, cudaStream_t st) {
+                         const FlashArgs& fa_in, int* err, cudaStream_t st) {
+  FlashArgs fa = fa_in;
   // Every TMA box must start inside its tensor: q rows [0, q_count), key rows
   // [q_offset + segment start, +seg_len) or [0, kv_rows).
   if (fa.q_count <= 0 || fa.kv_rows <= 0 || fa.heads <= 0 || fa.embed != fa.heads * kHeadDim ||
@@ -742,8 +856,41 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        FlashSmem::kLaunchBytes);
   if (e != cudaSuccess) return e;
-  const int span = fa.seg_len > 0 ? fa.seg_len : fa.q_count;
-  dim3 grid((span + 2 * kTileQ - 1) / (2 * kTileQ), fa.heads, segs);
+  dim3 grid;
+  if (fa.seg_len > 0) {
+    grid = dim3((fa.seg_len + 2 * kTileQ - 1) / (2 * kTileQ), fa.heads, segs);
+    fa.n_full = 0;
+    fa.splits = 1;
+  } else {
+    // Units (head, query pair); the partial last wave is split over key ranges when
+    // the caller gave a partial-result workspace (four-threads-per-row kernel).
+    const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
+    const int units = qpairs * fa.heads;
+    const int num_kv = (fa.kv_rows + kTileK - 1) / kTileK;
+    fa.n_full = units;
+    fa.splits = 1;
+    const bool w20_kernel = threads == kW20Threads;
+    if (w20_kernel && fa.part_o && fa.part_ml && fa.counters && fa.sms > 0) {
+      // The tail of `rem` units cut into s key ranges takes ceil(rem*s/sms) rounds
+      // of 1/s unit time; pick the s with the shortest tail (each split also pays
+      // a few percent for its own setup and the merge).
+      const int rem = units % fa.sms;
+      int best = 1;
+      double best_cost = 1.0;
+      for (int sp = 2; rem && sp <= std::min(kMaxSplits, num_kv); ++sp) {
+        const double cost = static_cast<double>((rem * sp + fa.sms - 1) / fa.sms) / sp + 0.03;
+        if (cost < best_cost && rem * sp * 2 <= fa.part_slots) {
+          best = sp;
+          best_cost = cost;
+        }
+      }
+      if (best >= 2) {
+        fa.n_full = units - rem;
+        fa.splits = best;
+      }
+    }
+    grid = dim3(fa.n_full + (units - fa.n_full) * fa.splits, 1, 1);
+  }
   kern<<<grid, threads, FlashSmem::kLaunchBytes, st>>>(mq, mk, mv, fa, err);
   return cudaGetLastError();
 }

@@ -59,7 +59,23 @@ struct FlashArgs {
   int embed;
   int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
   int poly_per8 = kDefaultPolyPer8;  // bf16 path: variant = poly + 8 * form (see launch_flash)
+  // Split-key tail of global attention (four-threads-per-row kernel only).  With
+  // U = heads x query-pairs units and `sms` multiprocessors, the last U mod sms
+  // units (the partial last wave) are each run as `splits` CTAs over disjoint key
+  // ranges; their unnormalised partial results meet in part_o / part_ml and the
+  // CTA that finishes last (counters) merges them.  No split when part_o is null.
+  int sms = 0;
+  float* part_o = nullptr;    // [slots][128][64] F32, one slot per (split CTA, query tile)
+  float* part_ml = nullptr;   // [slots][128][2] F32: reference max (log2 domain), row sum
+  int* counters = nullptr;    // [tail units][2] (at least part_slots ints), zero between launches
+  int part_slots = 0;
+  // Filled in by launch_flash (kernel-side view of the plan).
+  int n_full = 0;
+  int splits = 1;
 };
+// Slots a context provides for the split tail: rem < sms units, at most 4 key
+// ranges each, two query tiles per CTA.
+inline int flash_part_slots(int sms) { return 2 * 4 * sms; }
 
 // Tensor-map encoding through the driver entry point (no -lcuda needed).
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
