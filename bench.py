@@ -71,16 +71,18 @@ def load_peaks():
 
 
 def cpu_info():
-    model = ""
+    """Model name, logical CPU count and AVX-512 feature flags of the host."""
+    model, flags = "", []
     try:
         with open("/proc/cpuinfo") as f:
             for line in f:
-                if line.startswith("model name"):
+                if line.startswith("model name") and not model:
                     model = line.split(":", 1)[1].strip()
-                    break
+                elif line.startswith("flags") and not flags:
+                    flags = sorted(x for x in line.split(":", 1)[1].split() if x.startswith("avx512"))
     except OSError:
         pass
-    return model
+    return f"{model}; nproc {os.cpu_count()}; {' '.join(flags) or 'no avx512'}"
 
 
 # --------------------------------------------------------------------------- clocks
@@ -325,6 +327,24 @@ def run_ours(args):
     flops = wl.attention_flops()
     value = flops / (ms_per_step * 1e-3) / 1e12
 
+    # ---- per-phase times of the same step (CUDA events between its launches),
+    # the reference's phase names; outside the timed region above.
+    ctx.set_phase_profile(True)
+    phase_runs = []
+    for _ in range(max(3, min(args.steps, 10))):
+        flush_buf.zero_()
+        step()
+        phase_runs.append(ctx.phase_times())
+    ctx.set_phase_profile(False)
+    barrier()
+    phases = {k: round(statistics.median(r[k] for r in phase_runs), 4) for k in phase_runs[0]}
+    local_rows = local
+    gemm_tflops = {
+        "qkv": round(2.0 * local_rows * wl.embed * 3 * wl.embed / (phases["qkv"] * 1e-3) / 1e12, 1),
+        "proj": round(2.0 * local_rows * wl.embed * wl.embed / (phases["proj"] * 1e-3) / 1e12, 1),
+    }
+    ln_gbs = round(local_rows * wl.embed * 6 / (phases["ln"] * 1e-3) / 1e9, 1)  # F32 read + bf16 write
+
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
     # Q/K ~ N(0,1) per channel like QK-normalised rows; V bf16 (production path).
     g = torch.Generator(device="cuda").manual_seed(rank)
@@ -426,6 +446,7 @@ def run_ours(args):
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
                     "pinned H2D + va_attention_device_sharded + D2H per rank",
                     "max_abs_vs_device_path": e2e_diff},
+            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

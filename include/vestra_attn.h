@@ -194,6 +194,26 @@ int va_permute_views_device(const float* src_dev, float* dst_dev, const int* ord
  * device).  Returns VA_OK or VA_ERR_DEVICE with the code in va_last_error. */
 int va_check_device(va_ctx* ctx);
 
+/* Phase profile (the reference's DA_PHASE_PROFILE, vit_block.rs:980-990): while
+ * enabled, every device-path sub-block call (va_attention_device,
+ * va_block_attention_device, va_attention_device_sharded) records CUDA events
+ * between its launches.  va_phase_times then returns the last such call's
+ * durations in ms, in this order: [0] ln (LN1 / bf16 cast), [1] qkv (QKV GEMM with
+ * the fused qk_norm_rope and head pack), [2] all-gather of K'/V (0 unless sharded),
+ * [3] core (flash attention, unpack fused), [4] proj.  Profiling adds no
+ * synchronisation to the call; va_phase_times waits for the last event. */
+int va_set_phase_profile(va_ctx* ctx, int enable);
+int va_phase_times(va_ctx* ctx, float* ms_out /* [5] */);
+
+/* Failure-detection self-test (no reference counterpart; the reference has no
+ * device-side waits).  Launches one kernel whose only wait is on a barrier that
+ * nothing arrives on, through the same bounded wait the attention kernels use,
+ * with a limit of limit_us microseconds (1 .. 1e6).  The wait gives up, the
+ * kernel writes a timeout code into the device error word and returns; the call
+ * then returns VA_ERR_DEVICE exactly as a stalled attention launch would, and the
+ * context stays usable.  Any other status means the mechanism is broken. */
+int va_selftest_bounded_wait(va_ctx* ctx, int64_t limit_us);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,53 @@
+"""Failure detection without a GPU fault.
+
+Every wait in the library's kernels is bounded; a wait that runs out sets the
+CTA's abort flag and the context's device error word, the kernel unwinds, and the
+host entry point returns VA_ERR_DEVICE.  The self-test kernel waits on a barrier
+that nothing arrives on (a flag nobody sets), with a short limit, and the test
+checks that the status comes back, that the context stays usable afterwards, and
+that the error word is cleared once read.  Nothing here traps or faults the GPU.
+"""
+import time
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA GPU")]
+
+import synthetic as syn  # noqa: E402
+import vestra_attn as va  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = va.Context(va.default_config(max_rows=2 * 866, num_register=1), 0)
+    yield c
+    c.close()
+
+
+def test_bounded_wait_reports_timeout_and_context_recovers(ctx, oracle_mod):
+    t = time.perf_counter()
+    rc = ctx.selftest_bounded_wait(20_000)  # 20 ms limit
+    dt = time.perf_counter() - t
+    assert rc == va.VA_ERR_DEVICE, rc
+    assert "timed out" in ctx.last_error()
+    assert 0.015 < dt < 5.0, dt  # the wait lasted about its limit, then gave up
+    ctx.check_device()  # the error word was cleared when it was read
+
+    # The context still runs the attention path correctly after the timeout.
+    wl = syn.CONFIGS["cfg2_s2_global"]
+    p = syn.layer_weights(wl.embed, seed=2, layer=4)
+    ctx.load_layer(4, p)
+    x = syn.hidden_states(wl.rows, wl.embed, seed=2)
+    got = ctx.attention_host(4, x, wl.gh, wl.gw, wl.views, True)
+    pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, True)
+    rows = np.arange(0, wl.rows, 37, dtype=np.int64)
+    ref = oracle_mod.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=0, q_rows=rows)
+    assert np.abs(got[rows] - ref).max() <= 2e-2
+
+
+def test_selftest_limits_are_checked_on_the_host(ctx):
+    assert ctx.selftest_bounded_wait(0) == va.VA_ERR_INVALID
+    assert ctx.selftest_bounded_wait(2_000_000) == va.VA_ERR_INVALID

@@ -173,6 +173,22 @@ def test_attention_block_s12_global_subset(ctx, oracle_mod):
     assert_close(got, ref, what="S=12 global (row subset)")
 
 
+def test_attention_block_large_s32_global_subset(oracle_mod):
+    # DA3-LARGE shapes (E=1024, 16 heads), 32 views of 2 + 72x48 tokens: one
+    # 110,656-token global window (~50 TFLOP); rows are independent, so a seeded
+    # row sample checks the whole launch exactly.
+    wl = syn.CONFIGS["cfg5_large_s32_global"]
+    cfg = va.default_config(embed_dim=wl.embed, num_heads=wl.heads, max_rows=wl.rows, depth=24,
+                            num_register=wl.n_special - 1, rope_start=4, qknorm_start=4)
+    c = va.Context(cfg, 0)
+    try:
+        rows = np.sort(np.random.default_rng(5).choice(wl.rows, 64, replace=False)).astype(np.int64)
+        got, ref = _block_case(oracle_mod, c, wl, layer=7, seed=5, ls1=True, q_rows=rows)
+        assert_close(got, ref, what="LARGE S=32 global (row subset)")
+    finally:
+        c.close()
+
+
 def test_attention_block_s12_local_batched(ctx, oracle_mod):
     wl = syn.CONFIGS["cfg4_s12_local"]
     rows = np.sort(np.random.default_rng(4).choice(wl.rows, 128, replace=False)).astype(np.int64)

@@ -40,6 +40,7 @@ struct LayerWeights {
 };
 
 constexpr int kMaxHostChunks = 32;
+constexpr int kPhases = 5;
 
 struct PosKey {
   int64_t rows = -1;
@@ -75,6 +76,11 @@ struct va_ctx {
   cudaEvent_t ev_in[kMaxHostChunks] = {};
   cudaEvent_t ev_out[kMaxHostChunks] = {};
   int sms = 148;
+  // phase profile (va_set_phase_profile): events between the launches of the last
+  // device-path call: ln | qkv+qk_norm_rope | all-gather | core | proj
+  bool phase_profile = false;
+  bool phase_valid = false;
+  cudaEvent_t ph_ev[kPhases + 1] = {};
   // split-key tail of the attention kernel: partial rows and arrival counters
   float* part_o = nullptr;     // [2*sms][128][64]
   float* part_ml = nullptr;    // [2*sms][128][2]
@@ -301,12 +307,14 @@ int validate_branch(va_ctx* c, int layer, const BranchSpec& b) {
 // Projection stage for rows [r0, r1) of this rank's slice: LN1 / bf16 cast, then
 // the QKV GEMM with its bias + QK-norm + RoPE epilogue; Q' goes to c->q, K' and V
 // to the rank's rows of the key window.
-int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1, cudaStream_t st) {
+int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1, cudaStream_t st,
+              cudaEvent_t between = nullptr) {
   const LayerWeights& w = c->layers[layer];
   const int E = c->cfg.embed_dim;
   const int n = static_cast<int>(r1 - r0);
   VA_CUDA(c, va::launch_ln_cast(b.in + r0 * E, b.apply_ln1 ? w.norm1_w : nullptr, w.norm1_b,
                                 c->cfg.ln_eps, n, E, c->x + r0 * E, st));
+  if (between) VA_CUDA(c, cudaEventRecord(between, st));
   va::QkvEpilogueArgs qa{};
   qa.bias = w.qkv_b;
   const bool qk = layer_use_qknorm(c, layer);
@@ -333,7 +341,8 @@ int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1,
 // Attention stage for this rank's queries [q0, q1): fused flash attention against
 // the key window (global) or the queries' own views (local; the range then holds
 // whole views), then the output projection with its bias/ls1/residual epilogue.
-int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1, cudaStream_t st) {
+int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1, cudaStream_t st,
+               cudaEvent_t between = nullptr) {
   const LayerWeights& w = c->layers[layer];
   const int E = c->cfg.embed_dim;
   const int n = static_cast<int>(q1 - q0);
@@ -360,6 +369,7 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
   }
   set_split_workspace(c, &fa);
   VA_CUDA(c, va::launch_flash(c->q + q0 * E, kk, vv, fa, c->err, st));
+  if (between) VA_CUDA(c, cudaEventRecord(between, st));
   va::ProjEpilogueArgs pa{};
   pa.bias = w.proj_b;
   pa.ls1 = w.ls1;
@@ -375,12 +385,23 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
 int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
   int rc = validate_branch(c, layer, b);
   if (rc) return rc;
-  if ((rc = stage_qkv(c, layer, b, 0, b.rows, st))) return rc;
+  // With the phase profile on, an event goes between every two launches; the ln
+  // and qkv phases are split inside stage_qkv's two launches by mark(1).
+  const bool prof = c->phase_profile;
+  auto mark = [&](int i) { return prof ? cudaEventRecord(c->ph_ev[i], st) : cudaSuccess; };
+  c->phase_valid = false;
+  VA_CUDA(c, mark(0));
+  if ((rc = stage_qkv(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[1] : nullptr))) return rc;
+  VA_CUDA(c, mark(2));
   if (b.gather) {
     const int E = c->cfg.embed_dim;
     if ((rc = gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st))) return rc;
   }
-  return stage_attn(c, layer, b, 0, b.rows, st);
+  VA_CUDA(c, mark(3));
+  if ((rc = stage_attn(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[4] : nullptr))) return rc;
+  VA_CUDA(c, mark(5));
+  c->phase_valid = prof;
+  return VA_OK;
 }
 
 int read_device_error(va_ctx* c) {
@@ -460,6 +481,8 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   }
   if ((e = cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
     return bail(e);
+  for (int i = 0; i <= kPhases; ++i)
+    if ((e = cudaEventCreate(&c->ph_ev[i])) != cudaSuccess) return bail(e);
   {
     const size_t slots = static_cast<size_t>(va::flash_part_slots(c->sms));
     if ((e = dmalloc(&c->part_o, slots * 128 * 64)) != cudaSuccess) return bail(e);
@@ -502,6 +525,8 @@ void va_destroy(va_ctx* c) {
     if (c->ev_in[i]) cudaEventDestroy(c->ev_in[i]);
     if (c->ev_out[i]) cudaEventDestroy(c->ev_out[i]);
   }
+  for (int i = 0; i <= kPhases; ++i)
+    if (c->ph_ev[i]) cudaEventDestroy(c->ph_ev[i]);
   delete c;
 }
 
@@ -984,6 +1009,35 @@ int va_check_device(va_ctx* c) {
   if (!c) return VA_ERR_INVALID;
   VA_CUDA(c, cudaSetDevice(c->device));
   VA_CUDA(c, cudaDeviceSynchronize());
+  return read_device_error(c);
+}
+
+int va_set_phase_profile(va_ctx* c, int enable) {
+  if (!c) return VA_ERR_INVALID;
+  c->phase_profile = enable != 0;
+  c->phase_valid = false;
+  return VA_OK;
+}
+
+int va_phase_times(va_ctx* c, float* ms_out) {
+  if (!c || !ms_out) return VA_ERR_INVALID;
+  if (!c->phase_valid) return fail(c, VA_ERR_STATE, "no profiled device-path call since the profile was enabled");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaEventSynchronize(c->ph_ev[kPhases]));
+  for (int i = 0; i < kPhases; ++i) VA_CUDA(c, cudaEventElapsedTime(&ms_out[i], c->ph_ev[i], c->ph_ev[i + 1]));
+  return VA_OK;
+}
+
+int va_selftest_bounded_wait(va_ctx* c, int64_t limit_us) {
+  if (!c) return VA_ERR_INVALID;
+  if (limit_us <= 0 || limit_us > 1000000) return fail(c, VA_ERR_INVALID, "limit_us must be in (0, 1e6]");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  int rc = read_device_error(c);  // start from a clear error word
+  if (rc) return rc;
+  VA_CUDA(c, va::launch_bounded_wait_selftest(static_cast<unsigned long long>(limit_us) * 1000ull,
+                                              c->err, c->stream));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
   return read_device_error(c);
 }
 

@@ -106,6 +106,7 @@ cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, 
 cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
                                  int embed, cudaStream_t st);
 // View permutation: dst view i <- src view order[i] (order on the device).
+cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns, int* err, cudaStream_t st);
 cudaError_t launch_permute_views(const float* src, float* dst, const int* order, int views,
                                  int64_t view_elems, cudaStream_t st);
 

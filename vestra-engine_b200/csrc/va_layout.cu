@@ -238,4 +238,27 @@ cudaError_t launch_permute_views(const float* src, float* dst, const int* order,
   return cudaGetLastError();
 }
 
+// Failure-detection self-test: one thread waits on an mbarrier that nothing
+// arrives on, through the same bounded wait the pipelined kernels use, so the
+// wait gives up after limit_ns and writes kDevTimeoutConsumer into the device
+// error word; the kernel then returns normally.
+__global__ void bounded_wait_selftest_kernel(unsigned long long limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(b, 0, &abort_flag, err, kDevTimeoutConsumer, limit_ns);
+  __syncthreads();
+}
+
+cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns, int* err, cudaStream_t st) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, st>>>(limit_ns, err);
+  return cudaGetLastError();
+}
+
 }  // namespace va

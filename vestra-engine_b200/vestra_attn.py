@@ -35,6 +35,7 @@ EXPORTED = [
     "va_block_attention_device", "va_op_attention_device", "va_flash_attention_bf16",
     "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
+    "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
     "va_comm_unique_id", "va_comm_init", "va_attention_device_sharded", "va_op_attention_noalloc",
 ]
 
@@ -99,6 +100,9 @@ def load_library(path: str = LIB_PATH):
         "va_camera_inject_device": ([_vp, _vp, c_int, i64, c_int, _vp], c_int),
         "va_permute_views_device": ([_vp, _vp, _i32p, c_int, i64, _vp], c_int),
         "va_check_device": ([_vp], c_int),
+        "va_selftest_bounded_wait": ([_vp, ctypes.c_int64], c_int),
+        "va_set_phase_profile": ([_vp, c_int], c_int),
+        "va_phase_times": ([_vp, _vp], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -267,6 +271,25 @@ class Context:
 
     def check_device(self):
         self.check(self.lib.va_check_device(self.h))
+
+    PHASES = ("ln", "qkv", "allgather", "core", "proj")
+
+    def set_phase_profile(self, enable: bool):
+        self.check(self.lib.va_set_phase_profile(self.h, int(bool(enable))))
+
+    def phase_times(self) -> dict:
+        """Durations (ms) of the last profiled device-path call, by phase name."""
+        ms = np.zeros(len(self.PHASES), np.float32)
+        self.check(self.lib.va_phase_times(self.h, _ptr(ms)))
+        return dict(zip(self.PHASES, (float(v) for v in ms)))
+
+    def selftest_bounded_wait(self, limit_us: int) -> int:
+        """Runs the failure-detection self-test; returns the raw status (VA_ERR_DEVICE
+        when the bounded wait gave up as designed)."""
+        return self.lib.va_selftest_bounded_wait(self.h, int(limit_us))
+
+    def last_error(self) -> str:
+        return self.lib.va_last_error(self.h).decode()
 
 
 class CudaAttentionExecutor:
