@@ -90,11 +90,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {

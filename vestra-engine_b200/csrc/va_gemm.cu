@@ -11,11 +11,14 @@
 //   output O (token-major bf16), B = W_proj^T [E, E].  Epilogue: + bias, * ls1 when
 //   present, + residual when asked (vit_block.rs:1090), F32 store.
 //
-// Structure: one 128 x BN output tile per CTA, 6 warps.
+// Structure: one 128 x BN output tile per CTA, 10 warps, two CTAs per SM (the
+// STAGES-deep ring is sized for that), so one CTA's epilogue overlaps the other's
+// main loop.
 //   warp 0      TMA producer (one elected lane), STAGES-deep smem ring
 //   warp 1      TMEM allocator + single-thread UMMA issuer (M=128, N=BN, K=16 steps)
-//   warps 2..5  epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (tile rows), one
-//               row per thread, 32 columns per tcgen05.ld.
+//   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4)..+31 (tile rows), one
+//               row per thread; warps 2..5 take columns [0, BN/2), warps 6..9
+//               [BN/2, BN).
 // Operands arrive through TMA with SWIZZLE_128B (64 bf16 = one 128-B row per
 // box row), which is exactly the UMMA K-major SW128 canonical layout.
 #include <math.h>
@@ -29,11 +32,12 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
 
 __device__ __forceinline__ float ln_rsqrt(float var_eps) { return 1.0f / sqrtf(var_eps); }
 
-// LayerNorm of one 64-wide head row held in registers (torch semantics).
+// LayerNorm of one 64-wide head row held in registers (torch semantics); g and b
+// point at the affine parameters in shared memory.
 __device__ __forceinline__ void head_layernorm(float* x, const float* g, const float* b, float eps) {
   float mean = 0.f;
 #pragma unroll
@@ -48,7 +52,7 @@ __device__ __forceinline__ void head_layernorm(float* x, const float* g, const f
   var *= (1.0f / 64.0f);
   const float inv = ln_rsqrt(var + eps);
 #pragma unroll
-  for (int i = 0; i < 64; ++i) x[i] = (x[i] - mean) * inv * __ldg(g + i) + __ldg(b + i);
+  for (int i = 0; i < 64; ++i) x[i] = (x[i] - mean) * inv * g[i] + b[i];
 }
 
 // 2D RoPE of one 64-wide head row: channels [0,32) rotate with y, [32,64) with x.
@@ -78,95 +82,150 @@ __device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, 
   }
 }
 
-__device__ __forceinline__ void store_bf16_row64(__nv_bfloat16* dst, const float* x) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 u;
-    u.x = pack_bf16x2(x[8 * c + 0], x[8 * c + 1]);
-    u.y = pack_bf16x2(x[8 * c + 2], x[8 * c + 3]);
-    u.z = pack_bf16x2(x[8 * c + 4], x[8 * c + 5]);
-    u.w = pack_bf16x2(x[8 * c + 6], x[8 * c + 7]);
-    d[c] = u;
+// bf16 (or f16) of 8 consecutive values as one 16-byte chunk.
+__device__ __forceinline__ uint4 pack8(const float* x, bool f16) {
+  uint4 u;
+  if (f16) {
+    u.x = f16x2_from_f32(x[0], x[1]);
+    u.y = f16x2_from_f32(x[2], x[3]);
+    u.z = f16x2_from_f32(x[4], x[5]);
+    u.w = f16x2_from_f32(x[6], x[7]);
+  } else {
+    u.x = pack_bf16x2(x[0], x[1]);
+    u.y = pack_bf16x2(x[2], x[3]);
+    u.z = pack_bf16x2(x[4], x[5]);
+    u.w = pack_bf16x2(x[6], x[7]);
   }
+  return u;
 }
 
-__device__ __forceinline__ void store_f16_row64(__nv_bfloat16* dst, const float* x) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 u;
-    u.x = f16x2_from_f32(x[8 * c + 0], x[8 * c + 1]);
-    u.y = f16x2_from_f32(x[8 * c + 2], x[8 * c + 3]);
-    u.z = f16x2_from_f32(x[8 * c + 4], x[8 * c + 5]);
-    u.w = f16x2_from_f32(x[8 * c + 6], x[8 * c + 7]);
-    d[c] = u;
-  }
-}
+// Epilogue contract (warps 2..9 of the GEMM CTA, 256 threads):
+//   stage(cbuf, n0, t)  thread t < 256 copies its share of the tile's per-column
+//                       constants into shared memory, before the accumulator is ready;
+//   run(...)            thread (quad, half) turns TMEM row r, columns of its half, into
+//                       output values and writes them as 16 KB SWIZZLE_128B tiles of
+//                       128 rows x 128 B into the (by then idle) operand ring;
+//   store(...)          one thread of each half sends that half's tiles out by TMA.
+// Rows past M are computed from the zero-filled operands and clipped by the store.
+constexpr uint32_t kOutTileBytes = 16384;
 
 struct QkvEpilogue {
   QkvEpilogueArgs a;
+  CUtensorMap map_out[3];  // Q, K, V: [rows][E] 2-byte, box 64 x 128
+
+  // cbuf: [0, 256) bias of the tile's columns, [256, 320) gamma, [320, 384) beta of
+  // the section's QK-norm (1 and 0 when the section has none).
+  __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const {
+    const int section = n0 / a.embed;
+    cbuf[t] = a.bias[n0 + t];
+    if (t < 64) {
+      const float* g = section == 0 ? a.q_g : a.k_g;
+      const float* b = section == 0 ? a.q_b : a.k_b;
+      const bool norm = section < 2 && g != nullptr;
+      cbuf[256 + t] = norm ? g[t] : 1.0f;
+      cbuf[320 + t] = norm ? b[t] : 0.0f;
+    }
+  }
+
   template <int BN>
-  __device__ __forceinline__ void run(uint32_t tmem_row, int grow, bool valid, int n0) const {
-    const int section = n0 / a.embed;         // 0 = Q, 1 = K, 2 = V
-    const int h0 = (n0 - section * a.embed) / 64;
-    __nv_bfloat16* base = section == 0 ? a.q_out : (section == 1 ? a.k_out : a.v_out);
-    const float* g = section == 0 ? a.q_g : a.k_g;
-    const float* b = section == 0 ? a.q_b : a.k_b;
+  __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
+                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+    static_assert(BN == 256, "QKV tiles are 4 heads wide");
+    const int section = n0 / a.embed;  // 0 = Q, 1 = K, 2 = V
+    const bool norm = section < 2 && (section == 0 ? a.q_g : a.k_g) != nullptr;
+    const bool rope = section < 2 && a.pos != nullptr;
+    const bool f16 = section == 2 && a.v_f16;
+    const int2 pos = (rope && valid) ? a.pos[m0 + r] : make_int2(0, 0);
 #pragma unroll 1
-    for (int hh = 0; hh < BN / 64; ++hh) {
+    for (int j = 0; j < 2; ++j) {
+      const int hh = half * 2 + j;
       float x[64];
       tmem_ld32(tmem_row + hh * 64, x);
       tmem_ld32(tmem_row + hh * 64 + 32, x + 32);
-      if (!valid) continue;
-      const float* bias = a.bias + n0 + hh * 64;
+      if (valid) {
+        const float4* bias = reinterpret_cast<const float4*>(cbuf + hh * 64);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) x[i] += __ldg(bias + i);
-      if (section < 2) {
-        if (g) head_layernorm(x, g, b, a.qk_eps);
-        if (a.pos) head_rope(x, a.pos[grow], a.rope_cs, a.rope_pairing);
+        for (int i = 0; i < 16; ++i) {
+          const float4 v = bias[i];
+          x[4 * i] += v.x;
+          x[4 * i + 1] += v.y;
+          x[4 * i + 2] += v.z;
+          x[4 * i + 3] += v.w;
+        }
+        if (norm) head_layernorm(x, cbuf + 256, cbuf + 320, a.qk_eps);
+        if (rope) head_rope(x, pos, a.rope_cs, a.rope_pairing);
       }
-      __nv_bfloat16* dst = base + static_cast<size_t>(grow) * a.embed + (h0 + hh) * 64;
-      if (section == 2 && a.v_f16)
-        store_f16_row64(dst, x);
-      else
-        store_bf16_row64(dst, x);
+      const uint32_t tile = out_smem + hh * kOutTileBytes;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) st_shared_v4(tile + sw128_offset(r, c), pack8(x + 8 * c, f16));
     }
+  }
+
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+    const int section = n0 / a.embed;
+    const int h0 = (n0 - section * a.embed) / 64;
+    for (int j = 0; j < 2; ++j) {
+      const int hh = half * 2 + j;
+      tma_store_2d(&map_out[section], out_smem + hh * kOutTileBytes, (h0 + hh) * 64, m0);
+    }
+    bulk_commit_group();
   }
 };
 
 struct ProjEpilogue {
   ProjEpilogueArgs a;
+  CUtensorMap map_out;  // F32 [rows][embed], box 32 x 128
+
+  // cbuf: [0, 128) bias (0 when absent), [128, 256) ls1 (1 when absent).
+  __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const {
+    if (t < 128)
+      cbuf[t] = a.bias ? a.bias[n0 + t] : 0.0f;
+    else
+      cbuf[t] = a.ls1 ? a.ls1[n0 + t - 128] : 1.0f;
+  }
+
   template <int BN>
-  __device__ __forceinline__ void run(uint32_t tmem_row, int grow, bool valid, int n0) const {
+  __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
+                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+    static_assert(BN == 128, "projection tiles are 128 columns wide");
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int j = 0; j < 2; ++j) {
+      const int chunk = half * 2 + j;  // 32 columns
       float x[32];
-      tmem_ld32(tmem_row + c * 32, x);
-      if (!valid) continue;
-      const int n = n0 + c * 32;
-      const size_t off = static_cast<size_t>(grow) * a.embed + n;
+      tmem_ld32(tmem_row + chunk * 32, x);
+      if (valid) {
+        const float* bias = cbuf + chunk * 32;
+        const float* ls1 = cbuf + 128 + chunk * 32;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float y = x[i] + (a.bias ? __ldg(a.bias + n + i) : 0.f);
-        if (a.ls1) y *= __ldg(a.ls1 + n + i);
-        x[i] = y;
-      }
-      if (a.residual) {
-        const float4* r = reinterpret_cast<const float4*>(a.residual + off);
+        for (int i = 0; i < 32; ++i) x[i] = (x[i] + bias[i]) * ls1[i];
+        if (a.residual) {
+          const float4* res = reinterpret_cast<const float4*>(
+              a.residual + static_cast<size_t>(m0 + r) * a.embed + n0 + chunk * 32);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 rv = r[i];
-          x[4 * i] += rv.x;
-          x[4 * i + 1] += rv.y;
-          x[4 * i + 2] += rv.z;
-          x[4 * i + 3] += rv.w;
+          for (int i = 0; i < 8; ++i) {
+            const float4 v = res[i];
+            x[4 * i] += v.x;
+            x[4 * i + 1] += v.y;
+            x[4 * i + 2] += v.z;
+            x[4 * i + 3] += v.w;
+          }
         }
       }
-      float4* d = reinterpret_cast<float4*>(a.out + off);
+      const uint32_t tile = out_smem + chunk * kOutTileBytes;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
+      for (int c = 0; c < 8; ++c)
+        st_shared_v4(tile + sw128_offset(r, c),
+                     make_uint4(__float_as_uint(x[4 * c]), __float_as_uint(x[4 * c + 1]),
+                                __float_as_uint(x[4 * c + 2]), __float_as_uint(x[4 * c + 3])));
     }
+  }
+
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+    for (int j = 0; j < 2; ++j) {
+      const int chunk = half * 2 + j;
+      tma_store_2d(&map_out, out_smem + chunk * kOutTileBytes, n0 + chunk * 32, m0);
+    }
+    bulk_commit_group();
   }
 };
 
@@ -176,7 +235,10 @@ struct GemmSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kBarOffset = STAGES * kStageBytes;
-  static constexpr uint32_t kBytes = kBarOffset + 256;  // barriers + tmem slot + flags
+  static constexpr uint32_t kConstOffset = kBarOffset + 256;  // after barriers + tmem slot + flags
+  static constexpr uint32_t kBytes = kConstOffset + 2048;     // per-column epilogue constants
+  // The epilogue's output tiles reuse the operand ring once the accumulator is final.
+  static_assert(4 * kOutTileBytes <= STAGES * kStageBytes, "ring too small for the output tiles");
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;  // slack for 1024-B alignment
 };
 
@@ -190,9 +252,10 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 }
 
 template <int BN, int STAGES, class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 2)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a,
-                     const __grid_constant__ CUtensorMap map_b, int M, int K, Epi epi, int* err) {
+                     const __grid_constant__ CUtensorMap map_b, int M, int K,
+                     const __grid_constant__ Epi epi, int* err) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -274,15 +337,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_commit(accum_bar);
     }
   } else {
+    // Epilogue warps 2..9.  Every one of them reaches both named barriers: the
+    // accumulator wait is bounded and nothing else waits in between.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
     const int row = quad * 32 + lane;
+    float* cbuf = reinterpret_cast<float*>(smem + L::kConstOffset);
+    epi.stage(cbuf, n0, threadIdx.x - 64);
+    named_bar_sync(1, 256);
     bool ok = mbar_wait(accum_bar, 0, abort_flag, err, kDevTimeoutConsumer);
     ok = __all_sync(0xffffffffu, ok);  // reconverge: tcgen05.ld is warp-collective
     if (ok) {
       if (lane == 0) *accum_seen = 1;
       tc_fence_after();
-      epi.template run<BN>(tmem + (static_cast<uint32_t>(quad * 32) << 16), m0 + row,
-                           (m0 + row) < M, n0);
+      epi.template run<BN>(tmem + (static_cast<uint32_t>(quad * 32) << 16), row, m0, n0, half, cbuf,
+                           base_u32, (m0 + row) < M);
+    }
+    fence_proxy_async_smem();  // the tiles written above are read by the TMA store
+    named_bar_sync(2 + half, 128);
+    if (ok && ((warp - 2) & 3) == 0 && lane == 0) {
+      epi.store(half, m0, n0, base_u32);
+      bulk_wait_all();  // the ring may not be released while the store reads it
     }
   }
 
@@ -322,16 +397,23 @@ cudaError_t launch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, i
 
 cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t, int rows,
                             int embed, const QkvEpilogueArgs& epi, int* err, cudaStream_t st) {
-  if (embed % 256 != 0) return cudaErrorInvalidValue;
-  QkvEpilogue e{epi};
-  return launch_gemm<256, 4>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
+  if (embed % 256 != 0 || epi.embed != embed || epi.rows != rows) return cudaErrorInvalidValue;
+  QkvEpilogue e{};
+  e.a = epi;
+  if (!encode_tma_2d_bf16(&e.map_out[0], epi.q_out, embed, rows, 64, kBM) ||
+      !encode_tma_2d_bf16(&e.map_out[1], epi.k_out, embed, rows, 64, kBM) ||
+      !encode_tma_2d_bf16(&e.map_out[2], epi.v_out, embed, rows, 64, kBM))
+    return cudaErrorInvalidValue;
+  return launch_gemm<256, 2>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
 }
 
 cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
                              const ProjEpilogueArgs& epi, int* err, cudaStream_t st) {
-  if (n % 128 != 0 || epi.embed != n) return cudaErrorInvalidValue;
-  ProjEpilogue e{epi};
-  return launch_gemm<128, 4>(a, w_t, m, n, k, e, err, st);
+  if (n % 128 != 0 || epi.embed != n || epi.rows != m) return cudaErrorInvalidValue;
+  ProjEpilogue e{};
+  e.a = epi;
+  if (!encode_tma_2d_f32(&e.map_out, epi.out, n, m, 32, kBM)) return cudaErrorInvalidValue;
+  return launch_gemm<128, 3>(a, w_t, m, n, k, e, err, st);
 }
 
 }  // namespace va

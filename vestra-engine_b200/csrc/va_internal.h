@@ -80,6 +80,9 @@ inline int flash_part_slots(int sms) { return 2 * 4 * sms; }
 // Tensor-map encoding through the driver entry point (no -lcuda needed).
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer);
+// Same for F32 [outer][inner] (used by TMA stores of F32 output tiles).
+bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint32_t box_inner, uint32_t box_outer);
 bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                         uint32_t b0, uint32_t b1, uint32_t b2);
 

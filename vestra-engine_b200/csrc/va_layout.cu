@@ -51,6 +51,20 @@ bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint32_t box_inner, uint32_t box_outer) {
+  if (!get_encode()) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (inner * 4) % 16 != 0) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * 4};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                         uint32_t b0, uint32_t b1, uint32_t b2) {
   if (!get_encode()) return false;
