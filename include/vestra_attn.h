@@ -143,12 +143,21 @@ int va_op_attention_noalloc(const float* q, const float* k, const float* v, int 
 
 /* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
  * add the query-sharded global block: each rank owns an equal contiguous slice of
- * the view-major window, forms K'/V for it, and one in-place NCCL all-gather
- * assembles the window before the fused attention.  Local blocks need no
- * communication when each rank's slice holds whole views. */
+ * the view-major window and forms K'/V for it; the window is then assembled on
+ * every rank before the fused attention.  Local blocks need no communication when
+ * each rank's slice holds whole views. */
 /* Rank 0 creates the 128-byte communicator id and sends it to the other ranks. */
 int va_comm_unique_id(void* id_out);
+/* Collective.  Creates the NCCL communicator, then maps every peer's key/value
+ * window into this process (CUDA IPC, up to 8 ranks).  When every rank mapped
+ * every peer, K'/V are exchanged directly: the QKV GEMM's epilogue stores each
+ * finished K'/V tile into every peer's window over NVLink and a one-warp barrier
+ * kernel (release/acquire flags at system scope, bounded wait) closes the step.
+ * Otherwise, or with VA_KV_EXCHANGE=nccl in every rank's environment, an in-place
+ * NCCL all-gather assembles the window. */
 int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
+/* 0: no communicator, 1: NCCL all-gather, 2: direct peer stores. */
+int va_comm_exchange_mode(const va_ctx* ctx);
 /* ln1_local/out_local: device F32 [local_rows, E], this rank's rows
  * [rank*local_rows, (rank+1)*local_rows) of a window of nranks*local_rows tokens
  * made of view_count views.  Collective: every rank calls it for the same layer. */

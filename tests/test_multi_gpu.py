@@ -3,12 +3,16 @@
 One child process per GPU; rank 0 creates the NCCL unique id and hands it to the
 others through a multiprocessing queue, every rank then projects K'/V for its own
 equal token slice, all-gathers them in place and attends its queries to the whole
-window.  The concatenated rank outputs must match the single-GPU sub-block (same
-kernels; only the split of the single launch's last wave rounds differently) and
-meet the oracle gates on a row sample.
+window.  K'/V travel either by direct peer stores from the QKV epilogue (the
+default when every rank can map every peer's window) or by an NCCL all-gather
+(VA_KV_EXCHANGE=nccl); both must give the same result.  The concatenated rank
+outputs must match the single-GPU sub-block (same kernels; only the split of the
+single launch's last wave rounds differently) and meet the oracle gates on a row
+sample.
 Skipped when fewer GPUs than ranks are visible.
 """
 import multiprocessing as mp
+import os
 import queue
 
 import numpy as np
@@ -31,8 +35,10 @@ def _config(wl):
                              max_rows=wl.rows, depth=12, rope_start=4, qknorm_start=4)
 
 
-def _rank_main(rank, nranks, ids, results):
+def _rank_main(rank, nranks, exchange, ids, results):
     try:
+        if exchange == "nccl":
+            os.environ["VA_KV_EXCHANGE"] = "nccl"
         torch.cuda.set_device(rank)
         wl = syn.CONFIGS[WORKLOAD]
         row0, local = va.shard_rows(wl.rows, nranks, rank)
@@ -45,35 +51,44 @@ def _rank_main(rank, nranks, ids, results):
         else:
             uid = ids.get(timeout=TIMEOUT_S / 2)
         ctx.comm_init(uid, nranks, rank)
+        mode = ctx.exchange_mode()
         x = syn.hidden_states(wl.rows, wl.embed, seed=3)[row0:row0 + local]
         ln1 = torch.from_numpy(np.ascontiguousarray(x)).cuda()
         out = torch.empty_like(ln1)
-        for _ in range(2):  # the second call reuses the communicator and workspace
+        # Three calls: the direct exchange alternates between two window pairs, so the
+        # third call reuses the first call's pair on every rank.
+        outs = []
+        for _ in range(3):
             ctx.attention_device_sharded(LAYER, ln1, out, wl.gh, wl.gw, wl.views, True, stream=0)
-        torch.cuda.synchronize()
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy())
         ctx.check_device()
-        results.put((rank, "ok", out.cpu().numpy()))
+        same = all(np.array_equal(outs[0], o) for o in outs[1:])
+        results.put((rank, "ok" if same else "calls differ", (mode, outs[-1])))
         ctx.close()
     except Exception as e:  # reported to the parent, which fails the test
         results.put((rank, f"error: {e!r}", None))
 
 
+@pytest.mark.parametrize("exchange", ["direct", "nccl"])
 @pytest.mark.parametrize("nranks", [2, 4, 8])
-def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks):
+def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks, exchange):
     if torch.cuda.device_count() < nranks:
         pytest.skip(f"needs {nranks} GPUs")
     wl = syn.CONFIGS[WORKLOAD]
     mpc = mp.get_context("spawn")
     ids, results = mpc.Queue(), mpc.Queue()
-    procs = [mpc.Process(target=_rank_main, args=(r, nranks, ids, results)) for r in range(nranks)]
+    procs = [mpc.Process(target=_rank_main, args=(r, nranks, exchange, ids, results)) for r in range(nranks)]
     for p in procs:
         p.start()
     outs = {}
     try:
         for _ in range(nranks):
-            rank, status, arr = results.get(timeout=TIMEOUT_S)
+            rank, status, payload = results.get(timeout=TIMEOUT_S)
             assert status == "ok", f"rank {rank}: {status}"
-            outs[rank] = arr
+            mode, outs[rank] = payload
+            assert mode == exchange, f"rank {rank} exchanged K'/V by {mode}"
+
     except queue.Empty:
         pytest.fail("a rank did not report within the time limit")
     finally:

@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -41,6 +42,7 @@ struct LayerWeights {
 
 constexpr int kMaxHostChunks = 32;
 constexpr int kPhases = 5;
+constexpr int kArenaWindows = 6;  // three key/value window pairs
 
 struct PosKey {
   int64_t rows = -1;
@@ -62,6 +64,14 @@ struct va_ctx {
   __nv_bfloat16* q = nullptr;  // [cap][E] this rank's queries, token-major
   __nv_bfloat16* k = nullptr;  // [cap][E] key window (all ranks' slices after the gather)
   __nv_bfloat16* v = nullptr;  // [cap][E]
+  // One allocation holds three key/value window pairs and the exchange flags, so
+  // one IPC handle maps all of it into the peer processes.  Pair 0 (k, v) is this
+  // rank's own (single-GPU and local calls); the direct K'/V exchange alternates
+  // between pairs 1 and 2 call by call, so a peer only ever writes the pair this
+  // rank read two sharded calls ago and never one another call is using.
+  void* kv_arena = nullptr;
+  size_t win_bytes = 0;
+  int* xflags = nullptr;       // [kMaxRanks] exchange flags, written by the peers
   __nv_bfloat16* o = nullptr;  // [cap][E] attention output, token-major
   float* in_f32 = nullptr;     // host-path staging [cap][E]
   float* out_f32 = nullptr;
@@ -91,6 +101,10 @@ struct va_ctx {
   int2* op_pos = nullptr;
   size_t op_pos_cap = 0;
   va::Comm* comm = nullptr;    // set by va_comm_init (multi-GPU global blocks)
+  // direct K'/V exchange over NVLink (va_comm_init; else NCCL all-gather)
+  bool p2p = false;
+  int epoch = 0;
+  void* peer_arena[va::kMaxRanks] = {};
   std::string last_error;
 };
 
@@ -259,6 +273,11 @@ struct BranchSpec {
   const int2* pos;        // positions of the window (nullptr: no RoPE)
   int seg_len;            // 0: global attention over the window; > 0: per-view segments
   bool gather;            // all-gather K/V slices of every rank before the attention
+  __nv_bfloat16* kwin;    // key / value window buffers of this call
+  __nv_bfloat16* vwin;
+  int npeer;              // direct exchange: peers whose windows receive this slice
+  __nv_bfloat16* peer_k[va::kMaxPeers];
+  __nv_bfloat16* peer_v[va::kMaxPeers];
 };
 
 // In-place all-gather of this rank's K'/V slices into the window buffers.
@@ -273,6 +292,87 @@ int gather_kv(va_ctx* c, const __nv_bfloat16* k_slice, const __nv_bfloat16* v_sl
   if (!va::comm_allgather_inplace2(c->comm, c->k, c->v, per_rank, st, &err))
     return fail(c, VA_ERR_NCCL, err);
   return VA_OK;
+}
+
+void close_peers(va_ctx* c) {
+  for (int r = 0; r < va::kMaxRanks; ++r) {
+    if (c->peer_arena[r]) cudaIpcCloseMemHandle(c->peer_arena[r]);
+    c->peer_arena[r] = nullptr;
+  }
+  c->p2p = false;
+}
+
+// Maps every peer's kv_arena into this process (CUDA IPC) for the direct K'/V
+// exchange.  Every rank's outcome is all-gathered and the direct exchange is used
+// only when every rank mapped every peer; otherwise the NCCL all-gather stays in
+// use.  VA_KV_EXCHANGE=nccl forces the all-gather.  The flags are cleared before
+// the first collective, so no peer can have written one yet.
+int setup_peers(va_ctx* c) {
+  close_peers(c);
+  c->epoch = 0;
+  VA_CUDA(c, cudaMemset(c->xflags, 0, 256));
+  VA_CUDA(c, cudaDeviceSynchronize());
+  const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
+  if (nranks < 2 || nranks > va::kMaxRanks) return VA_OK;
+  const char* env = std::getenv("VA_KV_EXCHANGE");
+  const bool forced_nccl = env && std::string(env) == "nccl";
+  struct Slot {
+    cudaIpcMemHandle_t h;
+    int ok;
+    int pad;
+    unsigned long long win_bytes;  // every rank's arena must have the same layout
+    int pad2[12];
+  };
+  static_assert(sizeof(Slot) == 128, "slot size");
+  Slot mine{};
+  mine.ok = 0;
+  mine.win_bytes = c->win_bytes;
+  if (!forced_nccl) {
+    mine.ok = cudaIpcGetMemHandle(&mine.h, c->kv_arena) == cudaSuccess;
+    if (!mine.ok) cudaGetLastError();
+  }
+  Slot* dbuf = nullptr;
+  VA_CUDA(c, dmalloc(&dbuf, static_cast<size_t>(nranks) + 1));
+  std::vector<Slot> all(nranks);
+  std::string err;
+  int rc = VA_OK;
+  cudaError_t e = cudaMemcpy(dbuf + nranks, &mine, sizeof(Slot), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && !va::comm_allgather_bytes(c->comm, dbuf + nranks, dbuf, sizeof(Slot), c->stream, &err))
+    rc = fail(c, VA_ERR_NCCL, err);
+  if (e == cudaSuccess && rc == VA_OK) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess && rc == VA_OK)
+    e = cudaMemcpy(all.data(), dbuf, sizeof(Slot) * nranks, cudaMemcpyDeviceToHost);
+  int opened = rc == VA_OK && e == cudaSuccess;
+  for (int r = 0; opened && r < nranks; ++r) {
+    if (!all[r].ok || all[r].win_bytes != c->win_bytes) opened = 0;
+    if (!opened || r == rank) continue;
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, all[r].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      opened = 0;
+    } else {
+      c->peer_arena[r] = p;
+    }
+  }
+  // Second round: the direct exchange only if every rank mapped every peer.
+  if (rc == VA_OK) {
+    std::vector<Slot> flags(nranks);
+    Slot f{};
+    f.ok = opened;
+    e = cudaMemcpy(dbuf + nranks, &f, sizeof(Slot), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && !va::comm_allgather_bytes(c->comm, dbuf + nranks, dbuf, sizeof(Slot), c->stream, &err))
+      rc = fail(c, VA_ERR_NCCL, err);
+    if (e == cudaSuccess && rc == VA_OK) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess && rc == VA_OK)
+      e = cudaMemcpy(flags.data(), dbuf, sizeof(Slot) * nranks, cudaMemcpyDeviceToHost);
+    bool all_ok = e == cudaSuccess && rc == VA_OK;
+    for (int r = 0; all_ok && r < nranks; ++r) all_ok = flags[r].ok != 0;
+    c->p2p = all_ok;
+  }
+  cudaFree(dbuf);
+  if (!c->p2p) close_peers(c);
+  if (rc == VA_OK && e != cudaSuccess) rc = cuda_fail(c, e, "peer window exchange");
+  return rc;
 }
 
 int segments_for(va_ctx* c, int64_t rows, int view_count, int global, int* seg_len) {
@@ -293,6 +393,7 @@ void set_split_workspace(const va_ctx* c, va::FlashArgs* fa) {
 
 int validate_branch(va_ctx* c, int layer, const BranchSpec& b) {
   const LayerWeights& w = c->layers[layer];
+  if (!b.in || !b.out || !b.kwin || !b.vwin) return fail(c, VA_ERR_INVALID, "missing buffer");
   if (b.rows <= 0 || b.window_rows > c->cap || b.row_offset + b.rows > b.window_rows)
     return fail(c, VA_ERR_INVALID, "rows exceed the context's max_rows");
   if (b.window_rows > 0x7fffffff / 64) return fail(c, VA_ERR_INVALID, "rows too large");
@@ -327,8 +428,13 @@ int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1,
   qa.rope_cs = c->rope_cs;
   qa.rope_pairing = c->cfg.rope_pairing;
   qa.q_out = c->q + r0 * E;
-  qa.k_out = c->k + (b.row_offset + r0) * E;
-  qa.v_out = c->v + (b.row_offset + r0) * E;
+  qa.k_out = b.kwin + (b.row_offset + r0) * E;
+  qa.v_out = b.vwin + (b.row_offset + r0) * E;
+  qa.npeer = b.npeer;
+  for (int p = 0; p < b.npeer; ++p) {
+    qa.peer_k[p] = b.peer_k[p] + (b.row_offset + r0) * E;
+    qa.peer_v[p] = b.peer_v[p] + (b.row_offset + r0) * E;
+  }
   qa.rows = n;
   qa.embed = E;
   // V (and so P) stay bf16: measured faster on B200 than an f16 P formed with
@@ -355,12 +461,12 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
   fa.o_tok = c->o + q0 * E;
   fa.embed = E;
   fa.v_f16 = 0;
-  const __nv_bfloat16* kk = c->k;
-  const __nv_bfloat16* vv = c->v;
+  const __nv_bfloat16* kk = b.kwin;
+  const __nv_bfloat16* vv = b.vwin;
   if (b.seg_len > 0) {
     // Local blocks: every key a query needs lives in its own view.
-    kk = c->k + (b.row_offset + q0) * E;
-    vv = c->v + (b.row_offset + q0) * E;
+    kk = b.kwin + (b.row_offset + q0) * E;
+    vv = b.vwin + (b.row_offset + q0) * E;
     fa.q_offset = 0;
     fa.kv_rows = n;
   } else {
@@ -382,9 +488,34 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
 }
 
 // The device launch sequence of one attention sub-block (see the file header).
-int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
-  int rc = validate_branch(c, layer, b);
+int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
+  int rc = validate_branch(c, layer, b_in);
   if (rc) return rc;
+  BranchSpec b = b_in;
+  const bool direct = b.gather && c->p2p;
+  va::PeerBarrierArgs pb{};
+  if (direct) {
+    // Direct exchange: this call's window pair, and every peer's copy of it.
+    const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
+    const int set = 1 + ((++c->epoch) & 1);  // window pair 1 or 2
+    const size_t win = c->win_bytes;
+    char* own = static_cast<char*>(c->kv_arena);
+    b.kwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set) * win);
+    b.vwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set + 1) * win);
+    b.npeer = 0;
+    pb.local_flags = c->xflags;
+    pb.nranks = nranks;
+    pb.rank = rank;
+    pb.epoch = c->epoch;
+    for (int r = 0; r < nranks; ++r) {
+      if (r == rank) continue;
+      char* pa = static_cast<char*>(c->peer_arena[r]);
+      b.peer_k[b.npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set) * win);
+      b.peer_v[b.npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set + 1) * win);
+      ++b.npeer;
+      pb.peer_flags[r] = reinterpret_cast<int*>(pa + kArenaWindows * win);
+    }
+  }
   // With the phase profile on, an event goes between every two launches; the ln
   // and qkv phases are split inside stage_qkv's two launches by mark(1).
   const bool prof = c->phase_profile;
@@ -393,7 +524,9 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b, cudaStream_t st) {
   VA_CUDA(c, mark(0));
   if ((rc = stage_qkv(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[1] : nullptr))) return rc;
   VA_CUDA(c, mark(2));
-  if (b.gather) {
+  if (direct) {
+    VA_CUDA(c, va::launch_peer_barrier(pb, c->err, st));
+  } else if (b.gather) {
     const int E = c->cfg.embed_dim;
     if ((rc = gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st))) return rc;
   }
@@ -464,8 +597,16 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   const size_t n = static_cast<size_t>(c->cap) * E;
   if ((e = dmalloc(&c->x, n)) != cudaSuccess) return bail(e);
   if ((e = dmalloc(&c->q, n)) != cudaSuccess) return bail(e);
-  if ((e = dmalloc(&c->k, n)) != cudaSuccess) return bail(e);
-  if ((e = dmalloc(&c->v, n)) != cudaSuccess) return bail(e);
+  {
+    const size_t win = n * sizeof(__nv_bfloat16);
+    if ((e = cudaMalloc(&c->kv_arena, kArenaWindows * win + 256)) != cudaSuccess) return bail(e);
+    char* a = static_cast<char*>(c->kv_arena);
+    c->win_bytes = win;
+    c->k = reinterpret_cast<__nv_bfloat16*>(a);
+    c->v = reinterpret_cast<__nv_bfloat16*>(a + win);
+    c->xflags = reinterpret_cast<int*>(a + kArenaWindows * win);
+    if ((e = cudaMemset(c->xflags, 0, 256)) != cudaSuccess) return bail(e);
+  }
   if ((e = dmalloc(&c->o, n)) != cudaSuccess) return bail(e);
   if ((e = dmalloc(&c->in_f32, n)) != cudaSuccess) return bail(e);
   if ((e = dmalloc(&c->out_f32, n)) != cudaSuccess) return bail(e);
@@ -504,8 +645,9 @@ void va_destroy(va_ctx* c) {
   for (auto& l : c->layers) free_layer(l);
   dfree(c->x);
   dfree(c->q);
-  dfree(c->k);
-  dfree(c->v);
+  close_peers(c);
+  if (c->kv_arena) cudaFree(c->kv_arena);
+  c->kv_arena = nullptr;
   dfree(c->o);
   dfree(c->in_f32);
   dfree(c->out_f32);
@@ -592,7 +734,7 @@ int va_run_attention(va_ctx* c, int layer, const float* input, int64_t rows, int
   }
   const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
   VA_CUDA(c, cudaMemcpyAsync(c->in_f32, input, bytes, cudaMemcpyHostToDevice, c->stream));
-  BranchSpec b{c->in_f32, false, c->out_f32, nullptr, rows, 0, rows, pos, 0, false};
+  BranchSpec b{c->in_f32, false, c->out_f32, nullptr, rows, 0, rows, pos, 0, false, c->k, c->v, 0, {}, {}};
   if ((rc = run_branch(c, layer, b, c->stream))) return rc;
   VA_CUDA(c, cudaMemcpyAsync(out, c->out_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
   VA_CUDA(c, cudaStreamSynchronize(c->stream));
@@ -619,7 +761,7 @@ int make_branch(va_ctx* c, int layer, const float* in, bool apply_ln1, float* ou
     pos = c->pos;
   }
   *b = BranchSpec{in, apply_ln1, out, residual, local_rows, row_offset, window_rows, pos, seg_len,
-                  sharded && global};
+                  sharded && global, c->k, c->v, 0, {}, {}};
   return validate_branch(c, layer, *b);
 }
 
@@ -756,12 +898,19 @@ int va_comm_init(va_ctx* c, const void* id, int nranks, int rank) {
   if (!c || !id || nranks <= 0 || rank < 0 || rank >= nranks) return VA_ERR_INVALID;
   VA_CUDA(c, cudaSetDevice(c->device));
   if (c->comm) {
+    close_peers(c);
     va::comm_destroy(c->comm, false);
     c->comm = nullptr;
   }
   std::string err;
   c->comm = va::comm_init(id, nranks, rank, &err);
-  return c->comm ? VA_OK : fail(c, VA_ERR_NCCL, err);
+  if (!c->comm) return fail(c, VA_ERR_NCCL, err);
+  return setup_peers(c);
+}
+
+int va_comm_exchange_mode(const va_ctx* c) {
+  if (!c || !c->comm) return 0;
+  return c->p2p ? 2 : 1;
 }
 
 int va_attention_device_sharded(va_ctx* c, int layer, const float* ln1_local, float* out_local,

@@ -158,6 +158,21 @@ bool comm_allgather_inplace2(Comm* c, void* buf_a, void* buf_b, size_t count_per
   return true;
 }
 
+bool comm_allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStream_t st,
+                          std::string* err) {
+  const NcclApi* a = api();
+  if (!a) {
+    *err = g_api.error;
+    return false;
+  }
+  const ncclResult_t r = a->AllGather(send, recv, bytes, ncclUint8, c->comm, st);
+  if (r != ncclSuccess) {
+    *err = nccl_msg(a, r, "ncclAllGather");
+    return false;
+  }
+  return true;
+}
+
 bool comm_async_error(Comm* c, std::string* err) {
   const NcclApi* a = api();
   if (!a || !c) return false;

@@ -19,6 +19,10 @@ int comm_size(const Comm* c);
 // count_per_rank elements; this rank's slice is already in place.
 bool comm_allgather_inplace2(Comm* c, void* buf_a, void* buf_b, size_t count_per_rank,
                              cudaStream_t st, std::string* err);
+// All-gather of `bytes` bytes per rank: recv (device) receives nranks slices in rank
+// order; send (device) holds this rank's slice.
+bool comm_allgather_bytes(Comm* c, const void* send, void* recv, size_t bytes, cudaStream_t st,
+                          std::string* err);
 // True when the communicator reports an asynchronous failure (message in *err).
 bool comm_async_error(Comm* c, std::string* err);
 

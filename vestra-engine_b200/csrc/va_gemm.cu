@@ -161,6 +161,34 @@ struct QkvEpilogue {
     }
   }
 
+  // Direct K'/V exchange: the 128 threads of `half` copy this half's two output
+  // tiles (K or V section) row-major from shared memory into every peer's window,
+  // rows < M only (the rows past M belong to the next rank's slice there).  Each
+  // warp instruction covers 4 whole 128-byte rows.  Fenced at system scope.
+  __device__ __forceinline__ void peer_copy(int half, int t, int m0, int M, int n0,
+                                            uint32_t out_smem) const {
+    const int section = n0 / a.embed;
+    if (a.npeer == 0 || section == 0) return;
+    const int h0 = (n0 - section * a.embed) / 64;
+    const int chunk = t & 7;
+    for (int j = 0; j < 2; ++j) {
+      const int hh = half * 2 + j;
+      const uint32_t tile = out_smem + hh * kOutTileBytes;
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i) {
+        const int r = (t >> 3) + 16 * i;
+        if (m0 + r >= M) break;
+        const uint4 v = ld_shared_v4(tile + sw128_offset(r, chunk));
+        const size_t off = static_cast<size_t>(m0 + r) * a.embed + (h0 + hh) * 64 + chunk * 8;
+        for (int p = 0; p < a.npeer; ++p) {
+          __nv_bfloat16* dst = (section == 1 ? a.peer_k[p] : a.peer_v[p]) + off;
+          *reinterpret_cast<uint4*>(dst) = v;
+        }
+      }
+    }
+    __threadfence_system();
+  }
+
   __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
     const int section = n0 / a.embed;
     const int h0 = (n0 - section * a.embed) / 64;
@@ -219,6 +247,8 @@ struct ProjEpilogue {
                                 __float_as_uint(x[4 * c + 2]), __float_as_uint(x[4 * c + 3])));
     }
   }
+
+  __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
 
   __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
     for (int j = 0; j < 2; ++j) {
@@ -359,6 +389,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
       epi.store(half, m0, n0, base_u32);
       bulk_wait_all();  // the ring may not be released while the store reads it
     }
+    if (ok) epi.peer_copy(half, threadIdx.x - 64 - 128 * half, m0, M, n0, base_u32);
   }
 
   tc_fence_before();

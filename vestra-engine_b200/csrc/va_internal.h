@@ -11,6 +11,9 @@
 namespace va {
 
 // ---- QKV projection (K1): X[rows,E] bf16 x Wqkv^T -> Q,K,V token-major bf16 ----
+constexpr int kMaxRanks = 8;
+constexpr int kMaxPeers = kMaxRanks - 1;
+
 struct QkvEpilogueArgs {
   const float* bias;                  // [3E]
   const float* q_g; const float* q_b;  // [64] QK-norm (nullptr: no QK-norm)
@@ -25,7 +28,22 @@ struct QkvEpilogueArgs {
   int rows;
   int embed;
   int v_f16;                           // store V as f16 (the PV UMMA then runs in f16)
+  // Direct K'/V exchange: the same rows of K' and V are also stored into these
+  // peer GPUs' window buffers (their slice of this rank, over NVLink).
+  int npeer = 0;
+  __nv_bfloat16* peer_k[kMaxPeers] = {};
+  __nv_bfloat16* peer_v[kMaxPeers] = {};
 };
+
+// Barrier of the direct K'/V exchange: this rank tells every peer that its slice
+// has arrived there (flag = epoch in the peer's flag array at index `rank`) and
+// waits until every peer has told it the same.
+struct PeerBarrierArgs {
+  int* local_flags;            // [kMaxRanks], written by the peers
+  int* peer_flags[kMaxRanks];  // each peer's flag array (nullptr at index rank)
+  int nranks, rank, epoch;
+};
+cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, int* err, cudaStream_t st);
 
 // ---- output projection (K3): O[rows,E] bf16 x Wp^T + b (* ls1) (+ residual) -> F32 ----
 struct ProjEpilogueArgs {

@@ -39,7 +39,7 @@ bool get_encode() {
 
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer) {
-  if (!get_encode()) return false;
+  if (!get_encode() || base == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (inner * 2) % 16 != 0) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 2};
@@ -53,7 +53,7 @@ bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint
 
 bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                        uint32_t box_inner, uint32_t box_outer) {
-  if (!get_encode()) return false;
+  if (!get_encode() || base == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (inner * 4) % 16 != 0) return false;
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * 4};
@@ -67,7 +67,7 @@ bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
 
 bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                         uint32_t b0, uint32_t b1, uint32_t b2) {
-  if (!get_encode()) return false;
+  if (!get_encode() || base == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (d0 * 2) % 16 != 0) return false;
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
@@ -268,6 +268,37 @@ __global__ void bounded_wait_selftest_kernel(unsigned long long limit_ns, int* e
   __syncthreads();
   if (threadIdx.x == 0) mbar_wait_for(b, 0, &abort_flag, err, kDevTimeoutConsumer, limit_ns);
   __syncthreads();
+}
+
+// Direct K'/V exchange barrier, one warp: lane r publishes this rank's epoch to
+// peer r, then waits (bounded) for peer r's epoch here.  The QKV kernel before it
+// fenced its peer stores at system scope; the release/acquire pair orders them
+// before the peer's attention kernel reads them.
+constexpr unsigned long long kPeerWaitNs = 2000000000ull;
+
+__global__ void peer_barrier_kernel(PeerBarrierArgs a, int* err) {
+  const int r = threadIdx.x;
+  const bool peer = r < a.nranks && r != a.rank;
+  if (peer) {
+    __threadfence_system();
+    st_release_sys(a.peer_flags[r] + a.rank, a.epoch);
+  }
+  __syncwarp();
+  if (peer) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_sys(a.local_flags + r) < a.epoch) {
+      if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        report_error(err, kDevTimeoutPeer);
+        break;
+      }
+    }
+  }
+}
+
+cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, int* err, cudaStream_t st) {
+  if (a.nranks < 1 || a.nranks > kMaxRanks || a.rank < 0 || a.rank >= a.nranks) return cudaErrorInvalidValue;
+  peer_barrier_kernel<<<1, 32, 0, st>>>(a, err);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns, int* err, cudaStream_t st) {

@@ -24,6 +24,7 @@ enum DevError : int {
   kDevTimeoutMma = 2,       // MMA issuer gave up waiting for operands / P
   kDevTimeoutConsumer = 3,  // softmax / epilogue gave up waiting for the accumulator
   kDevBadShape = 4,         // a kernel saw a shape its host checks should have rejected
+  kDevTimeoutPeer = 5,      // the K'/V exchange barrier gave up waiting for a peer GPU
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -114,6 +115,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+
+// System-scope flag access (another GPU writes or reads the flag over NVLink).
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // Named barrier `id` (1..15) over `count` threads (a multiple of 32).

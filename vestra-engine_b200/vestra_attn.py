@@ -36,7 +36,8 @@ EXPORTED = [
     "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
-    "va_comm_unique_id", "va_comm_init", "va_attention_device_sharded", "va_op_attention_noalloc",
+    "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
+    "va_op_attention_noalloc",
 ]
 
 
@@ -90,6 +91,7 @@ def load_library(path: str = LIB_PATH):
                                     c_int),
         "va_comm_unique_id": ([_vp], c_int),
         "va_comm_init": ([_vp, _vp, c_int, c_int], c_int),
+        "va_comm_exchange_mode": ([_vp], c_int),
         "va_attention_device_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_op_attention_noalloc": ([_vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float, _vp, c_float,
                                      c_int, _vp, _vp], c_int),
@@ -247,6 +249,10 @@ class Context:
     def comm_init(self, comm_id: bytes, nranks: int, rank: int):
         buf = ctypes.create_string_buffer(bytes(comm_id), 128)
         self.check(self.lib.va_comm_init(self.h, buf, nranks, rank))
+
+    def exchange_mode(self) -> str:
+        """How K'/V reach the other ranks: "none", "nccl" or "direct" (peer stores)."""
+        return ("none", "nccl", "direct")[self.lib.va_comm_exchange_mode(self.h)]
 
     def attention_device_sharded(self, layer, ln1_local, out_local, gh, gw, view_count, global_, stream=0):
         self.check(self.lib.va_attention_device_sharded(self.h, layer, _ptr(ln1_local), _ptr(out_local),
