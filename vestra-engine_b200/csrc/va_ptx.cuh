@@ -71,6 +71,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep (up to hint_ns) until the
+// phase completes instead of spinning, so waiting warps leave their issue slots
+// to the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kWaitSleepHintNs = 20000;
+
 // Waits for the phase with the given parity to complete.  Returns false when the
 // wait timed out (the abort flag and the device error word are then set) or when
 // another thread of the CTA already aborted.
@@ -79,7 +95,7 @@ __device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, vol
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepHintNs)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
