@@ -638,7 +638,9 @@ __global__ void __launch_bounds__(kW20Threads, 1)
           float x0, x1, x2, x3, p0, p1, p2, p3;
           f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k], s[4 * k + 1]), sc2, ng0), x0, x1);
           f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k + 2], s[4 * k + 3]), sc2, ng1), x2, x3);
-          if (!tail && (k & 7) >= 8 - kPoly) {
+          // Column blocks k with k mod 8 < kPoly go to the FMA pipe; they come first
+          // so their dependency chains overlap the MUFU work of the later blocks.
+          if (!tail && (k & 7) < kPoly) {
             exp2_fma_x2(x0, x1, p0, p1);
             exp2_fma_x2(x2, x3, p2, p3);
           } else {
