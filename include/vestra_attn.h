@@ -141,6 +141,31 @@ int va_op_attention_noalloc(const float* q, const float* k, const float* v, int 
                             const float* pos_yx_dev, float freq, int rope_pairing, float* out,
                             void* stream);
 
+/* Transformer tail (SURVEY next row 1): the MLP sub-block and the whole block.
+ * va_load_mlp replaces the CudaMlpExecutor weight upload (vit_block.rs:190-236):
+ * norm2_w/b [E], fc1_w [E, mlp_hidden] and fc1_b [mlp_hidden], fc2_w [mlp_hidden, E]
+ * and fc2_b [E] in the reference's [in, out] orientation, ls2 [E] or NULL
+ * (presence-gated); mlp_hidden a multiple of 256 (4E for DA3).  The library copies
+ * and converts the matrices to bf16. */
+int va_load_mlp(va_ctx* ctx, int layer, int mlp_hidden, const float* norm2_w, const float* norm2_b,
+                const float* fc1_w, const float* fc1_b, const float* fc2_w, const float* fc2_b,
+                const float* ls2);
+/* run_tail_device (vit_block.rs:489-583): one whole block in place on device tokens
+ * F32 [rows, E]: x += proj(attention(LN1 x)) (*ls1); x += fc2(GELU_erf(fc1(LN2 x)))
+ * (*ls2) (vit_block.rs:1019-1139).  Needs va_load_layer with norm1 and va_load_mlp. */
+int va_block_device(va_ctx* ctx, int layer, float* tokens_dev, int64_t rows, int gh, int gw,
+                    int view_count, int global, void* stream);
+/* The same block over this rank's token slice of a query-sharded window (global
+ * blocks exchange K'/V as va_attention_device_sharded does; the MLP is
+ * token-local).  Collective for global blocks. */
+int va_block_device_sharded(va_ctx* ctx, int layer, float* tokens_local, int64_t local_rows,
+                            int gh, int gw, int view_count, int global, void* stream);
+/* TransformerTailExecutor::run_tail (vit_block.rs:110-129) with host buffers:
+ * tokens [rows, E] in, updated tokens out (may alias).  The reference's separate
+ * CPU-order LN1 input is not taken: LN1 is computed on the device from tokens. */
+int va_run_tail_host(va_ctx* ctx, int layer, const float* tokens, int64_t rows, int gh, int gw,
+                     int view_count, int global, float* out);
+
 /* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
  * add the query-sharded global block: each rank owns an equal contiguous slice of
  * the view-major window and forms K'/V for it; the window is then assembled on

@@ -550,6 +550,32 @@ int oracle_attention_block(const float* ln1, int64_t rows, int E, int heads, int
 
 // Double-precision naive attention (materialised scores) for small cases; used to
 // check the online-softmax core above.
+// MLP sub-block of one ViT block (vit_block.rs:1092-1129, device form :566-580):
+//   out = x + (GELU(LN2(x) @ fc1_w + fc1_b) @ fc2_w + fc2_b) * ls2
+// with GELU(z) = z/2 * (1 + erf(z / sqrt(2))) (the module doc, vit_block.rs:26),
+// LN2 eps = ln_eps, ls2 presence-gated (null: unscaled).  Weights [in, out].
+// x, out: [rows, E]; they may alias (the residual is read before it is written).
+void oracle_mlp_block(const float* x, int64_t rows, int E, int hidden, const float* n2_g,
+                      const float* n2_b, float ln_eps, const float* fc1_w, const float* fc1_b,
+                      const float* fc2_w, const float* fc2_b, const float* ls2, float* out,
+                      int threads) {
+  threads = resolve_threads(threads);
+  std::vector<float> ln((size_t)rows * E);
+  std::memcpy(ln.data(), x, sizeof(float) * ln.size());
+  layernorm_rows(ln.data(), rows, E, n2_g, n2_b, ln_eps, threads);
+  std::vector<float> h((size_t)rows * hidden);
+  linear(ln.data(), rows, E, fc1_w, hidden, fc1_b, nullptr, h.data(), threads);
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (int64_t i = 0; i < (int64_t)h.size(); ++i) {
+    const float z = h[i];
+    h[i] = 0.5f * z * (1.0f + std::erf(z * 0.70710678118654752f));
+  }
+  std::vector<float> m((size_t)rows * E);
+  linear(h.data(), rows, hidden, fc2_w, E, fc2_b, ls2, m.data(), threads);
+#pragma omp parallel for num_threads(threads) schedule(static)
+  for (int64_t i = 0; i < (int64_t)m.size(); ++i) out[i] = x[i] + m[i];
+}
+
 void oracle_attention_naive_f64(const double* q, const double* k, const double* v, int heads,
                                 int64_t n, int d, int64_t seg_len, double* out) {
   if (seg_len <= 0) seg_len = n;

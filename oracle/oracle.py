@@ -51,6 +51,8 @@ def _load():
                                            _f32p, _f32p, _i64p, c_i64, _f32p, c_int]
     lib.oracle_attention_block.restype = c_int
     lib.oracle_attention_naive_f64.argtypes = [_f64p, _f64p, _f64p, c_int, c_i64, c_int, c_i64, _f64p]
+    lib.oracle_mlp_block.argtypes = [_f32p, c_i64, c_int, c_int, _f32p, _f32p, c_float, _f32p, _f32p,
+                                     _f32p, _f32p, _f32p, _f32p, c_int]
     _lib = lib
     return lib
 
@@ -151,6 +153,31 @@ def attention_block(ln1, layer, heads, pos_yx=None, seg_len=0, rope_freq=100.0, 
     if rc != 0:
         raise ValueError("oracle_attention_block: shape error")
     return out
+
+
+def mlp_block(x, layer, ln_eps=1e-6, threads=0):
+    """MLP sub-block + residual (vit_block.rs:1092-1129): x + (GELU_erf(LN2(x) fc1) fc2) * ls2.
+
+    layer: dict with norm2_w, norm2_b [E], fc1_w [E,H], fc1_b [H], fc2_w [H,E], fc2_b [E],
+    optional ls2 [E] ([in,out] orientation)."""
+    x = _f32(x)
+    rows, E = x.shape
+    hidden = layer["fc1_w"].shape[1]
+    out = np.zeros_like(x)
+    _load().oracle_mlp_block(_p(x), rows, E, hidden, _p(_f32(layer["norm2_w"])), _p(_f32(layer["norm2_b"])),
+                             ln_eps, _p(_f32(layer["fc1_w"])), _p(_f32(layer["fc1_b"])), _p(_f32(layer["fc2_w"])),
+                             _p(_f32(layer["fc2_b"])), _p(_f32(layer.get("ls2"))), _p(out), threads)
+    return out
+
+
+def block(x, layer, heads, pos_yx=None, seg_len=0, ln_eps=1e-6, rope_freq=100.0, qk_norm_eps=1e-5,
+          use_qknorm=True, pairing=0, threads=0):
+    """One whole ViT block (vit_block.rs:1019-1139): x += attention(LN1(x)); x += MLP(x)."""
+    x = _f32(x)
+    ln1 = layernorm(x, layer["norm1_w"], layer["norm1_b"], ln_eps, threads)
+    x1 = x + attention_block(ln1, layer, heads, pos_yx=pos_yx, seg_len=seg_len, rope_freq=rope_freq,
+                             qk_norm_eps=qk_norm_eps, use_qknorm=use_qknorm, pairing=pairing, threads=threads)
+    return mlp_block(x1, layer, ln_eps, threads)
 
 
 def attention_naive_f64(q, k, v, seg_len=0):

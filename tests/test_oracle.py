@@ -218,3 +218,30 @@ def test_qknorm_gating_changes_output(oracle_mod):
     a = oracle_mod.attention_block(x, p, 2, use_qknorm=True)
     b = oracle_mod.attention_block(x, p, 2, use_qknorm=False)
     assert not np.array_equal(a, b)
+
+
+def test_mlp_block_matches_float64_restatement(oracle_mod):
+    # vit_block.rs:1092-1129: x + (GELU_erf(LN2(x) fc1 + b1) fc2 + b2) * ls2, restated
+    # independently in float64 torch (exact erf GELU).
+    torch = pytest.importorskip("torch")
+    x = syn.hidden_states(40, 256, seed=11)
+    for with_ls2 in (False, True):
+        p = syn.layer_weights(256, seed=11, layer=3, mlp=True, ls2=with_ls2)
+        got = oracle_mod.mlp_block(x, p, ln_eps=1e-6)
+        t = lambda a: torch.from_numpy(np.asarray(a, np.float64))  # noqa: E731
+        xt = t(x)
+        ln = torch.nn.functional.layer_norm(xt, (256,), t(p["norm2_w"]), t(p["norm2_b"]), eps=1e-6)
+        h = torch.nn.functional.gelu(ln @ t(p["fc1_w"]) + t(p["fc1_b"]), approximate="none")
+        m = h @ t(p["fc2_w"]) + t(p["fc2_b"])
+        if with_ls2:
+            m = m * t(p["ls2"])
+        ref = (xt + m).numpy()
+        assert np.abs(got - ref).max() <= 2e-5, (with_ls2, np.abs(got - ref).max())
+
+
+def test_mlp_ls2_presence_changes_output(oracle_mod):
+    # LayerScale presence gating holds for ls2 as for ls1 (vit_block.rs:1369-1401).
+    x = syn.hidden_states(16, 256, seed=12)
+    p = syn.layer_weights(256, seed=12, layer=2, mlp=True, ls2=True)
+    q = {k: v for k, v in p.items() if k != "ls2"}
+    assert np.abs(oracle_mod.mlp_block(x, p) - oracle_mod.mlp_block(x, q)).max() > 1e-3

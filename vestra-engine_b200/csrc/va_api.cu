@@ -44,6 +44,19 @@ constexpr int kMaxHostChunks = 32;
 constexpr int kPhases = 5;
 constexpr int kArenaWindows = 6;  // three key/value window pairs
 
+// MLP sub-block of one block (vit_block.rs:131-236): LN2, fc1 (+GELU), fc2 (+ls2).
+struct MlpWeights {
+  bool loaded = false;
+  int hidden = 0;
+  float* norm2_w = nullptr;           // [E]
+  float* norm2_b = nullptr;
+  __nv_bfloat16* w_fc1_t = nullptr;   // [hidden][E]
+  float* fc1_b = nullptr;             // [hidden]
+  __nv_bfloat16* w_fc2_t = nullptr;   // [E][hidden]
+  float* fc2_b = nullptr;             // [E]
+  float* ls2 = nullptr;               // [E] or null
+};
+
 struct PosKey {
   int64_t rows = -1;
   int gh = 0, gw = 0, views = 0, global = 0, n_special = 0;
@@ -59,6 +72,9 @@ struct va_ctx {
   va_config cfg{};
   int device = 0;
   std::vector<LayerWeights> layers;
+  std::vector<MlpWeights> mlps;
+  __nv_bfloat16* hbuf = nullptr;  // MLP hidden activations [cap][hidden_cap] bf16
+  int hidden_cap = 0;
   int64_t cap = 0;  // workspace rows
   __nv_bfloat16* x = nullptr;  // [cap][E] LN1 output, bf16
   __nv_bfloat16* q = nullptr;  // [cap][E] this rank's queries, token-major
@@ -175,6 +191,17 @@ void free_layer(LayerWeights& l) {
   dfree(l.kn_g);
   dfree(l.kn_b);
   l.loaded = false;
+}
+
+void free_mlp(MlpWeights& m) {
+  dfree(m.norm2_w);
+  dfree(m.norm2_b);
+  dfree(m.w_fc1_t);
+  dfree(m.fc1_b);
+  dfree(m.w_fc2_t);
+  dfree(m.fc2_b);
+  dfree(m.ls2);
+  m.loaded = false;
 }
 
 bool layer_use_qknorm(const va_ctx* c, int layer) {
@@ -585,6 +612,7 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   c->cfg = *cfg;
   c->device = device;
   c->layers.resize(cfg->depth);
+  c->mlps.resize(cfg->depth);
   c->cap = cfg->max_rows;
   auto bail = [&](cudaError_t e) {
     va_destroy(c);
@@ -643,6 +671,8 @@ void va_destroy(va_ctx* c) {
   if (c->h2d) cudaStreamSynchronize(c->h2d);
   if (c->d2h) cudaStreamSynchronize(c->d2h);
   for (auto& l : c->layers) free_layer(l);
+  for (auto& m : c->mlps) free_mlp(m);
+  dfree(c->hbuf);
   dfree(c->x);
   dfree(c->q);
   close_peers(c);
@@ -710,6 +740,42 @@ int va_load_layer(va_ctx* c, int layer, const float* norm1_w, const float* norm1
   return VA_OK;
 }
 
+int va_load_mlp(va_ctx* c, int layer, int mlp_hidden, const float* norm2_w, const float* norm2_b,
+                const float* fc1_w, const float* fc1_b, const float* fc2_w, const float* fc2_b,
+                const float* ls2) {
+  if (!c) return VA_ERR_INVALID;
+  if (layer < 0 || layer >= c->cfg.depth) return fail(c, VA_ERR_INVALID, "layer index out of range");
+  if (!norm2_w || !norm2_b || !fc1_w || !fc1_b || !fc2_w || !fc2_b)
+    return fail(c, VA_ERR_INVALID, "norm2, fc1 and fc2 tensors are required");
+  if (mlp_hidden <= 0 || mlp_hidden % 256 != 0)
+    return fail(c, VA_ERR_INVALID, "mlp_hidden must be a positive multiple of 256");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaDeviceSynchronize());  // earlier calls may still read the old weights / buffer
+  MlpWeights& m = c->mlps[layer];
+  free_mlp(m);
+  const int E = c->cfg.embed_dim;
+  if (mlp_hidden > c->hidden_cap) {
+    dfree(c->hbuf);
+    VA_CUDA(c, dmalloc(&c->hbuf, static_cast<size_t>(c->cap) * mlp_hidden));
+    c->hidden_cap = mlp_hidden;
+  }
+  std::vector<uint16_t> w1 = transpose_to_bf16(fc1_w, E, mlp_hidden);
+  std::vector<uint16_t> w2 = transpose_to_bf16(fc2_w, mlp_hidden, E);
+  VA_CUDA(c, dmalloc(&m.w_fc1_t, w1.size()));
+  VA_CUDA(c, cudaMemcpy(m.w_fc1_t, w1.data(), w1.size() * 2, cudaMemcpyHostToDevice));
+  VA_CUDA(c, dmalloc(&m.w_fc2_t, w2.size()));
+  VA_CUDA(c, cudaMemcpy(m.w_fc2_t, w2.data(), w2.size() * 2, cudaMemcpyHostToDevice));
+  int rc;
+  if ((rc = upload_vec(c, &m.norm2_w, norm2_w, E))) return rc;
+  if ((rc = upload_vec(c, &m.norm2_b, norm2_b, E))) return rc;
+  if ((rc = upload_vec(c, &m.fc1_b, fc1_b, mlp_hidden))) return rc;
+  if ((rc = upload_vec(c, &m.fc2_b, fc2_b, E))) return rc;
+  if ((rc = upload_vec(c, &m.ls2, ls2, E))) return rc;
+  m.hidden = mlp_hidden;
+  m.loaded = true;
+  return VA_OK;
+}
+
 int va_layer_flags(const va_ctx* c, int layer, int* use_qknorm, int* use_rope) {
   if (!c || layer < 0 || layer >= c->cfg.depth) return VA_ERR_INVALID;
   if (use_qknorm) *use_qknorm = layer_use_qknorm(c, layer) ? 1 : 0;
@@ -744,6 +810,30 @@ int va_run_attention(va_ctx* c, int layer, const float* input, int64_t rows, int
 }  // extern "C"
 
 namespace {
+
+// MLP sub-block in place on device tokens [rows][E] (vit_block.rs:1092-1129):
+// LN2 + bf16 cast, fc1 GEMM with bias + exact GELU, fc2 GEMM with bias, ls2 and
+// the residual add fused into its epilogue.
+int run_mlp(va_ctx* c, int layer, float* tokens, int64_t rows, cudaStream_t st) {
+  if (layer < 0 || layer >= c->cfg.depth || !c->mlps[layer].loaded)
+    return fail(c, VA_ERR_STATE, "MLP weights not loaded (va_load_mlp)");
+  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  const MlpWeights& m = c->mlps[layer];
+  const int E = c->cfg.embed_dim;
+  const int n = static_cast<int>(rows);
+  VA_CUDA(c, va::launch_ln_cast(tokens, m.norm2_w, m.norm2_b, c->cfg.ln_eps, n, E, c->x, st));
+  va::Fc1EpilogueArgs fa{m.fc1_b, c->hbuf, n, m.hidden};
+  VA_CUDA(c, va::launch_fc1_gemm(c->x, m.w_fc1_t, n, m.hidden, E, fa, c->err, st));
+  va::ProjEpilogueArgs pa{};
+  pa.bias = m.fc2_b;
+  pa.ls1 = m.ls2;
+  pa.residual = tokens;
+  pa.out = tokens;
+  pa.rows = n;
+  pa.embed = E;
+  VA_CUDA(c, va::launch_proj_gemm(c->hbuf, m.w_fc2_t, n, E, m.hidden, pa, c->err, st));
+  return VA_OK;
+}
 
 // Checks a closed-form-position call and builds its BranchSpec.  window_rows = the
 // whole view-major window (all ranks); local_rows = this rank's slice.
@@ -886,6 +976,50 @@ int va_block_attention_device(va_ctx* c, int layer, float* tokens_dev, int64_t r
   if (!c || !tokens_dev) return VA_ERR_INVALID;
   return device_call(c, layer, tokens_dev, true, tokens_dev, tokens_dev, rows, rows, 0, gh, gw,
                      view_count, global, false, static_cast<cudaStream_t>(stream));
+}
+
+int va_block_device(va_ctx* c, int layer, float* tokens_dev, int64_t rows, int gh, int gw,
+                    int view_count, int global, void* stream) {
+  if (!c || !tokens_dev) return VA_ERR_INVALID;
+  if (layer < 0 || layer >= c->cfg.depth || !c->mlps[layer].loaded)
+    return fail(c, VA_ERR_STATE, "MLP weights not loaded (va_load_mlp)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = device_call(c, layer, tokens_dev, true, tokens_dev, tokens_dev, rows, rows, 0, gh, gw,
+                       view_count, global, false, st);
+  if (rc) return rc;
+  return run_mlp(c, layer, tokens_dev, rows, st);
+}
+
+int va_block_device_sharded(va_ctx* c, int layer, float* tokens_local, int64_t local_rows, int gh,
+                            int gw, int view_count, int global, void* stream) {
+  if (!c || !tokens_local) return VA_ERR_INVALID;
+  if (layer < 0 || layer >= c->cfg.depth || !c->mlps[layer].loaded)
+    return fail(c, VA_ERR_STATE, "MLP weights not loaded (va_load_mlp)");
+  const int nranks = c->comm ? va::comm_size(c->comm) : 1;
+  const int rank = c->comm ? va::comm_rank(c->comm) : 0;
+  if (global && !c->comm) return fail(c, VA_ERR_STATE, "no communicator (va_comm_init)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = device_call(c, layer, tokens_local, true, tokens_local, tokens_local, local_rows * nranks,
+                       local_rows, local_rows * rank, gh, gw, view_count, global, true, st);
+  if (rc) return rc;
+  return run_mlp(c, layer, tokens_local, local_rows, st);
+}
+
+int va_run_tail_host(va_ctx* c, int layer, const float* tokens, int64_t rows, int gh, int gw,
+                     int view_count, int global, float* out) {
+  if (!c || !tokens || !out) return VA_ERR_INVALID;
+  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
+  VA_CUDA(c, cudaMemcpyAsync(c->in_f32, tokens, bytes, cudaMemcpyHostToDevice, c->stream));
+  int rc = va_block_device(c, layer, c->in_f32, rows, gh, gw, view_count, global, c->stream);
+  if (rc) {
+    cudaStreamSynchronize(c->stream);
+    return rc;
+  }
+  VA_CUDA(c, cudaMemcpyAsync(out, c->in_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  return read_device_error(c);
 }
 
 int va_comm_unique_id(void* id_out) {

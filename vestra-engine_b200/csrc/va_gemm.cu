@@ -200,6 +200,48 @@ struct QkvEpilogue {
   }
 };
 
+// MLP fc1 (vit_block.rs:1106-1115 / device :578): + bias, GELU with the exact erf
+// form z/2 * (1 + erf(z/sqrt 2)) (module doc, vit_block.rs:26), bf16 hidden out.
+struct Fc1Epilogue {
+  Fc1EpilogueArgs a;
+  CUtensorMap map_out;  // bf16 [rows][hidden], box 64 x 128
+
+  __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const { cbuf[t] = a.bias[n0 + t]; }
+
+  template <int BN>
+  __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
+                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+    static_assert(BN == 256, "fc1 tiles are 256 columns wide");
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int hh = half * 2 + j;  // 64-column block
+      float x[64];
+      tmem_ld32(tmem_row + hh * 64, x);
+      tmem_ld32(tmem_row + hh * 64 + 32, x + 32);
+      if (valid) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float z = x[i] + cbuf[hh * 64 + i];
+          x[i] = 0.5f * z * (1.0f + erff(z * 0.70710678118654752f));
+        }
+      }
+      const uint32_t tile = out_smem + hh * kOutTileBytes;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) st_shared_v4(tile + sw128_offset(r, c), pack8(x + 8 * c, false));
+    }
+  }
+
+  __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
+
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+    for (int j = 0; j < 2; ++j) {
+      const int hh = half * 2 + j;
+      tma_store_2d(&map_out, out_smem + hh * kOutTileBytes, n0 + hh * 64, m0);
+    }
+    bulk_commit_group();
+  }
+};
+
 struct ProjEpilogue {
   ProjEpilogueArgs a;
   CUtensorMap map_out;  // F32 [rows][embed], box 32 x 128
@@ -436,6 +478,15 @@ cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t
       !encode_tma_2d_bf16(&e.map_out[2], epi.v_out, embed, rows, 64, kBM))
     return cudaErrorInvalidValue;
   return launch_gemm<256, 2>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
+}
+
+cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
+                            const Fc1EpilogueArgs& epi, int* err, cudaStream_t st) {
+  if (n % 256 != 0 || epi.rows != m || epi.hidden != n || !epi.bias) return cudaErrorInvalidValue;
+  Fc1Epilogue e{};
+  e.a = epi;
+  if (!encode_tma_2d_bf16(&e.map_out, epi.out, n, m, 64, kBM)) return cudaErrorInvalidValue;
+  return launch_gemm<256, 2>(a, w_t, m, n, k, e, err, st);
 }
 
 cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,

@@ -35,6 +35,16 @@ struct QkvEpilogueArgs {
   __nv_bfloat16* peer_v[kMaxPeers] = {};
 };
 
+// MLP fc1 epilogue: + bias, exact GELU, bf16 out [rows][hidden].
+struct Fc1EpilogueArgs {
+  const float* bias;     // [hidden]
+  __nv_bfloat16* out;    // [rows][hidden]
+  int rows;
+  int hidden;
+};
+cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
+                            const Fc1EpilogueArgs& epi, int* err, cudaStream_t st);
+
 // Barrier of the direct K'/V exchange: this rank tells every peer that its slice
 // has arrived there (flag = epoch in the peer's flag array at index `rank`) and
 // waits until every peer has told it the same.

@@ -61,8 +61,10 @@ def hidden_states(rows: int, embed: int, seed: int = 0) -> np.ndarray:
 
 
 def layer_weights(embed: int, seed: int = 0, layer: int = 0, qknorm: bool = True, ls1: bool = False,
-                  bias: bool = False, norm1: bool = False, perturb_norm: bool = False) -> dict:
-    """One block's attention weights, [in, out] orientation."""
+                  bias: bool = False, norm1: bool = False, perturb_norm: bool = False, mlp: bool = False,
+                  ls2: bool = False, mlp_ratio: int = 4) -> dict:
+    """One block's weights, [in, out] orientation: attention (always), LN1 (norm1),
+    and the MLP sub-block (mlp: norm2, fc1 [E, ratio*E], fc2 [ratio*E, E], ls2)."""
     r = rng(seed, 1000 + layer)
     p = {
         "qkv_w": (0.02 * r.standard_normal((embed, 3 * embed))).astype(np.float32),
@@ -86,6 +88,17 @@ def layer_weights(embed: int, seed: int = 0, layer: int = 0, qknorm: bool = True
     if norm1:
         p["norm1_w"] = (1.0 + 0.1 * r.standard_normal(embed)).astype(np.float32)
         p["norm1_b"] = (0.1 * r.standard_normal(embed)).astype(np.float32)
+    if mlp:
+        m = rng(seed, 2000 + layer)
+        hidden = mlp_ratio * embed
+        p["norm2_w"] = (1.0 + 0.1 * m.standard_normal(embed)).astype(np.float32)
+        p["norm2_b"] = (0.1 * m.standard_normal(embed)).astype(np.float32)
+        p["fc1_w"] = (0.02 * m.standard_normal((embed, hidden))).astype(np.float32)
+        p["fc1_b"] = (0.02 * m.standard_normal(hidden)).astype(np.float32)
+        p["fc2_w"] = (0.02 * m.standard_normal((hidden, embed))).astype(np.float32)
+        p["fc2_b"] = (0.02 * m.standard_normal(embed)).astype(np.float32)
+        if ls2:
+            p["ls2"] = (0.1 + 0.05 * m.standard_normal(embed)).astype(np.float32)
     return p
 
 

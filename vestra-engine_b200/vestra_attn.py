@@ -36,6 +36,7 @@ EXPORTED = [
     "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
+    "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
     "va_op_attention_noalloc",
 ]
@@ -104,6 +105,10 @@ def load_library(path: str = LIB_PATH):
         "va_check_device": ([_vp], c_int),
         "va_selftest_bounded_wait": ([_vp, ctypes.c_int64], c_int),
         "va_set_phase_profile": ([_vp, c_int], c_int),
+        "va_load_mlp": ([_vp, c_int, c_int] + [_vp] * 7, c_int),
+        "va_block_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_block_device_sharded": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_run_tail_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_phase_times": ([_vp, _vp], c_int),
     }
     for name, (args, res) in sig.items():
@@ -206,6 +211,31 @@ class Context:
         self.check(self.lib.va_load_layer(self.h, layer, g("norm1_w"), g("norm1_b"), g("qkv_w"), g("qkv_b"),
                                           g("q_g"), g("q_b"), g("k_g"), g("k_b"), g("proj_w"), g("proj_b"),
                                           g("ls1")))
+
+    def load_mlp(self, layer: int, p: dict):
+        """p: norm2_w/b [E], fc1_w [E,H], fc1_b [H], fc2_w [H,E], fc2_b [E], optional ls2 [E]."""
+        keep = {k: _f32(v) for k, v in p.items() if v is not None}
+        g = lambda k: _ptr(keep.get(k))  # noqa: E731
+        hidden = keep["fc1_w"].shape[1]
+        self.check(self.lib.va_load_mlp(self.h, layer, hidden, g("norm2_w"), g("norm2_b"), g("fc1_w"),
+                                        g("fc1_b"), g("fc2_w"), g("fc2_b"), g("ls2")))
+
+    def block_device(self, layer, tokens_dev, gh, gw, view_count, global_, stream=0):
+        """One whole block in place on device tokens (run_tail_device, vit_block.rs:489-583)."""
+        self.check(self.lib.va_block_device(self.h, layer, _ptr(tokens_dev), tokens_dev.shape[0], gh, gw,
+                                            view_count, int(bool(global_)), stream))
+
+    def block_device_sharded(self, layer, tokens_local, gh, gw, view_count, global_, stream=0):
+        self.check(self.lib.va_block_device_sharded(self.h, layer, _ptr(tokens_local), tokens_local.shape[0],
+                                                    gh, gw, view_count, int(bool(global_)), stream))
+
+    def run_tail(self, layer, tokens, gh, gw, view_count, global_, out=None):
+        """TransformerTailExecutor::run_tail (vit_block.rs:110-129) on host tokens."""
+        tokens = _f32(tokens)
+        out = np.empty_like(tokens) if out is None else out
+        self.check(self.lib.va_run_tail_host(self.h, layer, _ptr(tokens), tokens.shape[0], gh, gw, view_count,
+                                             int(bool(global_)), _ptr(out)))
+        return out
 
     def layer_flags(self, layer: int):
         a, b = ctypes.c_int(), ctypes.c_int()
@@ -320,6 +350,38 @@ class CudaAttentionExecutor:
 
     def run_attention_views(self, layer_idx, ln1, gh, gw, view_count, global_):
         return self.ctx.attention_host(layer_idx, ln1, gh, gw, view_count, global_)
+
+
+class CudaTransformerTailExecutor:
+    """TransformerTailExecutor (vit_block.rs:110-129) backed by the sm_100a path.
+
+    Uploads every block's attention and MLP weights once from the reference's
+    `Weights` naming (vit_block.rs:30-53: norm1/2, attn_*, mlp_fc1/2, ls1/ls2).
+    run_tail returns the updated tokens of one block; the reference's `ln1`
+    argument is accepted for signature parity and not used (LN1 is recomputed on
+    the device from `tokens`).  No CPU fallback: failures raise.
+    """
+
+    def __init__(self, cfg: ModelConfig, weights: dict, device: int = 0, max_rows: int = 12 * 866):
+        self.cfg = cfg
+        self.ctx = Context(cfg.to_va(max_rows), device)
+        for i in range(cfg.depth):
+            if weights.get(wname(i, "attn_qkv.weight")) is None:
+                continue
+            self.ctx.load_layer(i, layer_params_from_weights(weights, i))
+            if weights.get(wname(i, "mlp_fc1.weight")) is not None:
+                self.ctx.load_mlp(i, mlp_params_from_weights(weights, i))
+
+    def run_tail(self, layer_idx, tokens, ln1, rows, gh, gw, global_, view_count, cfg=None):
+        del ln1, cfg
+        t = np.asarray(tokens, np.float32).reshape(rows, self.cfg.embed_dim)
+        return self.ctx.run_tail(layer_idx, t, gh, gw, view_count, global_)
+
+
+def mlp_params_from_weights(weights: dict, i: int) -> dict:
+    g = lambda s: weights.get(wname(i, s))  # noqa: E731
+    return {"norm2_w": g("norm2.weight"), "norm2_b": g("norm2.bias"), "fc1_w": g("mlp_fc1.weight"),
+            "fc1_b": g("mlp_fc1.bias"), "fc2_w": g("mlp_fc2.weight"), "fc2_b": g("mlp_fc2.bias"), "ls2": g("ls2")}
 
 
 def layer_params_from_weights(weights: dict, i: int) -> dict:
