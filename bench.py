@@ -6,7 +6,9 @@ per view, 10,392-token window, E=768, 12 heads x 64), FLOPs = 4 * N^2 * d * head
 A step is one global attention sub-block over the whole window: LN1 output (F32,
 resident in HBM) -> QKV UMMA with QK-norm/RoPE epilogue -> fused flash attention ->
 output projection (F32).  With --gpus N > 1 the window's queries are split into N
-equal token slices (one process per GPU) and K'/V are all-gathered over NCCL.
+equal token slices (one process per GPU); the QKV epilogue stores every K'/V tile
+into the peers' windows over NVLink (NCCL all-gather where that is unavailable).
+The line also reports one whole block (attention + LN2/MLP) under "block".
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -345,6 +347,35 @@ def run_ours(args):
     }
     ln_gbs = round(local_rows * wl.embed * 6 / (phases["ln"] * 1e-3) / 1e9, 1)  # F32 read + bf16 write
 
+    # ---- one whole block (device-resident tail: attention + LN2/MLP, residuals),
+    # reported beside the metric; tokens restored from a copy before every run.
+    pb = syn.layer_weights(wl.embed, seed=0, layer=LAYER, norm1=True, mlp=True)
+    ctx.load_layer(LAYER, pb)
+    ctx.load_mlp(LAYER, pb)
+    tok0 = ln1.clone()
+    tok = torch.empty_like(tok0)
+    block_ms = []
+    for i in range(args.warmup + args.steps):
+        flush_buf.zero_()
+        tok.copy_(tok0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        if world == 1:
+            ctx.block_device(LAYER, tok, wl.gh, wl.gw, wl.views, wl.global_, stream=sp)
+        else:
+            ctx.block_device_sharded(LAYER, tok, wl.gh, wl.gw, wl.views, wl.global_, stream=sp)
+        b.record(stream)
+        if i >= args.warmup:
+            block_ms.append((a, b))
+    barrier()
+    ctx.check_device()
+    block_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in block_ms))
+    mlp_flops = 16.0 * wl.rows * wl.embed * wl.embed
+    block = {"ms": round(block_ms, 4), "mlp_flops": mlp_flops,
+             "tflops_incl_mlp": round((flops + mlp_flops) / (block_ms * 1e-3) / 1e12, 1),
+             "what": "x += attention(LN1 x); x += fc2(GELU(fc1(LN2 x))) on device, one block"}
+    ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
+
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
     # Q/K ~ N(0,1) per channel like QK-normalised rows; V bf16 (production path).
     g = torch.Generator(device="cuda").manual_seed(rank)
@@ -446,7 +477,7 @@ def run_ours(args):
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
                     "pinned H2D + va_attention_device_sharded + D2H per rank",
                     "max_abs_vs_device_path": e2e_diff},
-            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs,
+            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -118,3 +118,68 @@ def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks, exchang
     a, b = got.astype(np.float64).ravel(), ref.astype(np.float64).ravel()
     cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
     assert err <= 2e-2 and cos >= 0.9999, (err, cos)
+
+
+def _block_rank_main(rank, nranks, ids, results):
+    try:
+        torch.cuda.set_device(rank)
+        wl = syn.CONFIGS[WORKLOAD]
+        row0, local = va.shard_rows(wl.rows, nranks, rank)
+        ctx = va.Context(_config(wl), rank)
+        p = syn.layer_weights(wl.embed, seed=8, layer=LAYER, norm1=True, mlp=True, ls1=True, ls2=True)
+        ctx.load_layer(LAYER, p)
+        ctx.load_mlp(LAYER, p)
+        if rank == 0:
+            uid = va.comm_unique_id()
+            for _ in range(nranks - 1):
+                ids.put(uid)
+        else:
+            uid = ids.get(timeout=TIMEOUT_S / 2)
+        ctx.comm_init(uid, nranks, rank)
+        x = syn.hidden_states(wl.rows, wl.embed, seed=8)[row0:row0 + local]
+        t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        ctx.block_device_sharded(LAYER, t, wl.gh, wl.gw, wl.views, True, stream=0)
+        torch.cuda.synchronize()
+        ctx.check_device()
+        results.put((rank, "ok", t.cpu().numpy()))
+        ctx.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        results.put((rank, f"error: {e!r}", None))
+
+
+def test_sharded_whole_block_matches_single_gpu():
+    # The device-resident tail over a query-sharded window: attention with the K'/V
+    # exchange, then the token-local LN2/MLP on every rank's slice.
+    nranks = 2
+    if torch.cuda.device_count() < nranks:
+        pytest.skip(f"needs {nranks} GPUs")
+    wl = syn.CONFIGS[WORKLOAD]
+    mpc = mp.get_context("spawn")
+    ids, results = mpc.Queue(), mpc.Queue()
+    procs = [mpc.Process(target=_block_rank_main, args=(r, nranks, ids, results)) for r in range(nranks)]
+    for pr in procs:
+        pr.start()
+    outs = {}
+    try:
+        for _ in range(nranks):
+            rank, status, arr = results.get(timeout=TIMEOUT_S)
+            assert status == "ok", f"rank {rank}: {status}"
+            outs[rank] = arr
+    except queue.Empty:
+        pytest.fail("a rank did not report within the time limit")
+    finally:
+        for pr in procs:
+            pr.join(timeout=60)
+            if pr.is_alive():
+                pr.kill()
+    sharded = np.concatenate([outs[r] for r in range(nranks)], axis=0)
+    ctx = va.Context(_config(wl), 0)
+    p = syn.layer_weights(wl.embed, seed=8, layer=LAYER, norm1=True, mlp=True, ls1=True, ls2=True)
+    ctx.load_layer(LAYER, p)
+    ctx.load_mlp(LAYER, p)
+    t = torch.from_numpy(syn.hidden_states(wl.rows, wl.embed, seed=8)).cuda()
+    ctx.block_device(LAYER, t, wl.gh, wl.gw, wl.views, True)
+    torch.cuda.synchronize()
+    single = t.cpu().numpy()
+    ctx.close()
+    assert float(np.abs(sharded - single).max()) <= 2e-3, float(np.abs(sharded - single).max())
