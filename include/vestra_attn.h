@@ -181,6 +181,12 @@ int va_comm_unique_id(void* id_out);
  * Otherwise, or with VA_KV_EXCHANGE=nccl in every rank's environment, an in-place
  * NCCL all-gather assembles the window. */
 int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
+/* va_attention_device_sharded with host buffers (pinned for overlap): this rank's
+ * ln1_local / out_local F32 [local_rows, E].  The rows are copied in chunks on a
+ * copy stream while their LN/QKV (and K'/V exchange stores) run, and the output is
+ * copied back chunk by chunk while later attention chunks compute.  Collective. */
+int va_attention_host_sharded(va_ctx* ctx, int layer, const float* ln1_local, float* out_local,
+                              int64_t local_rows, int gh, int gw, int view_count, int global);
 /* 0: no communicator, 1: NCCL all-gather, 2: direct peer stores. */
 int va_comm_exchange_mode(const va_ctx* ctx);
 /* ln1_local/out_local: device F32 [local_rows, E], this rank's rows

@@ -515,34 +515,54 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
 }
 
 // The device launch sequence of one attention sub-block (see the file header).
+// Direct K'/V exchange of one sharded call: picks the call's window pair (1 or 2,
+// alternating) and every peer's copy of it, and fills the barrier arguments.
+// Returns false when the call uses no direct exchange.
+bool prepare_exchange(va_ctx* c, BranchSpec* b, va::PeerBarrierArgs* pb) {
+  if (!b->gather || !c->p2p) return false;
+  const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
+  const int set = 1 + ((++c->epoch) & 1);
+  const size_t win = c->win_bytes;
+  char* own = static_cast<char*>(c->kv_arena);
+  b->kwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set) * win);
+  b->vwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set + 1) * win);
+  b->npeer = 0;
+  *pb = va::PeerBarrierArgs{};
+  pb->local_flags = c->xflags;
+  pb->nranks = nranks;
+  pb->rank = rank;
+  pb->epoch = c->epoch;
+  for (int r = 0; r < nranks; ++r) {
+    if (r == rank) continue;
+    char* pa = static_cast<char*>(c->peer_arena[r]);
+    b->peer_k[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set) * win);
+    b->peer_v[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set + 1) * win);
+    ++b->npeer;
+    pb->peer_flags[r] = reinterpret_cast<int*>(pa + kArenaWindows * win);
+  }
+  return true;
+}
+
+// The exchange step between the projection and the attention of a sharded call:
+// the direct exchange's barrier, or the NCCL all-gather.
+int exchange_step(va_ctx* c, const BranchSpec& b, bool direct, const va::PeerBarrierArgs& pb,
+                  cudaStream_t st) {
+  if (direct) {
+    VA_CUDA(c, va::launch_peer_barrier(pb, c->err, st));
+  } else if (b.gather) {
+    const int E = c->cfg.embed_dim;
+    return gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st);
+  }
+  return VA_OK;
+}
+
+// The device launch sequence of one attention sub-block (see the file header).
 int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
   int rc = validate_branch(c, layer, b_in);
   if (rc) return rc;
   BranchSpec b = b_in;
-  const bool direct = b.gather && c->p2p;
   va::PeerBarrierArgs pb{};
-  if (direct) {
-    // Direct exchange: this call's window pair, and every peer's copy of it.
-    const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
-    const int set = 1 + ((++c->epoch) & 1);  // window pair 1 or 2
-    const size_t win = c->win_bytes;
-    char* own = static_cast<char*>(c->kv_arena);
-    b.kwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set) * win);
-    b.vwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set + 1) * win);
-    b.npeer = 0;
-    pb.local_flags = c->xflags;
-    pb.nranks = nranks;
-    pb.rank = rank;
-    pb.epoch = c->epoch;
-    for (int r = 0; r < nranks; ++r) {
-      if (r == rank) continue;
-      char* pa = static_cast<char*>(c->peer_arena[r]);
-      b.peer_k[b.npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set) * win);
-      b.peer_v[b.npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set + 1) * win);
-      ++b.npeer;
-      pb.peer_flags[r] = reinterpret_cast<int*>(pa + kArenaWindows * win);
-    }
-  }
+  const bool direct = prepare_exchange(c, &b, &pb);
   // With the phase profile on, an event goes between every two launches; the ln
   // and qkv phases are split inside stage_qkv's two launches by mark(1).
   const bool prof = c->phase_profile;
@@ -551,12 +571,7 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
   VA_CUDA(c, mark(0));
   if ((rc = stage_qkv(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[1] : nullptr))) return rc;
   VA_CUDA(c, mark(2));
-  if (direct) {
-    VA_CUDA(c, va::launch_peer_barrier(pb, c->err, st));
-  } else if (b.gather) {
-    const int E = c->cfg.embed_dim;
-    if ((rc = gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st))) return rc;
-  }
+  if ((rc = exchange_step(c, b, direct, pb, st))) return rc;
   VA_CUDA(c, mark(3));
   if ((rc = stage_attn(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[4] : nullptr))) return rc;
   VA_CUDA(c, mark(5));
@@ -903,19 +918,14 @@ void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Boun
   *out = split_rows(rows, per_chunk * 256);
 }
 
-}  // namespace
-
-extern "C" {
-
-int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int gh, int gw,
-                      int view_count, int global, float* out) {
-  if (!c || !ln1 || !out) return VA_ERR_INVALID;
-  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
-  VA_CUDA(c, cudaSetDevice(c->device));
-  BranchSpec b;
-  int rc = make_branch(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
-                       view_count, global, false, &b);
-  if (rc) return rc;
+// The host-buffer path of one sub-block call (this rank's rows), chunked so that
+// the copies overlap the compute (see plan_host_chunks); for a sharded global
+// block the K'/V exchange runs between the last projection chunk and the first
+// attention chunk.
+int host_call(va_ctx* c, int layer, BranchSpec b, int view_count, const float* ln1, float* out) {
+  int rc = VA_OK;
+  va::PeerBarrierArgs pb{};
+  const bool direct = prepare_exchange(c, &b, &pb);
   Bounds in, outb;
   plan_host_chunks(c, b, view_count, &in, &outb);
   const int E = c->cfg.embed_dim;
@@ -948,6 +958,7 @@ int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int 
     }
   }
   if (b.seg_len == 0) {
+    if ((rc = exchange_step(c, b, direct, pb, c->stream))) return finish(rc);
     for (int j = 0; j < n_out; ++j) {
       if ((rc = stage_attn(c, layer, b, outb[j], outb[j + 1], c->stream))) return finish(rc);
       VA_HOST(cudaEventRecord(c->ev_out[j], c->stream));
@@ -962,6 +973,38 @@ int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int 
   VA_CUDA(c, cudaStreamSynchronize(c->d2h));
   finish(VA_OK);
   return read_device_error(c);
+}
+
+
+}  // namespace
+
+extern "C" {
+
+int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int gh, int gw,
+                      int view_count, int global, float* out) {
+  if (!c || !ln1 || !out) return VA_ERR_INVALID;
+  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  BranchSpec b;
+  int rc = make_branch(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
+                       view_count, global, false, &b);
+  if (rc) return rc;
+  return host_call(c, layer, b, view_count, ln1, out);
+}
+
+int va_attention_host_sharded(va_ctx* c, int layer, const float* ln1_local, float* out_local,
+                              int64_t local_rows, int gh, int gw, int view_count, int global) {
+  if (!c || !ln1_local || !out_local) return VA_ERR_INVALID;
+  if (local_rows <= 0 || local_rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  const int nranks = c->comm ? va::comm_size(c->comm) : 1;
+  const int rank = c->comm ? va::comm_rank(c->comm) : 0;
+  if (global && !c->comm) return fail(c, VA_ERR_STATE, "no communicator (va_comm_init)");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  BranchSpec b;
+  int rc = make_branch(c, layer, c->in_f32, false, c->out_f32, nullptr, local_rows * nranks,
+                       local_rows, local_rows * rank, gh, gw, view_count, global, true, &b);
+  if (rc) return rc;
+  return host_call(c, layer, b, view_count, ln1_local, out_local);
 }
 
 int va_attention_device(va_ctx* c, int layer, const float* ln1_dev, float* out_dev, int64_t rows,

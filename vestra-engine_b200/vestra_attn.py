@@ -38,6 +38,7 @@ EXPORTED = [
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
+    "va_attention_host_sharded",
     "va_op_attention_noalloc",
 ]
 
@@ -93,6 +94,7 @@ def load_library(path: str = LIB_PATH):
         "va_comm_unique_id": ([_vp], c_int),
         "va_comm_init": ([_vp, _vp, c_int, c_int], c_int),
         "va_comm_exchange_mode": ([_vp], c_int),
+        "va_attention_host_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int], c_int),
         "va_attention_device_sharded": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_op_attention_noalloc": ([_vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float, _vp, c_float,
                                      c_int, _vp, _vp], c_int),
@@ -279,6 +281,17 @@ class Context:
     def comm_init(self, comm_id: bytes, nranks: int, rank: int):
         buf = ctypes.create_string_buffer(bytes(comm_id), 128)
         self.check(self.lib.va_comm_init(self.h, buf, nranks, rank))
+
+    def attention_host_sharded(self, layer, ln1_local, gh, gw, view_count, global_, out=None):
+        """This rank's slice of a query-sharded window, host buffers (collective)."""
+        ln1_local = ln1_local if hasattr(ln1_local, "data_ptr") else _f32(ln1_local)
+        if out is None:
+            out = (np.empty_like(ln1_local) if isinstance(ln1_local, np.ndarray)
+                   else ln1_local.new_empty(ln1_local.shape))
+        self.check(self.lib.va_attention_host_sharded(self.h, layer, _ptr(ln1_local), _ptr(out),
+                                                      ln1_local.shape[0], gh, gw, view_count,
+                                                      int(bool(global_))))
+        return out
 
     def exchange_mode(self) -> str:
         """How K'/V reach the other ranks: "none", "nccl" or "direct" (peer stores)."""
