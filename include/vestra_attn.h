@@ -166,6 +166,27 @@ int va_block_device_sharded(va_ctx* ctx, int layer, float* tokens_local, int64_t
 int va_run_tail_host(va_ctx* ctx, int layer, const float* tokens, int64_t rows, int gh, int gw,
                      int view_count, int global, float* out);
 
+/* Multi-view device route (SURVEY next row 2; forward_multi_view_with_persistent_
+ * cuda_tail, backbone.rs:885-1137).  va_load_vit_norm uploads vit.norm.weight/bias
+ * [E] for the captures.  va_backbone_device runs blocks [first_layer, last_layer)
+ * in place on view-major device tokens [view_count * n, E] (n = 1 + num_register +
+ * gh*gw): block `layer` is global when alt_start >= 0, layer >= alt_start and layer
+ * is odd (backbone.rs:459-460); before block alt_start the camera slots are written
+ * into token 0 of every view (view 0 <- slot 0, the others <- slot 1,
+ * backbone.rs:746-768; camera_dev [2E] device, or NULL); after the last local block
+ * before a global one the tokens are snapshotted on the device.  For each i < n_out
+ * with out_layers[i] == layer, after that block: feat_dev[i] [views, n - n_special,
+ * W] and cam_dev[i] [views, W] (W = 2E when cat_token, else E) receive the
+ * post-processed capture of backbone.rs:1139-1179 (patch rows LayerNormed with
+ * vit.norm, concatenated after the local snapshot's rows when cat_token).  Every
+ * block needs va_load_layer (with norm1) and va_load_mlp.  Launches only, on
+ * `stream`; nothing is copied to the host. */
+int va_load_vit_norm(va_ctx* ctx, const float* norm_w, const float* norm_b);
+int va_backbone_device(va_ctx* ctx, float* tokens_dev, int64_t rows, int gh, int gw, int view_count,
+                       int first_layer, int last_layer, int alt_start, int cat_token,
+                       const float* camera_dev, int n_out, const int* out_layers,
+                       float* const* feat_dev, float* const* cam_dev, void* stream);
+
 /* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
  * add the query-sharded global block: each rank owns an equal contiguous slice of
  * the view-major window and forms K'/V for it; the window is then assembled on

@@ -75,6 +75,10 @@ struct va_ctx {
   std::vector<MlpWeights> mlps;
   __nv_bfloat16* hbuf = nullptr;  // MLP hidden activations [cap][hidden_cap] bf16
   int hidden_cap = 0;
+  // multi-layer device route (va_backbone_device)
+  float* local_snap = nullptr;    // [cap][E] tokens after the last local block before a global one
+  float* vit_norm_w = nullptr;    // [E] final-norm affine of the captures
+  float* vit_norm_b = nullptr;
   int64_t cap = 0;  // workspace rows
   __nv_bfloat16* x = nullptr;  // [cap][E] LN1 output, bf16
   __nv_bfloat16* q = nullptr;  // [cap][E] this rank's queries, token-major
@@ -688,6 +692,9 @@ void va_destroy(va_ctx* c) {
   for (auto& l : c->layers) free_layer(l);
   for (auto& m : c->mlps) free_mlp(m);
   dfree(c->hbuf);
+  dfree(c->local_snap);
+  dfree(c->vit_norm_w);
+  dfree(c->vit_norm_b);
   dfree(c->x);
   dfree(c->q);
   close_peers(c);
@@ -1031,6 +1038,62 @@ int va_block_device(va_ctx* c, int layer, float* tokens_dev, int64_t rows, int g
                        view_count, global, false, st);
   if (rc) return rc;
   return run_mlp(c, layer, tokens_dev, rows, st);
+}
+
+int va_load_vit_norm(va_ctx* c, const float* norm_w, const float* norm_b) {
+  if (!c || !norm_w || !norm_b) return VA_ERR_INVALID;
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaDeviceSynchronize());
+  dfree(c->vit_norm_w);
+  dfree(c->vit_norm_b);
+  int rc;
+  if ((rc = upload_vec(c, &c->vit_norm_w, norm_w, c->cfg.embed_dim))) return rc;
+  return upload_vec(c, &c->vit_norm_b, norm_b, c->cfg.embed_dim);
+}
+
+int va_backbone_device(va_ctx* c, float* tokens_dev, int64_t rows, int gh, int gw, int view_count,
+                       int first_layer, int last_layer, int alt_start, int cat_token,
+                       const float* camera_dev, int n_out, const int* out_layers,
+                       float* const* feat_dev, float* const* cam_dev, void* stream) {
+  if (!c || !tokens_dev || view_count <= 0) return VA_ERR_INVALID;
+  if (first_layer < 0 || last_layer > c->cfg.depth || first_layer >= last_layer)
+    return fail(c, VA_ERR_INVALID, "layer range out of bounds");
+  if (n_out < 0 || (n_out > 0 && (!out_layers || !feat_dev || !cam_dev)))
+    return fail(c, VA_ERR_INVALID, "captures need out_layers, feat and cam buffers");
+  if (n_out > 0 && !c->vit_norm_w) return fail(c, VA_ERR_STATE, "captures need va_load_vit_norm");
+  const int n_special = 1 + c->cfg.num_register;
+  const int64_t n = n_special + static_cast<int64_t>(gh) * gw;
+  if (n * view_count != rows) return fail(c, VA_ERR_INVALID, "rows must equal view_count * tokens per view");
+  for (int i = 0; i < n_out; ++i)
+    if (!feat_dev[i] || !cam_dev[i]) return fail(c, VA_ERR_INVALID, "missing capture buffer");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int E = c->cfg.embed_dim;
+  auto is_global = [&](int l) { return alt_start >= 0 && l >= alt_start && l % 2 == 1; };
+  bool snap_valid = false;
+  for (int layer = first_layer; layer < last_layer; ++layer) {
+    const bool global = is_global(layer);
+    if (camera_dev && layer == alt_start)
+      VA_CUDA(c, va::launch_camera_inject(tokens_dev, camera_dev, view_count, static_cast<int>(n), E, st));
+    int rc = va_block_device(c, layer, tokens_dev, rows, gh, gw, view_count, global ? 1 : 0, st);
+    if (rc) return rc;
+    for (int i = 0; i < n_out; ++i) {
+      if (out_layers[i] != layer) continue;
+      if (global && cat_token && !snap_valid)
+        return fail(c, VA_ERR_STATE, "a global capture needs the preceding local block in the range");
+      const float* local = global ? c->local_snap : tokens_dev;
+      VA_CUDA(c, va::launch_capture(tokens_dev, local, c->vit_norm_w, c->vit_norm_b, c->cfg.ln_eps,
+                                    view_count, static_cast<int>(n), n_special, E, cat_token ? 1 : 0,
+                                    feat_dev[i], cam_dev[i], st));
+    }
+    if (!global && layer + 1 < last_layer && is_global(layer + 1)) {
+      if (!c->local_snap) VA_CUDA(c, dmalloc(&c->local_snap, static_cast<size_t>(c->cap) * E));
+      VA_CUDA(c, cudaMemcpyAsync(c->local_snap, tokens_dev, static_cast<size_t>(rows) * E * sizeof(float),
+                                 cudaMemcpyDeviceToDevice, st));
+      snap_valid = true;
+    }
+  }
+  return VA_OK;
 }
 
 int va_block_device_sharded(va_ctx* c, int layer, float* tokens_local, int64_t local_rows, int gh,

@@ -137,6 +137,9 @@ cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, 
 cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
                                  int embed, cudaStream_t st);
 // View permutation: dst view i <- src view order[i] (order on the device).
+cudaError_t launch_capture(const float* x, const float* local_x, const float* g, const float* b,
+                           float eps, int views, int n, int n_special, int E, int cat, float* feat,
+                           float* cam, cudaStream_t st);
 cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns, int* err, cudaStream_t st);
 cudaError_t launch_permute_views(const float* src, float* dst, const int* order, int views,
                                  int64_t view_elems, cudaStream_t st);

@@ -252,6 +252,61 @@ cudaError_t launch_permute_views(const float* src, float* dst, const int* order,
   return cudaGetLastError();
 }
 
+// Capture of one out layer (backbone.rs:1139-1179), one warp per patch row:
+//   cat_token: feat[v][t] = [local_x row | LN_norm(x row)] (2E), cam[v] = [local_x row 0 | x row 0]
+//   otherwise: feat[v][t] = LN_norm(x row) (E),              cam[v] = x row 0
+// for the n - n_special patch rows t of every view v; LN with eps over E.
+__global__ void capture_kernel(const float* __restrict__ x, const float* __restrict__ local_x,
+                               const float* __restrict__ g, const float* __restrict__ b, float eps,
+                               int views, int n, int n_special, int E, int cat, float* feat,
+                               float* cam) {
+  const int n_patch = n - n_special;
+  const int64_t task = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int width = cat ? 2 * E : E;
+  if (task < static_cast<int64_t>(views) * n_patch) {
+    const int v = static_cast<int>(task / n_patch), t = static_cast<int>(task % n_patch);
+    const float* xr = x + (static_cast<int64_t>(v) * n + n_special + t) * E;
+    float* dst = feat + task * width;
+    float s = 0.f;
+    for (int c = lane; c < E; c += 32) s += xr[c];
+    const float mean = warp_sum(s) / E;
+    float q = 0.f;
+    for (int c = lane; c < E; c += 32) {
+      const float d = xr[c] - mean;
+      q += d * d;
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) / E + eps);
+    float* nd = cat ? dst + E : dst;
+    for (int c = lane; c < E; c += 32) nd[c] = (xr[c] - mean) * inv * g[c] + b[c];
+    if (cat) {
+      const float* lr = local_x + (static_cast<int64_t>(v) * n + n_special + t) * E;
+      for (int c = lane; c < E; c += 32) dst[c] = lr[c];
+    }
+  } else if (task < static_cast<int64_t>(views) * n_patch + views) {
+    const int v = static_cast<int>(task - static_cast<int64_t>(views) * n_patch);
+    const float* xr = x + static_cast<int64_t>(v) * n * E;
+    float* dst = cam + static_cast<int64_t>(v) * width;
+    if (cat) {
+      const float* lr = local_x + static_cast<int64_t>(v) * n * E;
+      for (int c = lane; c < E; c += 32) dst[c] = lr[c];
+      for (int c = lane; c < E; c += 32) dst[E + c] = xr[c];
+    } else {
+      for (int c = lane; c < E; c += 32) dst[c] = xr[c];
+    }
+  }
+}
+
+cudaError_t launch_capture(const float* x, const float* local_x, const float* g, const float* b,
+                           float eps, int views, int n, int n_special, int E, int cat, float* feat,
+                           float* cam, cudaStream_t st) {
+  const int64_t tasks = static_cast<int64_t>(views) * (n - n_special) + views;
+  const int per_block = 8;
+  capture_kernel<<<static_cast<unsigned>((tasks + per_block - 1) / per_block), 32 * per_block, 0, st>>>(
+      x, local_x, g, b, eps, views, n, n_special, E, cat, feat, cam);
+  return cudaGetLastError();
+}
+
 // Failure-detection self-test: one thread waits on an mbarrier that nothing
 // arrives on, through the same bounded wait the pipelined kernels use, so the
 // wait gives up after limit_ns and writes kDevTimeoutConsumer into the device

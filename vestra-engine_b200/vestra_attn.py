@@ -37,6 +37,7 @@ EXPORTED = [
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
+    "va_load_vit_norm", "va_backbone_device",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
     "va_attention_host_sharded",
     "va_op_attention_noalloc",
@@ -108,6 +109,9 @@ def load_library(path: str = LIB_PATH):
         "va_selftest_bounded_wait": ([_vp, ctypes.c_int64], c_int),
         "va_set_phase_profile": ([_vp, c_int], c_int),
         "va_load_mlp": ([_vp, c_int, c_int] + [_vp] * 7, c_int),
+        "va_load_vit_norm": ([_vp, _vp, _vp], c_int),
+        "va_backbone_device": ([_vp, _vp, i64, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _vp, c_int,
+                                _vp, _vp, _vp, _vp], c_int),
         "va_block_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_block_device_sharded": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_run_tail_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
@@ -238,6 +242,30 @@ class Context:
         self.check(self.lib.va_run_tail_host(self.h, layer, _ptr(tokens), tokens.shape[0], gh, gw, view_count,
                                              int(bool(global_)), _ptr(out)))
         return out
+
+    def load_vit_norm(self, w, b):
+        w, b = _f32(w), _f32(b)
+        self.check(self.lib.va_load_vit_norm(self.h, _ptr(w), _ptr(b)))
+
+    def backbone_device(self, tokens_dev, gh, gw, view_count, first_layer, last_layer, alt_start,
+                        camera_dev=None, out_layers=(), cat_token=True, stream=0):
+        """Blocks [first_layer, last_layer) in place on view-major device tokens
+        (backbone.rs:885-1137).  Returns {layer: (feat, cam)} device tensors of the
+        captures at out_layers."""
+        import torch
+        E = tokens_dev.shape[1]
+        n = tokens_dev.shape[0] // view_count
+        n_special = n - gh * gw
+        width = 2 * E if cat_token else E
+        caps = {l: (torch.empty(view_count, n - n_special, width, device=tokens_dev.device),
+                    torch.empty(view_count, width, device=tokens_dev.device)) for l in out_layers}
+        layers = (ctypes.c_int * max(1, len(out_layers)))(*out_layers)
+        feats = (ctypes.c_void_p * max(1, len(out_layers)))(*[caps[l][0].data_ptr() for l in out_layers])
+        cams = (ctypes.c_void_p * max(1, len(out_layers)))(*[caps[l][1].data_ptr() for l in out_layers])
+        self.check(self.lib.va_backbone_device(self.h, _ptr(tokens_dev), tokens_dev.shape[0], gh, gw, view_count,
+                                               first_layer, last_layer, alt_start, int(bool(cat_token)),
+                                               _ptr(camera_dev), len(out_layers), layers, feats, cams, stream))
+        return caps
 
     def layer_flags(self, layer: int):
         a, b = ctypes.c_int(), ctypes.c_int()
