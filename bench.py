@@ -374,6 +374,32 @@ def run_ours(args):
     block = {"ms": round(block_ms, 4), "mlp_flops": mlp_flops,
              "tflops_incl_mlp": round((flops + mlp_flops) / (block_ms * 1e-3) / 1e12, 1),
              "what": "x += attention(LN1 x); x += fc2(GELU(fc1(LN2 x))) on device, one block"}
+    # ---- the whole 12-block stack of one window (DA3-BASE schedule: alt_start 4,
+    # global blocks 5/7/9/11, the others local), single GPU only.
+    window = None
+    if world == 1:
+        for layer in range(12):
+            pl = syn.layer_weights(wl.embed, seed=0, layer=layer, norm1=True, mlp=True)
+            ctx.load_layer(layer, pl)
+            ctx.load_mlp(layer, pl)
+        win_ms = []
+        for i in range(max(3, args.warmup) + max(3, args.steps // 2)):
+            flush_buf.zero_()
+            tok.copy_(tok0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ctx.backbone_device(tok, wl.gh, wl.gw, wl.views, 0, 12, 4, stream=sp)
+            b.record(stream)
+            if i >= max(3, args.warmup):
+                win_ms.append((a, b))
+        torch.cuda.synchronize()
+        ctx.check_device()
+        win_ms = statistics.mean(a.elapsed_time(b) for a, b in win_ms)
+        n_tok = wl.rows // wl.views
+        attn_win = 4 * flops + 8 * 4.0 * wl.views * n_tok * n_tok * 64 * wl.heads
+        window = {"ms": round(win_ms, 3), "blocks": 12, "global_blocks": [5, 7, 9, 11],
+                  "attention_flops": attn_win, "attention_tflops": round(attn_win / (win_ms * 1e-3) / 1e12, 1),
+                  "what": "12 whole blocks (attention + MLP) of the S=12 window on device, va_backbone_device"}
     ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
 
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
@@ -470,7 +496,7 @@ def run_ours(args):
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
                     "va_attention_host_sharded (C ABI, pinned host in/out, per rank)",
                     "max_abs_vs_device_path": e2e_diff},
-            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block,
+            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
