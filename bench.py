@@ -375,31 +375,39 @@ def run_ours(args):
              "tflops_incl_mlp": round((flops + mlp_flops) / (block_ms * 1e-3) / 1e12, 1),
              "what": "x += attention(LN1 x); x += fc2(GELU(fc1(LN2 x))) on device, one block"}
     # ---- the whole 12-block stack of one window (DA3-BASE schedule: alt_start 4,
-    # global blocks 5/7/9/11, the others local), single GPU only.
+    # global blocks 5/7/9/11, the others local).  With N GPUs every rank holds whole
+    # views (12 on 8: 2,2,2,2,1,1,1,1): local blocks need no communication, global
+    # blocks exchange K'/V between the uneven slices.
     window = None
-    if world == 1:
+    n_tok = wl.rows // wl.views
+    if wl.views >= world and (world == 1 or ctx.exchange_mode() == "direct"):
         for layer in range(12):
             pl = syn.layer_weights(wl.embed, seed=0, layer=layer, norm1=True, mlp=True)
             ctx.load_layer(layer, pl)
             ctx.load_mlp(layer, pl)
+        v0, vrows = va.shard_views(wl.views, n_tok, world, rank)
+        xw = torch.from_numpy(np.ascontiguousarray(x_all[v0:v0 + vrows])).cuda()
+        tw = torch.empty_like(xw)
         win_ms = []
         for i in range(max(3, args.warmup) + max(3, args.steps // 2)):
             flush_buf.zero_()
-            tok.copy_(tok0)
+            tw.copy_(xw)
+            barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            ctx.backbone_device(tok, wl.gh, wl.gw, wl.views, 0, 12, 4, stream=sp)
+            ctx.backbone_device_sharded(tw, v0, wl.rows, wl.gh, wl.gw, wl.views, 0, 12, 4, stream=sp)
             b.record(stream)
             if i >= max(3, args.warmup):
                 win_ms.append((a, b))
-        torch.cuda.synchronize()
+        barrier()
         ctx.check_device()
-        win_ms = statistics.mean(a.elapsed_time(b) for a, b in win_ms)
-        n_tok = wl.rows // wl.views
+        win_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in win_ms))
         attn_win = 4 * flops + 8 * 4.0 * wl.views * n_tok * n_tok * 64 * wl.heads
         window = {"ms": round(win_ms, 3), "blocks": 12, "global_blocks": [5, 7, 9, 11],
                   "attention_flops": attn_win, "attention_tflops": round(attn_win / (win_ms * 1e-3) / 1e12, 1),
-                  "what": "12 whole blocks (attention + MLP) of the S=12 window on device, va_backbone_device"}
+                  "views_per_rank": [va.shard_views(wl.views, n_tok, world, r)[1] // n_tok for r in range(world)],
+                  "what": "12 whole blocks (attention + MLP) of the S=12 window on device, "
+                          "va_backbone_device_sharded (max over ranks)"}
     ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
 
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream

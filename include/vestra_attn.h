@@ -186,6 +186,21 @@ int va_backbone_device(va_ctx* ctx, float* tokens_dev, int64_t rows, int gh, int
                        int first_layer, int last_layer, int alt_start, int cat_token,
                        const float* camera_dev, int n_out, const int* out_layers,
                        float* const* feat_dev, float* const* cam_dev, void* stream);
+/* The same route over this rank's slice of a window shared by the ranks of a
+ * communicator (one process per GPU): tokens_local holds rows [row_offset,
+ * row_offset + local_rows) of a window_rows = view_count * n window, whole views
+ * (slices may be uneven, e.g. 12 views on 8 GPUs as 2,2,2,2,1,1,1,1).  Local blocks
+ * run on the rank's own views with no communication; global blocks exchange K'/V
+ * (uneven slices need the direct exchange) and the MLP stays token-local.  The
+ * camera slots follow the window's view order (only the rank holding view 0 writes
+ * the reference slot); captures cover the rank's own views.  Collective whenever
+ * the layer range holds a global block. */
+int va_backbone_device_sharded(va_ctx* ctx, float* tokens_local, int64_t local_rows,
+                               int64_t row_offset, int64_t window_rows, int gh, int gw,
+                               int view_count, int first_layer, int last_layer, int alt_start,
+                               int cat_token, const float* camera_dev, int n_out,
+                               const int* out_layers, float* const* feat_dev,
+                               float* const* cam_dev, void* stream);
 
 /* Multi-GPU (one process per GPU).  The reference has no multi-GPU code; these
  * add the query-sharded global block: each rank owns an equal contiguous slice of

@@ -109,3 +109,13 @@ def test_shard_rows():
     assert va.shard_rows(10392, 1, 0) == (0, 10392)
     with pytest.raises(ValueError):
         va.shard_rows(10392, 5, 0)
+
+
+def test_shard_views_splits_whole_views_evenly():
+    # 12 views on 8 GPUs: 2,2,2,2,1,1,1,1 whole views, contiguous and in order.
+    spans = [va.shard_views(12, 866, 8, r) for r in range(8)]
+    assert [s[1] // 866 for s in spans] == [2, 2, 2, 2, 1, 1, 1, 1]
+    assert [s[0] for s in spans] == [0, 1732, 3464, 5196, 6928, 7794, 8660, 9526]
+    assert spans[-1][0] + spans[-1][1] == 12 * 866
+    with pytest.raises(ValueError):
+        va.shard_views(3, 866, 4, 0)

@@ -187,3 +187,82 @@ def test_sharded_whole_block_matches_single_gpu():
     single = t.cpu().numpy()
     ctx.close()
     assert float(np.abs(sharded - single).max()) <= 2e-3, float(np.abs(sharded - single).max())
+
+
+def _route_rank_main(rank, nranks, ids, results):
+    try:
+        torch.cuda.set_device(rank)
+        wl = syn.Workload("s3_global", 768, 12, 3, 36, 24, 2, True)
+        n = wl.rows // wl.views
+        row0, local = va.shard_views(wl.views, n, nranks, rank)
+        ctx = va.Context(_config(wl), rank)
+        for layer in range(3, 7):
+            p = syn.layer_weights(wl.embed, seed=9, layer=layer, norm1=True, mlp=True)
+            ctx.load_layer(layer, p)
+            ctx.load_mlp(layer, p)
+        ctx.load_vit_norm(np.ones(wl.embed, np.float32), np.zeros(wl.embed, np.float32))
+        if rank == 0:
+            uid = va.comm_unique_id()
+            for _ in range(nranks - 1):
+                ids.put(uid)
+        else:
+            uid = ids.get(timeout=TIMEOUT_S / 2)
+        ctx.comm_init(uid, nranks, rank)
+        x = syn.hidden_states(wl.rows, wl.embed, seed=9)[row0:row0 + local]
+        t = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+        cam = torch.from_numpy(syn.camera_tokens(wl.embed, seed=9)).cuda()
+        caps = ctx.backbone_device_sharded(t, row0, wl.rows, wl.gh, wl.gw, wl.views, 3, 7, 4, camera_dev=cam,
+                                           out_layers=(4, 5))
+        torch.cuda.synchronize()
+        ctx.check_device()
+        results.put((rank, "ok", (t.cpu().numpy(), {k: (v[0].cpu().numpy(), v[1].cpu().numpy())
+                                                    for k, v in caps.items()})))
+        ctx.close()
+    except Exception as e:  # reported to the parent, which fails the test
+        results.put((rank, f"error: {e!r}", None))
+
+
+def test_sharded_backbone_route_uneven_views_matches_single_gpu():
+    # Three views on two GPUs (2 + 1 whole views): local blocks run on each rank's
+    # own views, the global block exchanges K'/V between uneven slices.
+    nranks = 2
+    if torch.cuda.device_count() < nranks:
+        pytest.skip(f"needs {nranks} GPUs")
+    wl = syn.Workload("s3_global", 768, 12, 3, 36, 24, 2, True)
+    mpc = mp.get_context("spawn")
+    ids, results = mpc.Queue(), mpc.Queue()
+    procs = [mpc.Process(target=_route_rank_main, args=(r, nranks, ids, results)) for r in range(nranks)]
+    for pr in procs:
+        pr.start()
+    outs = {}
+    try:
+        for _ in range(nranks):
+            rank, status, payload = results.get(timeout=TIMEOUT_S)
+            assert status == "ok", f"rank {rank}: {status}"
+            outs[rank] = payload
+    except queue.Empty:
+        pytest.fail("a rank did not report within the time limit")
+    finally:
+        for pr in procs:
+            pr.join(timeout=60)
+            if pr.is_alive():
+                pr.kill()
+    ctx = va.Context(_config(wl), 0)
+    for layer in range(3, 7):
+        p = syn.layer_weights(wl.embed, seed=9, layer=layer, norm1=True, mlp=True)
+        ctx.load_layer(layer, p)
+        ctx.load_mlp(layer, p)
+    ctx.load_vit_norm(np.ones(wl.embed, np.float32), np.zeros(wl.embed, np.float32))
+    t = torch.from_numpy(syn.hidden_states(wl.rows, wl.embed, seed=9)).cuda()
+    cam = torch.from_numpy(syn.camera_tokens(wl.embed, seed=9)).cuda()
+    caps = ctx.backbone_device(t, wl.gh, wl.gw, wl.views, 3, 7, 4, camera_dev=cam, out_layers=(4, 5))
+    torch.cuda.synchronize()
+    single = t.cpu().numpy()
+    sharded = np.concatenate([outs[r][0] for r in range(nranks)], axis=0)
+    assert float(np.abs(sharded - single).max()) <= 2e-3, float(np.abs(sharded - single).max())
+    for layer in (4, 5):
+        for i in range(2):
+            got = np.concatenate([outs[r][1][layer][i] for r in range(nranks)], axis=0)
+            ref = caps[layer][i].cpu().numpy()
+            assert float(np.abs(got - ref).max()) <= 2e-3, (layer, i, float(np.abs(got - ref).max()))
+    ctx.close()

@@ -95,8 +95,18 @@ struct va_ctx {
   __nv_bfloat16* o = nullptr;  // [cap][E] attention output, token-major
   float* in_f32 = nullptr;     // host-path staging [cap][E]
   float* out_f32 = nullptr;
-  int2* pos = nullptr;         // [cap]
-  PosKey pos_key;
+  int2* pos = nullptr;         // [cap] explicit tables (va_run_attention)
+  // Closed-form position tables by shape, least recently used evicted: a layer loop
+  // alternating local and global blocks finds both tables resident and launches
+  // without uploads or synchronisation.
+  struct PosEntry {
+    PosKey key;
+    int2* dev = nullptr;
+    int64_t cap = 0;
+    uint64_t used = 0;
+  };
+  PosEntry pos_cache[4];
+  uint64_t pos_clock = 0;
   float2* rope_cs = nullptr;   // [rope_npos][16]
   int rope_npos = 0;
   int* err = nullptr;          // device error word
@@ -234,11 +244,18 @@ int ensure_rope_table(va_ctx* c, int npos) {
   return VA_OK;
 }
 
-// Closed-form position table (vit_block.rs:841-881) into c->pos, cached.
-int ensure_positions(va_ctx* c, int64_t rows, int gh, int gw, int views, int global) {
+// Closed-form position table (vit_block.rs:841-881) of one window shape, from the
+// context's cache; *out receives the device table.
+int ensure_positions(va_ctx* c, int64_t rows, int gh, int gw, int views, int global,
+                     const int2** out) {
   const int n_special = 1 + c->cfg.num_register;
   PosKey key{rows, gh, gw, views, global, n_special};
-  if (c->pos_key == key) return VA_OK;
+  for (auto& e : c->pos_cache)
+    if (e.dev && e.key == key) {
+      e.used = ++c->pos_clock;
+      *out = e.dev;
+      return VA_OK;
+    }
   const int64_t per_view = n_special + static_cast<int64_t>(gh) * gw;
   if (views <= 0 || per_view * views != rows)
     return fail(c, VA_ERR_INVALID, "rows must equal view_count * (1 + num_register + gh*gw)");
@@ -255,12 +272,23 @@ int ensure_positions(va_ctx* c, int64_t rows, int gh, int gw, int views, int glo
         maxp = std::max(maxp, std::max(p[t].x, p[t].y));
       }
     }
-  // Kernels of an earlier call (on any stream) may still read the old table.
-  VA_CUDA(c, cudaDeviceSynchronize());
+  va_ctx::PosEntry* slot = &c->pos_cache[0];
+  for (auto& e : c->pos_cache)
+    if (!e.dev || e.used < slot->used) slot = &e;
+  // The evicted table (or a smaller rope table) may still be read by queued kernels.
+  if (slot->dev || maxp + 1 > c->rope_npos) VA_CUDA(c, cudaDeviceSynchronize());
   int rc = ensure_rope_table(c, maxp + 1);
   if (rc) return rc;
-  VA_CUDA(c, cudaMemcpy(c->pos, p.data(), p.size() * sizeof(int2), cudaMemcpyHostToDevice));
-  c->pos_key = key;
+  if (slot->cap < rows) {
+    dfree(slot->dev);
+    slot->cap = 0;
+    VA_CUDA(c, dmalloc(&slot->dev, static_cast<size_t>(rows)));
+    slot->cap = rows;
+  }
+  VA_CUDA(c, cudaMemcpy(slot->dev, p.data(), p.size() * sizeof(int2), cudaMemcpyHostToDevice));
+  slot->key = key;
+  slot->used = ++c->pos_clock;
+  *out = slot->dev;
   return VA_OK;
 }
 
@@ -279,7 +307,6 @@ int upload_positions(va_ctx* c, const float* pos_yx, int64_t rows, int2* dst) {
   int rc = ensure_rope_table(c, maxp + 1);
   if (rc) return rc;
   VA_CUDA(c, cudaMemcpy(dst, p.data(), p.size() * sizeof(int2), cudaMemcpyHostToDevice));
-  c->pos_key = PosKey{};  // the cached closed-form table was overwritten
   return VA_OK;
 }
 
@@ -704,6 +731,7 @@ void va_destroy(va_ctx* c) {
   dfree(c->in_f32);
   dfree(c->out_f32);
   dfree(c->pos);
+  for (auto& e : c->pos_cache) dfree(e.dev);
   dfree(c->rope_cs);
   dfree(c->err);
   dfree(c->op_buf);
@@ -869,8 +897,7 @@ int make_branch(va_ctx* c, int layer, const float* in, bool apply_ln1, float* ou
   if ((rc = segments_for(c, window_rows, view_count, global, &seg_len))) return rc;
   const int2* pos = nullptr;
   if (layer_use_rope(c, layer)) {
-    if ((rc = ensure_positions(c, window_rows, gh, gw, view_count, global))) return rc;
-    pos = c->pos;
+    if ((rc = ensure_positions(c, window_rows, gh, gw, view_count, global, &pos))) return rc;
   }
   *b = BranchSpec{in, apply_ln1, out, residual, local_rows, row_offset, window_rows, pos, seg_len,
                   sharded && global, c->k, c->v, 0, {}, {}};
@@ -1055,7 +1082,18 @@ int va_backbone_device(va_ctx* c, float* tokens_dev, int64_t rows, int gh, int g
                        int first_layer, int last_layer, int alt_start, int cat_token,
                        const float* camera_dev, int n_out, const int* out_layers,
                        float* const* feat_dev, float* const* cam_dev, void* stream) {
-  if (!c || !tokens_dev || view_count <= 0) return VA_ERR_INVALID;
+  return va_backbone_device_sharded(c, tokens_dev, rows, 0, rows, gh, gw, view_count, first_layer,
+                                    last_layer, alt_start, cat_token, camera_dev, n_out, out_layers,
+                                    feat_dev, cam_dev, stream);
+}
+
+int va_backbone_device_sharded(va_ctx* c, float* tokens_local, int64_t local_rows,
+                               int64_t row_offset, int64_t window_rows, int gh, int gw,
+                               int view_count, int first_layer, int last_layer, int alt_start,
+                               int cat_token, const float* camera_dev, int n_out,
+                               const int* out_layers, float* const* feat_dev,
+                               float* const* cam_dev, void* stream) {
+  if (!c || !tokens_local || view_count <= 0) return VA_ERR_INVALID;
   if (first_layer < 0 || last_layer > c->cfg.depth || first_layer >= last_layer)
     return fail(c, VA_ERR_INVALID, "layer range out of bounds");
   if (n_out < 0 || (n_out > 0 && (!out_layers || !feat_dev || !cam_dev)))
@@ -1063,32 +1101,58 @@ int va_backbone_device(va_ctx* c, float* tokens_dev, int64_t rows, int gh, int g
   if (n_out > 0 && !c->vit_norm_w) return fail(c, VA_ERR_STATE, "captures need va_load_vit_norm");
   const int n_special = 1 + c->cfg.num_register;
   const int64_t n = n_special + static_cast<int64_t>(gh) * gw;
-  if (n * view_count != rows) return fail(c, VA_ERR_INVALID, "rows must equal view_count * tokens per view");
+  if (n * view_count != window_rows) return fail(c, VA_ERR_INVALID, "window_rows must equal view_count * tokens per view");
+  if (local_rows <= 0 || local_rows % n || row_offset % n || row_offset < 0 ||
+      row_offset + local_rows > window_rows)
+    return fail(c, VA_ERR_INVALID, "a rank's slice must hold whole views of the window");
+  const bool sharded = local_rows != window_rows;
   for (int i = 0; i < n_out; ++i)
     if (!feat_dev[i] || !cam_dev[i]) return fail(c, VA_ERR_INVALID, "missing capture buffer");
+  auto is_global = [&](int l) { return alt_start >= 0 && l >= alt_start && l % 2 == 1; };
+  if (sharded) {
+    bool any_global = false;
+    for (int l = first_layer; l < last_layer; ++l) any_global |= is_global(l);
+    if (any_global && !c->comm) return fail(c, VA_ERR_STATE, "global blocks over a sharded window need va_comm_init");
+    // The NCCL fallback needs equal slices; view-aligned uneven slices need the
+    // direct exchange.
+    if (any_global && !c->p2p && window_rows != local_rows * va::comm_size(c->comm))
+      return fail(c, VA_ERR_STATE, "uneven view slices need the direct K'/V exchange");
+  }
   VA_CUDA(c, cudaSetDevice(c->device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int E = c->cfg.embed_dim;
-  auto is_global = [&](int l) { return alt_start >= 0 && l >= alt_start && l % 2 == 1; };
+  const int local_views = static_cast<int>(local_rows / n);
   bool snap_valid = false;
   for (int layer = first_layer; layer < last_layer; ++layer) {
     const bool global = is_global(layer);
     if (camera_dev && layer == alt_start)
-      VA_CUDA(c, va::launch_camera_inject(tokens_dev, camera_dev, view_count, static_cast<int>(n), E, st));
-    int rc = va_block_device(c, layer, tokens_dev, rows, gh, gw, view_count, global ? 1 : 0, st);
+      VA_CUDA(c, va::launch_camera_inject(tokens_local, camera_dev, local_views, static_cast<int>(n), E, st,
+                                          row_offset == 0));
+    if (layer < 0 || !c->mlps[layer].loaded) return fail(c, VA_ERR_STATE, "MLP weights not loaded (va_load_mlp)");
+    int rc;
+    if (global && sharded) {
+      // Query-sharded global block over the whole window, then the token-local MLP.
+      rc = device_call(c, layer, tokens_local, true, tokens_local, tokens_local, window_rows, local_rows,
+                       row_offset, gh, gw, view_count, 1, true, st);
+      if (!rc) rc = run_mlp(c, layer, tokens_local, local_rows, st);
+    } else {
+      // Local blocks (and every block on one GPU) run on the rank's own views.
+      rc = va_block_device(c, layer, tokens_local, local_rows, gh, gw, global ? view_count : local_views,
+                           global ? 1 : 0, st);
+    }
     if (rc) return rc;
     for (int i = 0; i < n_out; ++i) {
       if (out_layers[i] != layer) continue;
       if (global && cat_token && !snap_valid)
         return fail(c, VA_ERR_STATE, "a global capture needs the preceding local block in the range");
-      const float* local = global ? c->local_snap : tokens_dev;
-      VA_CUDA(c, va::launch_capture(tokens_dev, local, c->vit_norm_w, c->vit_norm_b, c->cfg.ln_eps,
-                                    view_count, static_cast<int>(n), n_special, E, cat_token ? 1 : 0,
+      const float* local = global ? c->local_snap : tokens_local;
+      VA_CUDA(c, va::launch_capture(tokens_local, local, c->vit_norm_w, c->vit_norm_b, c->cfg.ln_eps,
+                                    local_views, static_cast<int>(n), n_special, E, cat_token ? 1 : 0,
                                     feat_dev[i], cam_dev[i], st));
     }
     if (!global && layer + 1 < last_layer && is_global(layer + 1)) {
       if (!c->local_snap) VA_CUDA(c, dmalloc(&c->local_snap, static_cast<size_t>(c->cap) * E));
-      VA_CUDA(c, cudaMemcpyAsync(c->local_snap, tokens_dev, static_cast<size_t>(rows) * E * sizeof(float),
+      VA_CUDA(c, cudaMemcpyAsync(c->local_snap, tokens_local, static_cast<size_t>(local_rows) * E * sizeof(float),
                                  cudaMemcpyDeviceToDevice, st));
       snap_valid = true;
     }

@@ -135,7 +135,7 @@ cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, 
 // Camera-token slots (backbone.rs:746-768): token 0 of view 0 <- cam[0:E],
 // token 0 of every later view <- cam[E:2E].
 cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
-                                 int embed, cudaStream_t st);
+                                 int embed, cudaStream_t st, bool first_is_reference = true);
 // View permutation: dst view i <- src view order[i] (order on the device).
 cudaError_t launch_capture(const float* x, const float* local_x, const float* g, const float* b,
                            float eps, int views, int n, int n_special, int E, int cat, float* feat,

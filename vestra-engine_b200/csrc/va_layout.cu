@@ -190,10 +190,12 @@ __global__ void __launch_bounds__(256) prep_heads_kernel(
       out_f16 ? f16x2_from_f32(a0, a1) : pack_bf16x2(a0, a1);
 }
 
+// first_is_reference: view 0 of this buffer is the window's view 0 (reference
+// slot); a rank whose slice starts later gives every one of its views the source slot.
 __global__ void camera_inject_kernel(float* tokens, const float* cam, int views,
-                                     int tokens_per_view, int embed) {
+                                     int tokens_per_view, int embed, int first_is_reference) {
   const int view = blockIdx.x;
-  const float* src = cam + (view > 0 ? embed : 0);
+  const float* src = cam + ((view > 0 || !first_is_reference) ? embed : 0);
   float* dst = tokens + static_cast<size_t>(view) * tokens_per_view * embed;
   for (int c = threadIdx.x; c < embed; c += blockDim.x) dst[c] = src[c];
 }
@@ -236,9 +238,10 @@ cudaError_t launch_prep_heads(const float* x, int heads, int n, const float* g, 
 }
 
 cudaError_t launch_camera_inject(float* tokens, const float* cam, int views, int tokens_per_view,
-                                 int embed, cudaStream_t st) {
+                                 int embed, cudaStream_t st, bool first_is_reference) {
   if (views <= 0) return cudaSuccess;
-  camera_inject_kernel<<<views, 256, 0, st>>>(tokens, cam, views, tokens_per_view, embed);
+  camera_inject_kernel<<<views, 256, 0, st>>>(tokens, cam, views, tokens_per_view, embed,
+                                              first_is_reference ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -37,7 +37,7 @@ EXPORTED = [
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times",
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
-    "va_load_vit_norm", "va_backbone_device",
+    "va_load_vit_norm", "va_backbone_device", "va_backbone_device_sharded",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
     "va_attention_host_sharded",
     "va_op_attention_noalloc",
@@ -112,6 +112,8 @@ def load_library(path: str = LIB_PATH):
         "va_load_vit_norm": ([_vp, _vp, _vp], c_int),
         "va_backbone_device": ([_vp, _vp, i64, c_int, c_int, c_int, c_int, c_int, c_int, c_int, _vp, c_int,
                                 _vp, _vp, _vp, _vp], c_int),
+        "va_backbone_device_sharded": ([_vp, _vp, i64, i64, i64, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                        _vp, c_int, _vp, _vp, _vp, _vp], c_int),
         "va_block_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_block_device_sharded": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_run_tail_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
@@ -252,19 +254,28 @@ class Context:
         """Blocks [first_layer, last_layer) in place on view-major device tokens
         (backbone.rs:885-1137).  Returns {layer: (feat, cam)} device tensors of the
         captures at out_layers."""
+        return self.backbone_device_sharded(tokens_dev, 0, tokens_dev.shape[0], gh, gw, view_count, first_layer,
+                                            last_layer, alt_start, camera_dev, out_layers, cat_token, stream)
+
+    def backbone_device_sharded(self, tokens_local, row_offset, window_rows, gh, gw, view_count, first_layer,
+                                last_layer, alt_start, camera_dev=None, out_layers=(), cat_token=True, stream=0):
+        """This rank's whole views [row_offset, row_offset + rows) of a window_rows window
+        (collective when the range holds a global block).  Captures cover the rank's views."""
         import torch
-        E = tokens_dev.shape[1]
-        n = tokens_dev.shape[0] // view_count
+        E = tokens_local.shape[1]
+        n = window_rows // view_count
+        local_views = tokens_local.shape[0] // n
         n_special = n - gh * gw
         width = 2 * E if cat_token else E
-        caps = {l: (torch.empty(view_count, n - n_special, width, device=tokens_dev.device),
-                    torch.empty(view_count, width, device=tokens_dev.device)) for l in out_layers}
+        caps = {l: (torch.empty(local_views, n - n_special, width, device=tokens_local.device),
+                    torch.empty(local_views, width, device=tokens_local.device)) for l in out_layers}
         layers = (ctypes.c_int * max(1, len(out_layers)))(*out_layers)
         feats = (ctypes.c_void_p * max(1, len(out_layers)))(*[caps[l][0].data_ptr() for l in out_layers])
         cams = (ctypes.c_void_p * max(1, len(out_layers)))(*[caps[l][1].data_ptr() for l in out_layers])
-        self.check(self.lib.va_backbone_device(self.h, _ptr(tokens_dev), tokens_dev.shape[0], gh, gw, view_count,
-                                               first_layer, last_layer, alt_start, int(bool(cat_token)),
-                                               _ptr(camera_dev), len(out_layers), layers, feats, cams, stream))
+        self.check(self.lib.va_backbone_device_sharded(
+            self.h, _ptr(tokens_local), tokens_local.shape[0], row_offset, window_rows, gh, gw, view_count,
+            first_layer, last_layer, alt_start, int(bool(cat_token)), _ptr(camera_dev), len(out_layers), layers,
+            feats, cams, stream))
         return caps
 
     def layer_flags(self, layer: int):
@@ -467,6 +478,17 @@ def comm_unique_id() -> bytes:
     if rc != VA_OK:
         raise VestraError(rc, "va_comm_unique_id failed (NCCL unavailable?)")
     return buf.raw
+
+
+def shard_views(view_count: int, tokens_per_view: int, nranks: int, rank: int) -> tuple[int, int]:
+    """(row_offset, local_rows) of a rank's whole views: view_count views split as
+    evenly as possible, the first ranks taking one more (12 on 8: 2,2,2,2,1,1,1,1)."""
+    if view_count < nranks:
+        raise ValueError(f"{view_count} views cannot give every one of {nranks} ranks a view")
+    base, extra = divmod(view_count, nranks)
+    first = rank * base + min(rank, extra)
+    count = base + (1 if rank < extra else 0)
+    return first * tokens_per_view, count * tokens_per_view
 
 
 def shard_rows(window_rows: int, nranks: int, rank: int) -> tuple[int, int]:
