@@ -259,10 +259,19 @@ def test_sharded_backbone_route_uneven_views_matches_single_gpu():
     torch.cuda.synchronize()
     single = t.cpu().numpy()
     sharded = np.concatenate([outs[r][0] for r in range(nranks)], axis=0)
-    assert float(np.abs(sharded - single).max()) <= 2e-3, float(np.abs(sharded - single).max())
+
+    # Rank 0's attention launches split their last wave over key ranges and the
+    # single launch does not, so the two agree to rounding that four blocks carry
+    # forward: the parity gates apply (a wrong slot or view order would be O(1)).
+    def gate(got, ref, what):
+        got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+        err = float(np.abs(got - ref).max())
+        cos = float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref)))
+        assert err <= 2e-2 and cos >= 0.9999, f"{what}: max-abs {err:.3e} cos {cos:.7f}"
+
+    gate(sharded, single, "tokens")
     for layer in (4, 5):
-        for i in range(2):
+        for i, what in enumerate(("feat", "cam")):
             got = np.concatenate([outs[r][1][layer][i] for r in range(nranks)], axis=0)
-            ref = caps[layer][i].cpu().numpy()
-            assert float(np.abs(got - ref).max()) <= 2e-3, (layer, i, float(np.abs(got - ref).max()))
+            gate(got, caps[layer][i].cpu().numpy(), f"{what} capture {layer}")
     ctx.close()
