@@ -928,7 +928,7 @@ Bounds split_rows(int64_t rows, int64_t step) {
 // Chunking of the host path (va_attention_host).  Local blocks: groups of whole
 // views, each copied in, projected, attended, projected out and copied back on its
 // own, so the two copy directions overlap each other and the compute.  Global
-// blocks: the input in ~8 chunks of 128-row multiples (their LN/QKV overlaps the
+// blocks: the input in up to 8 chunks of >= 1024 rows (their LN/QKV overlaps the
 // later copies in), then the queries in chunks of about one wave of attention CTAs
 // (sms / heads CTAs of 256 queries each), so the copy out of one chunk overlaps the
 // attention of the next; no query can finish before the last key has arrived.
@@ -943,7 +943,9 @@ void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Boun
     (void)view_count;
     return;
   }
-  const int64_t step_in = std::max<int64_t>(128, ((rows + 7) / 8 + 127) / 128 * 128);
+  // At most 8 input chunks and at least 1024 rows each: a QKV launch of fewer rows
+  // (under ~70 CTAs) leaves most SMs idle and, when sharded, starves the peer stores.
+  const int64_t step_in = std::max<int64_t>(1024, ((rows + 7) / 8 + 127) / 128 * 128);
   *in = split_rows(rows, step_in);
   const int64_t pairs = (rows + 255) / 256;
   const int64_t per_wave = std::max<int64_t>(1, c->sms / std::max(1, c->cfg.num_heads));
