@@ -610,6 +610,8 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
   return VA_OK;
 }
 
+int host_call(va_ctx* c, int layer, struct BranchSpec b, int view_count, const float* ln1, float* out);
+
 int read_device_error(va_ctx* c) {
   int h = 0;
   VA_CUDA(c, cudaMemcpy(&h, c->err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -848,13 +850,11 @@ int va_run_attention(va_ctx* c, int layer, const float* input, int64_t rows, int
     if ((rc = upload_positions(c, positions_yx, rows, c->pos))) return rc;
     pos = c->pos;
   }
-  const size_t bytes = static_cast<size_t>(rows) * c->cfg.embed_dim * sizeof(float);
-  VA_CUDA(c, cudaMemcpyAsync(c->in_f32, input, bytes, cudaMemcpyHostToDevice, c->stream));
+  // The same chunked host pipeline as va_attention_host, so both seams compute
+  // the same rows in the same launches (bitwise equal for equal positions).
   BranchSpec b{c->in_f32, false, c->out_f32, nullptr, rows, 0, rows, pos, 0, false, c->k, c->v, 0, {}, {}};
-  if ((rc = run_branch(c, layer, b, c->stream))) return rc;
-  VA_CUDA(c, cudaMemcpyAsync(out, c->out_f32, bytes, cudaMemcpyDeviceToHost, c->stream));
-  VA_CUDA(c, cudaStreamSynchronize(c->stream));
-  return read_device_error(c);
+  if ((rc = validate_branch(c, layer, b))) return rc;
+  return host_call(c, layer, b, 1, input, out);
 }
 
 }  // extern "C"
