@@ -929,11 +929,10 @@ Bounds split_rows(int64_t rows, int64_t step) {
 // views, each copied in, projected, attended, projected out and copied back on its
 // own, so the two copy directions overlap each other and the compute.  Global
 // blocks: the input in up to 8 chunks of >= 1024 rows (their LN/QKV overlaps the
-// later copies in), then one query pair per head (split over key ranges by the
-// attention launch, so copying out starts early), then chunks of about one wave of
-// attention CTAs (sms / heads CTAs of 256 queries each), so the copy out of one chunk
-// overlaps the attention of the next; no query can finish before the last key has
-// arrived.
+// later copies in), then output chunks of 1, 2, 4, ... query pairs per head up to
+// about one wave of attention CTAs (sms / heads CTAs of 256 queries each), so the
+// copy out of one chunk overlaps the attention of the next; no query can finish
+// before the last key has arrived.
 void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Bounds* in,
                       Bounds* out) {
   const int64_t rows = b.rows;
@@ -949,22 +948,21 @@ void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Boun
   // (under ~70 CTAs) leaves most SMs idle and, when sharded, starves the peer stores.
   const int64_t step_in = std::max<int64_t>(1024, ((rows + 7) / 8 + 127) / 128 * 128);
   *in = split_rows(rows, step_in);
-  // The first output chunk is one query pair per head: its few units are split over
-  // key ranges by the attention launch, so the first rows reach the copy-out stream
-  // in a fraction of a full key pass; the rest go in chunks of about one wave.
+  // Output chunks of 1, 2, 4, ... query pairs per head, then about one wave each: the
+  // small first chunks are split over key ranges by the attention launch, so rows
+  // reach the copy-out stream early, and each chunk's attention ends before the copy
+  // of the previous chunk does, keeping the device-to-host stream busy.
   const int64_t pairs = (rows + 255) / 256;
-  out->assign(1, 0);
-  int64_t done = 0;
-  if (pairs > 1) {
-    out->push_back(256);
-    done = 1;
-  }
-  const int64_t rest = pairs - done;
   const int64_t per_wave = std::max<int64_t>(1, c->sms / std::max(1, c->cfg.num_heads));
-  const int64_t n_rest = std::min<int64_t>(kMaxHostChunks - 1, (rest + per_wave - 1) / per_wave);
-  const int64_t per_chunk = (rest + n_rest - 1) / n_rest;
-  for (int64_t p = done + per_chunk; p < pairs; p += per_chunk) out->push_back(p * 256);
-  out->push_back(rows);
+  out->assign(1, 0);
+  int64_t done = 0, size = 1;
+  while (done < pairs && static_cast<int>(out->size()) < kMaxHostChunks) {
+    const int64_t take = std::min(size, pairs - done);
+    done += take;
+    out->push_back(std::min(rows, done * 256));
+    size = std::min(2 * size, per_wave);
+  }
+  if (done < pairs) out->back() = rows;
 }
 
 // The host-buffer path of one sub-block call (this rank's rows), chunked so that
