@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 attention path of the DA3 ViT backbone (Vestra Engine).
 
-Metric (BASELINE.json): global-attention TFLOP/s at S=12 views (504x336, 866 tokens
+Metric: global-attention TFLOP/s at S=12 views (504x336, 866 tokens
 per view, 10,392-token window, E=768, 12 heads x 64), FLOPs = 4 * N^2 * d * heads.
 A step is one global attention sub-block over the whole window: LN1 output (F32,
 resident in HBM) -> QKV UMMA with QK-norm/RoPE epilogue -> fused flash attention ->

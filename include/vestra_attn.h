@@ -141,7 +141,7 @@ int va_op_attention_noalloc(const float* q, const float* k, const float* v, int 
                             const float* pos_yx_dev, float freq, int rope_pairing, float* out,
                             void* stream);
 
-/* Transformer tail (SURVEY next row 1): the MLP sub-block and the whole block.
+/* Transformer tail: the MLP sub-block and the whole block.
  * va_load_mlp replaces the CudaMlpExecutor weight upload (vit_block.rs:190-236):
  * norm2_w/b [E], fc1_w [E, mlp_hidden] and fc1_b [mlp_hidden], fc2_w [mlp_hidden, E]
  * and fc2_b [E] in the reference's [in, out] orientation, ls2 [E] or NULL
@@ -166,7 +166,7 @@ int va_block_device_sharded(va_ctx* ctx, int layer, float* tokens_local, int64_t
 int va_run_tail_host(va_ctx* ctx, int layer, const float* tokens, int64_t rows, int gh, int gw,
                      int view_count, int global, float* out);
 
-/* Multi-view device route (SURVEY next row 2; forward_multi_view_with_persistent_
+/* Multi-view device route (forward_multi_view_with_persistent_
  * cuda_tail, backbone.rs:885-1137).  va_load_vit_norm uploads vit.norm.weight/bias
  * [E] for the captures.  va_backbone_device runs blocks [first_layer, last_layer)
  * in place on view-major device tokens [view_count * n, E] (n = 1 + num_register +

@@ -1,6 +1,6 @@
 """GPU parity of the sm_100a attention path against the CPU F32 restatement (oracle/).
 
-Gates (BASELINE.json north_star): per-layer output max-abs error <= 2e-2 and
+Gates: per-layer output max-abs error <= 2e-2 and
 cosine similarity >= 0.9999 against the CPU F32 attention on identical seeded
 inputs; S=1 multi-view bitwise equal to the single-view path; view-order restore
 bit-exact.  Every call goes through the C ABI (libvestra_attn.so).
@@ -15,8 +15,8 @@ pytestmark = [pytest.mark.gpu,
 import synthetic as syn  # noqa: E402
 import vestra_attn as va  # noqa: E402
 
-MAX_ABS = 2e-2   # BASELINE gate, per-layer output
-MIN_COS = 0.9999  # BASELINE gate
+MAX_ABS = 2e-2   # parity gate, per-layer output
+MIN_COS = 0.9999  # parity gate
 
 
 def cos_sim(a, b):
@@ -42,7 +42,7 @@ def bf16_round(x):
 
 @pytest.fixture(scope="module")
 def ctx():
-    # BASELINE shapes: 2 special tokens per view (CLS + 1 register) -> 866 tokens.
+    # Benchmark shapes: 2 special tokens per view (CLS + 1 register) -> 866 tokens.
     cfg = va.default_config(max_rows=12 * 866, depth=12, rope_start=4, qknorm_start=4, num_register=1)
     c = va.Context(cfg, 0)
     yield c

@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs of the BASELINE shapes (no dataset or checkpoint exists here).
+"""Seeded synthetic inputs of the benchmark shapes (no dataset or checkpoint exists here).
 
 Hidden states ~ N(0,1) F32, QKV/proj weights ~ N(0, 0.02), QK-norm gamma 1 / beta 0,
 biases 0 unless asked, ls1 absent unless asked; camera slots ~ N(0,1).  Weights use
@@ -37,12 +37,12 @@ class Workload:
         return self.rows if self.global_ else self.tokens_per_view
 
     def attention_flops(self) -> float:
-        """4 * N^2 * d * heads summed over the attention segments (BASELINE formula)."""
+        """4 * N^2 * d * heads summed over the attention segments (the metric's FLOP count)."""
         segs = self.rows // self.seg_len
         return 4.0 * segs * self.seg_len ** 2 * 64 * self.heads
 
 
-# BASELINE.json configs (504x336 -> 36x24 patches; 1008x672 -> 72x48), n_special = 2.
+# Benchmark configs (504x336 -> 36x24 patches; 1008x672 -> 72x48), n_special = 2.
 CONFIGS = {
     "cfg1_single_view": Workload("cfg1_single_view", 768, 12, 1, 36, 24, 2, False),
     "cfg2_s2_global": Workload("cfg2_s2_global", 768, 12, 2, 36, 24, 2, True),
