@@ -166,6 +166,42 @@ int va_block_device_sharded(va_ctx* ctx, int layer, float* tokens_local, int64_t
 int va_run_tail_host(va_ctx* ctx, int layer, const float* tokens, int64_t rows, int gh, int gw,
                      int view_count, int global, float* out);
 
+/* Token input side: patch projection and CLS / register / position assembly on
+ * the device, producing the view-major tokens va_backbone_device consumes.
+ *
+ * va_load_patch_embed replaces CudaPatchEmbedExecutor::new (patch_embed.rs:150-198)
+ * and the weight lookups of prepare_tokens (pos_embed.rs:236-300): weight_oihw
+ * vit.patch_embed.weight [E][3][patch][patch], bias vit.patch_embed.bias [E],
+ * cls_token vit.cls_token [E], pos_embed vit.pos_embed [pos_rows][E] (row 0 = CLS,
+ * then a square grid*grid table; a non-square count is VA_ERR_INVALID like
+ * infer_grid, pos_embed.rs:89-106), register_tokens [num_register][E] (num_register
+ * must equal the context's; NULL when 0), interp_offset 0.1 for DA3
+ * (DEFAULT_INTERP_OFFSET, pos_embed.rs:41-55).  The filter is stored as bf16.
+ *
+ * va_prepare_tokens_device = prepare_tokens for `views` images at once: image
+ * NCHW F32 [views][3][height][width] -> tokens F32 [views][n][E], n = 1 +
+ * num_register + gh*gw, gh = height/patch, gw = width/patch; per view row 0 =
+ * cls + pos[0], rows 1..num_register = register tokens, then patch rows
+ * (row-major over the patch grid) = conv + bias + pos[1 + p].  position: NULL
+ * (the bicubic table of interpolate_pos_embed, pos_embed.rs:122-172, built on
+ * the device once per (gh, gw) and cached) or a device table [(1 + gh*gw)][E].
+ * height/width not multiples of patch, or views*gh*gw above max_rows, are
+ * VA_ERR_INVALID.  Launches only, on `stream`.
+ *
+ * va_prepare_tokens_host: the same with host buffers (CudaPatchEmbedExecutor::run,
+ * patch_embed.rs:200-245, for several views; position NULL or a host table).
+ * va_pos_embed_device: the cached interpolated table alone (PosEmbedCache::
+ * get_or_build, pos_embed.rs:199-222), out [(1 + gh*gw)][E] on the device. */
+int va_load_patch_embed(va_ctx* ctx, const float* weight_oihw, const float* bias,
+                        const float* cls_token, const float* pos_embed, int64_t pos_rows,
+                        const float* register_tokens, int num_register, int patch,
+                        float interp_offset);
+int va_prepare_tokens_device(va_ctx* ctx, const float* image, int views, int height, int width,
+                             const float* position, float* tokens, void* stream);
+int va_prepare_tokens_host(va_ctx* ctx, const float* image, int views, int height, int width,
+                           const float* position, float* tokens);
+int va_pos_embed_device(va_ctx* ctx, int gh, int gw, float* out, void* stream);
+
 /* Multi-view device route (forward_multi_view_with_persistent_
  * cuda_tail, backbone.rs:885-1137).  va_load_vit_norm uploads vit.norm.weight/bias
  * [E] for the captures.  va_backbone_device runs blocks [first_layer, last_layer)
@@ -239,7 +275,8 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
  * (24): poly 0..2 = how many of every 8 exponential pairs run on the FMA pipe
  * instead of MUFU; form 0, 1, 2, 4 = one softmax row per thread (instruction
  * formulations), form 3 = four threads per row (20 warps), form 5 = form 3 with
- * the two query tiles taking turns in the exponential section.  Query i is row
+ * the two query tiles taking turns in the exponential section, form 6 = form 3
+ * with the split tail off (one CTA per unit).  Query i is row
  * q_offset + i of the key window.  seg_len = 0: every query attends to all kv_rows
  * keys; seg_len > 0: independent segments of seg_len tokens (q_offset and q_count
  * multiples of seg_len).  out bf16 [q_count, heads*64]. */

@@ -57,6 +57,22 @@ struct MlpWeights {
   float* ls2 = nullptr;               // [E] or null
 };
 
+// Patch projection and token assembly (patch_embed.rs:33-36, pos_embed.rs:23-39).
+struct PatchEmbedWeights {
+  bool loaded = false;
+  int patch = 0;
+  int kp = 0;          // 3*patch^2 rounded up to the GEMM's 64-wide K slab
+  int grid = 0;        // side of the learned position grid
+  int n_register = 0;
+  float offset = 0.1f; // interpolation offset (interp_offset)
+  __nv_bfloat16* w_t = nullptr;   // [E][kp] filter rows, zero past 3*patch^2
+  float* bias = nullptr;          // [E]
+  float* cls = nullptr;           // [E]
+  float* pos = nullptr;           // [(grid*grid + 1)][E]
+  float* regs = nullptr;          // [n_register][E] or null
+  __nv_bfloat16* rows = nullptr;  // own patch-row buffer [cap][kp] when kp > E (else the LN1 buffer)
+};
+
 struct PosKey {
   int64_t rows = -1;
   int gh = 0, gw = 0, views = 0, global = 0, n_special = 0;
@@ -135,6 +151,17 @@ struct va_ctx {
   bool p2p = false;
   int epoch = 0;
   void* peer_arena[va::kMaxRanks] = {};
+  // token input side (va_load_patch_embed)
+  PatchEmbedWeights pe;
+  // Interpolated position tables [(1 + gh*gw)][E] by patch grid, least recently
+  // used evicted (PosEmbedCache, pos_embed.rs:183-222, on the device).
+  struct PosTable {
+    int gh = 0, gw = 0;
+    float* dev = nullptr;
+    uint64_t used = 0;
+  };
+  PosTable pe_cache[4];
+  uint64_t pe_clock = 0;
   std::string last_error;
 };
 
@@ -216,6 +243,45 @@ void free_mlp(MlpWeights& m) {
   dfree(m.fc2_b);
   dfree(m.ls2);
   m.loaded = false;
+}
+
+void free_patch_embed(va_ctx* c) {
+  PatchEmbedWeights& p = c->pe;
+  dfree(p.w_t);
+  dfree(p.bias);
+  dfree(p.cls);
+  dfree(p.pos);
+  dfree(p.regs);
+  dfree(p.rows);
+  p.loaded = false;
+  for (auto& e : c->pe_cache) {
+    dfree(e.dev);
+    e = va_ctx::PosTable{};
+  }
+}
+
+// The interpolated position table of patch grid (gh, gw), built on `st` on first use.
+int ensure_pos_table(va_ctx* c, int gh, int gw, cudaStream_t st, const float** out) {
+  va_ctx::PosTable* hit = nullptr;
+  for (auto& e : c->pe_cache)
+    if (e.dev && e.gh == gh && e.gw == gw) hit = &e;
+  if (!hit) {
+    hit = &c->pe_cache[0];
+    for (auto& e : c->pe_cache)
+      if (e.used < hit->used) hit = &e;
+    dfree(hit->dev);  // cudaFree waits for work still reading the evicted table
+    *hit = va_ctx::PosTable{};
+    VA_CUDA(c, dmalloc(&hit->dev, static_cast<size_t>(1 + gh * gw) * c->cfg.embed_dim));
+    VA_CUDA(c, va::launch_pos_interp(c->pe.pos, c->pe.grid, c->cfg.embed_dim, gh, gw, c->pe.offset,
+                                     hit->dev, st));
+    // Built once per grid; finishing it here lets later calls on any stream read it.
+    VA_CUDA(c, cudaStreamSynchronize(st));
+    hit->gh = gh;
+    hit->gw = gw;
+  }
+  hit->used = ++c->pe_clock;
+  *out = hit->dev;
+  return VA_OK;
 }
 
 bool layer_use_qknorm(const va_ctx* c, int layer) {
@@ -720,6 +786,7 @@ void va_destroy(va_ctx* c) {
   if (c->d2h) cudaStreamSynchronize(c->d2h);
   for (auto& l : c->layers) free_layer(l);
   for (auto& m : c->mlps) free_mlp(m);
+  free_patch_embed(c);
   dfree(c->hbuf);
   dfree(c->local_snap);
   dfree(c->vit_norm_w);
@@ -1083,6 +1150,139 @@ int va_load_vit_norm(va_ctx* c, const float* norm_w, const float* norm_b) {
   return upload_vec(c, &c->vit_norm_b, norm_b, c->cfg.embed_dim);
 }
 
+int va_load_patch_embed(va_ctx* c, const float* weight_oihw, const float* bias,
+                        const float* cls_token, const float* pos_embed, int64_t pos_rows,
+                        const float* register_tokens, int num_register, int patch,
+                        float interp_offset) {
+  if (!c) return VA_ERR_INVALID;
+  if (!weight_oihw || !bias || !cls_token || !pos_embed)
+    return fail(c, VA_ERR_INVALID, "patch filter, bias, cls token and pos_embed are required");
+  if (patch <= 0 || 3 * patch * patch > 4096) return fail(c, VA_ERR_INVALID, "patch size out of range");
+  if (num_register != c->cfg.num_register || (num_register > 0 && !register_tokens))
+    return fail(c, VA_ERR_INVALID, "num_register must match the context and come with its tokens");
+  // infer_grid (pos_embed.rs:89-106): 1 CLS row + a square grid.
+  const int64_t grid_rows = pos_rows - 1;
+  int grid = static_cast<int>(std::llround(std::sqrt(static_cast<double>(std::max<int64_t>(grid_rows, 0)))));
+  if (pos_rows < 2 || static_cast<int64_t>(grid) * grid != grid_rows)
+    return fail(c, VA_ERR_INVALID, "pos_embed patch-row count is not a perfect square");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaDeviceSynchronize());
+  free_patch_embed(c);
+  const int E = c->cfg.embed_dim, features = 3 * patch * patch;
+  const int kp = (features + 63) / 64 * 64;
+  // OIHW [E][3][p][p] is already [E][features] K-major; pad K to kp with zeros.
+  std::vector<uint16_t> w(static_cast<size_t>(E) * kp, 0);
+  for (int o = 0; o < E; ++o)
+    for (int i = 0; i < features; ++i)
+      w[static_cast<size_t>(o) * kp + i] = f32_to_bf16_rne(weight_oihw[static_cast<size_t>(o) * features + i]);
+  PatchEmbedWeights& p = c->pe;
+  VA_CUDA(c, dmalloc(&p.w_t, w.size()));
+  VA_CUDA(c, cudaMemcpy(p.w_t, w.data(), w.size() * 2, cudaMemcpyHostToDevice));
+  int rc;
+  if ((rc = upload_vec(c, &p.bias, bias, E))) return rc;
+  if ((rc = upload_vec(c, &p.cls, cls_token, E))) return rc;
+  if ((rc = upload_vec(c, &p.pos, pos_embed, static_cast<size_t>(pos_rows) * E))) return rc;
+  if (num_register > 0 && (rc = upload_vec(c, &p.regs, register_tokens, static_cast<size_t>(num_register) * E)))
+    return rc;
+  if (kp > E) VA_CUDA(c, dmalloc(&p.rows, static_cast<size_t>(c->cap) * kp));
+  p.patch = patch;
+  p.kp = kp;
+  p.grid = grid;
+  p.n_register = num_register;
+  p.offset = interp_offset;
+  p.loaded = true;
+  return VA_OK;
+}
+
+int va_pos_embed_device(va_ctx* c, int gh, int gw, float* out, void* stream) {
+  if (!c || !out) return VA_ERR_INVALID;
+  if (!c->pe.loaded) return fail(c, VA_ERR_STATE, "patch embedding not loaded (va_load_patch_embed)");
+  if (gh <= 0 || gw <= 0) return fail(c, VA_ERR_INVALID, "empty patch grid");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* table = nullptr;
+  int rc = ensure_pos_table(c, gh, gw, st, &table);
+  if (rc) return rc;
+  VA_CUDA(c, cudaMemcpyAsync(out, table, static_cast<size_t>(1 + gh * gw) * c->cfg.embed_dim * sizeof(float),
+                             cudaMemcpyDeviceToDevice, st));
+  return VA_OK;
+}
+
+int va_prepare_tokens_device(va_ctx* c, const float* image, int views, int height, int width,
+                             const float* position, float* tokens, void* stream) {
+  if (!c || !image || !tokens) return VA_ERR_INVALID;
+  const PatchEmbedWeights& p = c->pe;
+  if (!p.loaded) return fail(c, VA_ERR_STATE, "patch embedding not loaded (va_load_patch_embed)");
+  if (views <= 0 || height <= 0 || width <= 0 || height % p.patch || width % p.patch)
+    return fail(c, VA_ERR_INVALID, "height and width must be positive multiples of patch_size");
+  const int gh = height / p.patch, gw = width / p.patch;
+  const int64_t n_patches = static_cast<int64_t>(gh) * gw;
+  if (static_cast<int64_t>(views) * n_patches > c->cap)
+    return fail(c, VA_ERR_INVALID, "views * patches exceed the context's max_rows");
+  if ((reinterpret_cast<uintptr_t>(tokens) | reinterpret_cast<uintptr_t>(position)) & 15)
+    return fail(c, VA_ERR_INVALID, "tokens and position must be 16-byte aligned");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* pos = position;
+  int rc;
+  if (!pos && (rc = ensure_pos_table(c, gh, gw, st, &pos))) return rc;
+  const int E = c->cfg.embed_dim, n_special = 1 + p.n_register;
+  const int n_tok = n_special + static_cast<int>(n_patches);
+  __nv_bfloat16* rows = p.rows ? p.rows : c->x;
+  VA_CUDA(c, va::launch_patchify(image, views, height, width, p.patch, p.kp, rows, st));
+  va::PatchEpilogueArgs ea{};
+  ea.bias = p.bias;
+  ea.pos = pos;
+  ea.out = tokens;
+  ea.rows = static_cast<int>(views * n_patches);
+  ea.n_patches = static_cast<int>(n_patches);
+  ea.n_tok = n_tok;
+  ea.n_special = n_special;
+  ea.embed = E;
+  VA_CUDA(c, va::launch_patch_gemm(rows, p.w_t, p.kp, ea, c->err, st));
+  VA_CUDA(c, va::launch_token_specials(p.cls, pos, p.regs, p.n_register, views, n_tok, E, tokens, st));
+  return VA_OK;
+}
+
+int va_prepare_tokens_host(va_ctx* c, const float* image, int views, int height, int width,
+                           const float* position, float* tokens) {
+  if (!c || !image || !tokens) return VA_ERR_INVALID;
+  const PatchEmbedWeights& p = c->pe;
+  if (!p.loaded) return fail(c, VA_ERR_STATE, "patch embedding not loaded (va_load_patch_embed)");
+  if (views <= 0 || height <= 0 || width <= 0 || height % p.patch || width % p.patch)
+    return fail(c, VA_ERR_INVALID, "height and width must be positive multiples of patch_size");
+  const int E = c->cfg.embed_dim;
+  const int64_t n_patches = static_cast<int64_t>(height / p.patch) * (width / p.patch);
+  const int64_t n_tok = 1 + p.n_register + n_patches;
+  const size_t img_elems = static_cast<size_t>(views) * 3 * height * width;
+  const size_t tok_elems = static_cast<size_t>(views) * n_tok * E;
+  const size_t staging = static_cast<size_t>(c->cap) * E;
+  if (img_elems > staging || tok_elems > staging)
+    return fail(c, VA_ERR_INVALID, "image or tokens exceed the host staging buffers (max_rows * E floats)");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  float* pos_dev = nullptr;
+  const size_t pos_elems = static_cast<size_t>(1 + n_patches) * E;
+  if (position) {
+    VA_CUDA(c, dmalloc(&pos_dev, pos_elems));
+    VA_CUDA(c, cudaMemcpy(pos_dev, position, pos_elems * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  int rc = VA_OK;
+  cudaError_t e = cudaMemcpyAsync(c->in_f32, image, img_elems * sizeof(float), cudaMemcpyHostToDevice, c->stream);
+  if (e != cudaSuccess) rc = cuda_fail(c, e, "image upload");
+  if (!rc) rc = va_prepare_tokens_device(c, c->in_f32, views, height, width, pos_dev, c->out_f32, c->stream);
+  if (!rc) {
+    e = cudaMemcpyAsync(tokens, c->out_f32, tok_elems * sizeof(float), cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) rc = cuda_fail(c, e, "token download");
+  }
+  if (pos_dev) {
+    cudaStreamSynchronize(c->stream);
+    dfree(pos_dev);
+  }
+  if (rc) return rc;
+  return read_device_error(c);
+}
+
 int va_backbone_device(va_ctx* c, float* tokens_dev, int64_t rows, int gh, int gw, int view_count,
                        int first_layer, int last_layer, int alt_start, int cat_token,
                        const float* camera_dev, int n_out, const int* out_layers,
@@ -1313,8 +1513,8 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   fa.embed = heads * 64;
   fa.v_f16 = v_f16 ? 1 : 0;
   if (variant >= 0) {
-    if ((variant & 7) > 2 || (variant >> 3) > 5)
-      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..5)");
+    if ((variant & 7) > 2 || (variant >> 3) > 6)
+      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..6)");
     fa.poly_per8 = variant;
   }
   set_split_workspace(c, &fa);

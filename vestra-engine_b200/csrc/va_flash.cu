@@ -126,11 +126,12 @@ __device__ __forceinline__ SplitPos split_pos(const FlashArgs& fa) {
 // the CTAs of one head (same K/V) run together; units >= n_full are split over
 // `splits` key ranges of whole 128-key tiles.  Local attention: grid (query pairs
 // of a segment, heads, segments), never split.
+template <bool kSplit = true>
 __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
   Geom g;
   if (fa.seg_len == 0) {
     const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
-    const SplitPos sp = split_pos(fa);
+    const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{static_cast<int>(blockIdx.x), 0, 1, 0};
     g.head = sp.unit / qpairs;
     g.q0 = (sp.unit % qpairs) * 2 * kTileQ;
     g.q_end = fa.q_count;
@@ -551,13 +552,15 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // its 16-lane slice and, of every 8 key columns, the pair (2*(i%4), 2*(i%4)+1).
 // kOrder: the two query tiles take turns in the exponential section, as in the
 // "rows" layout.
-template <int kPoly, bool kOrder>
+// kSplit: the kernel has the split-tail merge (a launch with splits == 1 uses the
+// instance without it, which keeps fewer values live).
+template <int kPoly, bool kOrder, bool kSplit = true>
 __global__ void __launch_bounds__(kW20Threads, 1)
     flash_fwd_d64_w20_kernel(const __grid_constant__ CUtensorMap map_q,
                              const __grid_constant__ CUtensorMap map_k,
                              const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
   const Ctl c = make_ctl();
-  const Geom g = make_geom(fa);
+  const Geom g = make_geom<kSplit>(fa);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t tmem = cta_setup(c, g, 256, &map_q, &map_k, &map_v);
@@ -698,8 +701,8 @@ __global__ void __launch_bounds__(kW20Threads, 1)
         l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
         tmem_ld_16x256b_x8(tO, o);
       }
-      const SplitPos sp = split_pos(fa);
-      if (sp.nsplit > 1) {
+      const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{0, 0, 1, 0};
+      if (kSplit && sp.nsplit > 1) {
         // Split tail: publish this key range's partial rows, count the arrival, and
         // let the CTA that arrives last merge every split.  All 8 warps of the tile
         // get here (each wait above is bounded), so both named barriers complete.
@@ -831,28 +834,19 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
        flash_fwd_d64_w20_kernel<2, false>},
       {flash_fwd_d64_w20_kernel<0, true>, flash_fwd_d64_w20_kernel<1, true>,
        flash_fwd_d64_w20_kernel<2, true>}};
+  static const Kern w20_nosplit[3] = {flash_fwd_d64_w20_kernel<0, false, false>,
+                                      flash_fwd_d64_w20_kernel<1, false, false>,
+                                      flash_fwd_d64_w20_kernel<2, false, false>};
   Kern kern;
   int threads = kRowsThreads;
-  if (fa.v_f16) {
-    kern = flash_fwd_d64_kernel<true, 0, 0>;
-  } else {
+  bool w20_kernel = false, no_split = false;
+  if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (fa.poly_per8 < 0 || poly > 2 || form > 5) return cudaErrorInvalidValue;
-    if (form == 3 || form == 5) {
-      kern = w20[form == 5][poly];
-      threads = kW20Threads;
-      // setmaxnreg.inc draws on the registers the CTA launched with.
-      cudaFuncAttributes attr;
-      cudaError_t e = cudaFuncGetAttributes(&attr, kern);
-      if (e != cudaSuccess) return e;
-      if (attr.numRegs < kW20MinLaunchRegs) return cudaErrorInvalidConfiguration;
-    } else {
-      kern = rows[form][poly];
-    }
+    if (fa.poly_per8 < 0 || poly > 2 || form > 6) return cudaErrorInvalidValue;
+    w20_kernel = form == 3 || form == 5 || form == 6;
+    // form 6: form 3 with the split tail turned off (one CTA per unit).
+    no_split = form == 6;
   }
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       FlashSmem::kLaunchBytes);
-  if (e != cudaSuccess) return e;
   dim3 grid;
   if (fa.seg_len > 0) {
     grid = dim3((fa.seg_len + 2 * kTileQ - 1) / (2 * kTileQ), fa.heads, segs);
@@ -866,8 +860,7 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     const int num_kv = (fa.kv_rows + kTileK - 1) / kTileK;
     fa.n_full = units;
     fa.splits = 1;
-    const bool w20_kernel = threads == kW20Threads;
-    if (w20_kernel && fa.part_o && fa.part_ml && fa.counters && fa.sms > 0) {
+    if (w20_kernel && !no_split && fa.part_o && fa.part_ml && fa.counters && fa.sms > 0) {
       // The tail of `rem` units cut into s key ranges takes ceil(rem*s/sms) rounds
       // of 1/s unit time; pick the s with the shortest tail (each split also pays
       // a few percent for its own setup and the merge).
@@ -888,6 +881,29 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     }
     grid = dim3(fa.n_full + (units - fa.n_full) * fa.splits, 1, 1);
   }
+  if (fa.v_f16) {
+    kern = flash_fwd_d64_kernel<true, 0, 0>;
+  } else {
+    const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
+    if (w20_kernel) {
+      // A launch without a split (local, or global with splits == 1) runs the
+      // instance without the merge code.
+      kern = fa.splits > 1 ? w20[form == 5][poly]
+             : form == 5   ? w20[1][poly]
+                           : w20_nosplit[poly];
+      threads = kW20Threads;
+      // setmaxnreg.inc draws on the registers the CTA launched with.
+      cudaFuncAttributes attr;
+      cudaError_t e = cudaFuncGetAttributes(&attr, kern);
+      if (e != cudaSuccess) return e;
+      if (attr.numRegs < kW20MinLaunchRegs) return cudaErrorInvalidConfiguration;
+    } else {
+      kern = rows[form][poly];
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       FlashSmem::kLaunchBytes);
+  if (e != cudaSuccess) return e;
   kern<<<grid, threads, FlashSmem::kLaunchBytes, st>>>(mq, mk, mv, fa, err);
   return cudaGetLastError();
 }

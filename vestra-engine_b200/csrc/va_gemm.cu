@@ -301,6 +301,47 @@ struct ProjEpilogue {
   }
 };
 
+// Patch projection (patch_embed.rs:53-133 + pos_embed.rs:254-300): + bias + the
+// patch's interpolated position, F32 rows written straight to the token rows
+// (a view's patch rows follow its n_special rows, so a 128-row tile can end in one
+// view and continue in the next, which a TMA box cannot follow).
+struct PatchEpilogue {
+  PatchEpilogueArgs a;
+
+  __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const {
+    if (t < 128) cbuf[t] = a.bias[n0 + t];
+  }
+
+  template <int BN>
+  __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
+                                      const float* cbuf, uint32_t, bool valid) const {
+    static_assert(BN == 128, "patch tiles are 128 columns wide");
+    const int m = m0 + r;
+    const int view = m / a.n_patches, p = m - view * a.n_patches;
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int chunk = half * 2 + j;  // 32 columns
+      float x[32];
+      tmem_ld32(tmem_row + chunk * 32, x);  // warp-collective: every lane loads
+      if (!valid) continue;
+      const int col = n0 + chunk * 32;
+      const float4* pos = reinterpret_cast<const float4*>(a.pos + static_cast<size_t>(1 + p) * a.embed + col);
+      float4* out = reinterpret_cast<float4*>(
+          a.out + (static_cast<size_t>(view) * a.n_tok + a.n_special + p) * a.embed + col);
+      const float* bias = cbuf + chunk * 32;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 q = __ldg(pos + i);
+        out[i] = make_float4(x[4 * i] + bias[4 * i] + q.x, x[4 * i + 1] + bias[4 * i + 1] + q.y,
+                             x[4 * i + 2] + bias[4 * i + 2] + q.z, x[4 * i + 3] + bias[4 * i + 3] + q.w);
+      }
+    }
+  }
+
+  __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
+  __device__ __forceinline__ void store(int, int, int, uint32_t) const {}
+};
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t kABytes = kBM * kBK * 2;
@@ -496,6 +537,16 @@ cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, i
   e.a = epi;
   if (!encode_tma_2d_f32(&e.map_out, epi.out, n, m, 32, kBM)) return cudaErrorInvalidValue;
   return launch_gemm<128, 3>(a, w_t, m, n, k, e, err, st);
+}
+
+cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int k,
+                              const PatchEpilogueArgs& epi, int* err, cudaStream_t st) {
+  if (epi.rows <= 0 || epi.n_patches <= 0 || epi.embed % 128 != 0 || k % kBK != 0 || !epi.bias ||
+      !epi.pos || !epi.out || epi.n_tok != epi.n_special + epi.n_patches || epi.rows % epi.n_patches)
+    return cudaErrorInvalidValue;
+  PatchEpilogue e{};
+  e.a = epi;
+  return launch_gemm<128, 3>(a, w_t, epi.rows, epi.embed, k, e, err, st);
 }
 
 }  // namespace va

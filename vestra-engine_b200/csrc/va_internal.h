@@ -65,6 +65,19 @@ struct ProjEpilogueArgs {
   int embed;
 };
 
+// Patch projection epilogue: GEMM row m = patch p of view s (m = s*n_patches + p),
+// written to token row s*n_tok + n_special + p as conv + bias + pos[1 + p].
+struct PatchEpilogueArgs {
+  const float* bias;  // [E]
+  const float* pos;   // [(1 + n_patches)][E]: row 0 = CLS position, row 1 + p = patch p
+  float* out;         // [views][n_tok][E]
+  int rows;           // views * n_patches
+  int n_patches;
+  int n_tok;          // n_special + n_patches
+  int n_special;
+  int embed;
+};
+
 // ---- fused flash attention (K2) ----
 // Default softmax variant (poly + 8 * form): form 3 (four threads per row, 20
 // warps), every exponential on MUFU.
@@ -143,5 +156,22 @@ cudaError_t launch_capture(const float* x, const float* local_x, const float* g,
 cudaError_t launch_bounded_wait_selftest(unsigned long long limit_ns, int* err, cudaStream_t st);
 cudaError_t launch_permute_views(const float* src, float* dst, const int* order, int views,
                                  int64_t view_elems, cudaStream_t st);
+
+// ---- token input side (patch projection, CLS/register/position assembly) ----
+// NCHW F32 images [views][3][H][W] -> bf16 patch rows [views*gh*gw][kp], feature
+// index c*patch*patch + ky*patch + kx (the OIHW filter's flattening), zero past 3*patch^2.
+cudaError_t launch_patchify(const float* img, int views, int height, int width, int patch, int kp,
+                            __nv_bfloat16* rows, cudaStream_t st);
+// Bicubic (a = -0.75) resampling of the learned [grid*grid + 1][E] table to
+// [1 + gh*gw][E], CLS row copied.
+cudaError_t launch_pos_interp(const float* pos_embed, int grid, int embed, int gh, int gw,
+                              float interp_offset, float* out, cudaStream_t st);
+// Special rows of every view: row 0 = cls + pos[0], rows 1..n_register = registers.
+cudaError_t launch_token_specials(const float* cls, const float* pos, const float* registers,
+                                  int n_register, int views, int n_tok, int embed, float* out,
+                                  cudaStream_t st);
+// Patch projection GEMM: a = patch rows [rows][k] bf16, w_t = filter [E][k] bf16.
+cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int k,
+                              const PatchEpilogueArgs& epi, int* err, cudaStream_t st);
 
 }  // namespace va

@@ -8,6 +8,10 @@
 //                then bf16 token-major; one warp per row, two channels per lane.
 //   camera_inject  camera-token slots before block alt_start (backbone.rs:746-768).
 //   permute_views  view-order permutation (engine.rs:198-205 restore, backbone.rs:218-224).
+//   patchify / pos_interp / token_specials  the token input side (patch_embed.rs:53-133,
+//                pos_embed.rs:122-172, :254-300): NCHW images to bf16 patch rows for
+//                the projection GEMM, the bicubic position table, the CLS and
+//                register rows.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -210,7 +214,133 @@ __global__ void permute_views_kernel(const float4* src, float4* dst, const int* 
     d[i] = s[i];
 }
 
+// Patch rows for the projection GEMM (patch_embed.rs:53-133: a conv with
+// kernel = stride = patch and no padding is one GEMM over these rows).  Thread =
+// 8 consecutive features of one patch row (one 16-byte store).
+__global__ void patchify_kernel(const float* __restrict__ img, int views, int height, int width,
+                                int patch, int kp, __nv_bfloat16* __restrict__ rows) {
+  const int gw = width / patch, n_patches = (height / patch) * gw;
+  const int vec_per_row = kp / 8;
+  const int64_t total = static_cast<int64_t>(views) * n_patches * vec_per_row;
+  const int pp = patch * patch, features = 3 * pp;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / vec_per_row;
+    const int k0 = static_cast<int>(i - m * vec_per_row) * 8;
+    const int view = static_cast<int>(m / n_patches), p = static_cast<int>(m - static_cast<int64_t>(view) * n_patches);
+    const int py = p / gw, px = p - py * gw;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int k = k0 + e;
+      v[e] = 0.0f;
+      if (k < features) {
+        const int c = k / pp, rem = k - c * pp;
+        const int ky = rem / patch, kx = rem - ky * patch;
+        v[e] = __ldg(img + ((static_cast<size_t>(view) * 3 + c) * height + py * patch + ky) * width +
+                     px * patch + kx);
+      }
+    }
+    uint4 u;
+    u.x = pack_bf16x2(v[0], v[1]);
+    u.y = pack_bf16x2(v[2], v[3]);
+    u.z = pack_bf16x2(v[4], v[5]);
+    u.w = pack_bf16x2(v[6], v[7]);
+    reinterpret_cast<uint4*>(rows)[i] = u;
+  }
+}
+
+// Keys' cubic convolution kernel with a = -0.75 (pos_embed.rs:73-83), every
+// operation rounded separately so the table is bit-identical to an F32 CPU
+// evaluation in the same order.
+__device__ __forceinline__ float cubic_a075(float x) {
+  x = fabsf(x);
+  if (x < 1.0f) return __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(__fmul_rn(1.25f, x), 2.25f), x), x), 1.0f);
+  if (x < 2.0f)
+    return __fmul_rn(__fsub_rn(__fmul_rn(__fadd_rn(__fmul_rn(__fsub_rn(x, 5.0f), x), 8.0f), x), 4.0f),
+                     -0.75f);
+  return 0.0f;
+}
+
+// interpolate_pos_embed (pos_embed.rs:122-172): thread = one channel of one row.
+__global__ void pos_interp_kernel(const float* __restrict__ src, int grid, int embed, int gh, int gw,
+                                  float offset, float* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(1 + gh * gw) * embed;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / embed), ch = static_cast<int>(i - static_cast<int64_t>(row) * embed);
+    if (row == 0) {
+      out[i] = src[ch];
+      continue;
+    }
+    const int o = row - 1, oy = o / gw, ox = o - oy * gw;
+    const float m = static_cast<float>(grid);
+    const float sx = __fdiv_rn(__fadd_rn(static_cast<float>(gw), offset), m);
+    const float sy = __fdiv_rn(__fadd_rn(static_cast<float>(gh), offset), m);
+    const float iy = __fsub_rn(__fdiv_rn(__fadd_rn(static_cast<float>(oy), 0.5f), sy), 0.5f);
+    const float ix = __fsub_rn(__fdiv_rn(__fadd_rn(static_cast<float>(ox), 0.5f), sx), 0.5f);
+    const float y0f = floorf(iy), x0f = floorf(ix);
+    const int y0 = static_cast<int>(y0f), x0 = static_cast<int>(x0f);
+    const float fy = __fsub_rn(iy, y0f), fx = __fsub_rn(ix, x0f);
+    float acc = 0.0f;
+#pragma unroll
+    for (int dy = -1; dy <= 2; ++dy) {
+      const float wy = cubic_a075(__fsub_rn(fy, static_cast<float>(dy)));
+      const int yy = min(max(y0 + dy, 0), grid - 1);
+#pragma unroll
+      for (int dx = -1; dx <= 2; ++dx) {
+        const float wx = cubic_a075(__fsub_rn(fx, static_cast<float>(dx)));
+        const int xx = min(max(x0 + dx, 0), grid - 1);
+        const float s = __ldg(src + (static_cast<size_t>(1 + yy * grid + xx)) * embed + ch);
+        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(wy, wx), s));
+      }
+    }
+    out[i] = acc;
+  }
+}
+
+// Special rows of every view (pos_embed.rs:254-300): CLS + its position, then the
+// register tokens unchanged.
+__global__ void token_specials_kernel(const float* __restrict__ cls, const float* __restrict__ pos,
+                                      const float* __restrict__ registers, int n_tok, int embed,
+                                      float* __restrict__ out) {
+  const int view = blockIdx.x, row = blockIdx.y;
+  float* dst = out + (static_cast<size_t>(view) * n_tok + row) * embed;
+  for (int c = threadIdx.x; c < embed; c += blockDim.x)
+    dst[c] = row == 0 ? __fadd_rn(cls[c], pos[c]) : registers[static_cast<size_t>(row - 1) * embed + c];
+}
+
 }  // namespace
+
+cudaError_t launch_patchify(const float* img, int views, int height, int width, int patch, int kp,
+                            __nv_bfloat16* rows, cudaStream_t st) {
+  if (!img || !rows || views <= 0 || patch <= 0 || height % patch || width % patch || height <= 0 ||
+      width <= 0 || kp % 8 || kp < 3 * patch * patch)
+    return cudaErrorInvalidValue;
+  const int64_t total = static_cast<int64_t>(views) * (height / patch) * (width / patch) * (kp / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  patchify_kernel<<<blocks, 256, 0, st>>>(img, views, height, width, patch, kp, rows);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pos_interp(const float* pos_embed, int grid, int embed, int gh, int gw,
+                              float interp_offset, float* out, cudaStream_t st) {
+  if (!pos_embed || !out || grid <= 0 || embed <= 0 || gh <= 0 || gw <= 0) return cudaErrorInvalidValue;
+  const int64_t total = static_cast<int64_t>(1 + gh * gw) * embed;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  pos_interp_kernel<<<blocks, 256, 0, st>>>(pos_embed, grid, embed, gh, gw, interp_offset, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_token_specials(const float* cls, const float* pos, const float* registers,
+                                  int n_register, int views, int n_tok, int embed, float* out,
+                                  cudaStream_t st) {
+  if (!cls || !pos || !out || views <= 0 || n_register < 0 || (n_register > 0 && !registers) ||
+      n_tok <= n_register)
+    return cudaErrorInvalidValue;
+  token_specials_kernel<<<dim3(views, 1 + n_register), 256, 0, st>>>(cls, pos, registers, n_tok, embed, out);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_ln_cast(const float* x, const float* g, const float* b, float eps, int rows,
                            int embed, __nv_bfloat16* y, cudaStream_t st) {

@@ -104,3 +104,25 @@ def layer_weights(embed: int, seed: int = 0, layer: int = 0, qknorm: bool = True
 
 def camera_tokens(embed: int, seed: int = 0) -> np.ndarray:
     return rng(seed, 7).standard_normal(2 * embed, dtype=np.float32)
+
+
+def images(views: int, height: int, width: int, seed: int = 0) -> np.ndarray:
+    """Normalised NCHW images [views, 3, H, W] (preprocessed pixels are roughly N(0, 1))."""
+    return rng(seed, 8).standard_normal((views, 3, height, width), dtype=np.float32)
+
+
+def patch_embed_weights(embed: int, patch: int = 14, grid: int = 37, num_register: int = 0,
+                        seed: int = 0) -> dict:
+    """Patch filter [E, 3, p, p] (OIHW), bias [E], CLS [E], learned positions
+    [grid*grid + 1, E] and register tokens [num_register, E] (DA3: patch 14, 37x37)."""
+    r = rng(seed, 9)
+    p = {
+        "weight": (0.02 * r.standard_normal((embed, 3, patch, patch))).astype(np.float32),
+        "bias": (0.02 * r.standard_normal(embed)).astype(np.float32),
+        "cls": (0.02 * r.standard_normal(embed)).astype(np.float32),
+        "pos_embed": (0.02 * r.standard_normal((grid * grid + 1, embed))).astype(np.float32),
+        "registers": None,
+    }
+    if num_register:
+        p["registers"] = (0.02 * r.standard_normal((num_register, embed))).astype(np.float32)
+    return p

@@ -41,6 +41,7 @@ EXPORTED = [
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
     "va_attention_host_sharded",
     "va_op_attention_noalloc",
+    "va_load_patch_embed", "va_prepare_tokens_device", "va_prepare_tokens_host", "va_pos_embed_device",
 ]
 
 
@@ -118,6 +119,10 @@ def load_library(path: str = LIB_PATH):
         "va_block_device_sharded": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_run_tail_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_phase_times": ([_vp, _vp], c_int),
+        "va_load_patch_embed": ([_vp, _vp, _vp, _vp, _vp, i64, _vp, c_int, c_int, c_float], c_int),
+        "va_prepare_tokens_device": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp, _vp], c_int),
+        "va_prepare_tokens_host": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp], c_int),
+        "va_pos_embed_device": ([_vp, c_int, c_int, _vp, _vp], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -173,6 +178,7 @@ class ModelConfig:
     rope_freq: float = 100.0
     ln_eps: float = 1e-6
     alt_start: int = 4
+    patch_size: int = 14
 
     def to_va(self, max_rows: int, qk_norm_eps: float = 1e-5, rope_pairing: int = 0) -> VaConfig:
         return default_config(embed_dim=self.embed_dim, num_heads=self.num_heads, head_dim=self.head_dim,
@@ -376,6 +382,42 @@ class Context:
         when the bounded wait gave up as designed)."""
         return self.lib.va_selftest_bounded_wait(self.h, int(limit_us))
 
+    def load_patch_embed(self, weight_oihw, bias, cls_token, pos_embed, register_tokens=None, patch=14,
+                         interp_offset=0.1):
+        """Patch filter [E, 3, p, p], bias [E], CLS [E], learned positions [M*M + 1, E],
+        register tokens [num_register, E] (pos_embed.rs:23-39, patch_embed.rs:33-36)."""
+        w, b, c = _f32(weight_oihw), _f32(bias), _f32(cls_token)
+        pe = _f32(pos_embed).reshape(-1, self.cfg.embed_dim)
+        regs = None if register_tokens is None else _f32(register_tokens).reshape(-1, self.cfg.embed_dim)
+        nreg = 0 if regs is None else regs.shape[0]
+        self.check(self.lib.va_load_patch_embed(self.h, _ptr(w), _ptr(b), _ptr(c), _ptr(pe), pe.shape[0],
+                                                None if regs is None else _ptr(regs), nreg, patch,
+                                                float(interp_offset)))
+        self._patch = patch
+
+    def prepare_tokens_device(self, image_dev, views, height, width, tokens_dev, position_dev=None, stream=0):
+        """prepare_tokens for `views` NCHW images on the device -> view-major tokens
+        [views * (1 + num_register + gh*gw), E] (pos_embed.rs:236-300)."""
+        self.check(self.lib.va_prepare_tokens_device(self.h, _ptr(image_dev), views, height, width,
+                                                     None if position_dev is None else _ptr(position_dev),
+                                                     _ptr(tokens_dev), stream))
+
+    def prepare_tokens_host(self, images, height, width, position=None):
+        """Host images [views, 3, H, W] (or one [3, H, W]) -> tokens [views, n, E]."""
+        img = _f32(images).reshape(-1, 3, height, width)
+        views = img.shape[0]
+        patch = self._patch
+        n = 1 + self.cfg.num_register + (height // patch) * (width // patch)
+        out = np.empty((views, n, self.cfg.embed_dim), np.float32)
+        pos = None if position is None else _f32(position)
+        self.check(self.lib.va_prepare_tokens_host(self.h, _ptr(img), views, height, width,
+                                                   None if pos is None else _ptr(pos), _ptr(out)))
+        return out
+
+    def pos_embed_device(self, gh, gw, out_dev, stream=0):
+        """The interpolated position table [(1 + gh*gw), E] (PosEmbedCache::get_or_build)."""
+        self.check(self.lib.va_pos_embed_device(self.h, gh, gw, _ptr(out_dev), stream))
+
     def last_error(self) -> str:
         return self.lib.va_last_error(self.h).decode()
 
@@ -428,6 +470,40 @@ class CudaTransformerTailExecutor:
         del ln1, cfg
         t = np.asarray(tokens, np.float32).reshape(rows, self.cfg.embed_dim)
         return self.ctx.run_tail(layer_idx, t, gh, gw, view_count, global_)
+
+
+PATCH_EMBED_WEIGHT = "vit.patch_embed.weight"
+PATCH_EMBED_BIAS = "vit.patch_embed.bias"
+POS_EMBED_WEIGHT = "vit.pos_embed"
+CLS_TOKEN_WEIGHT = "vit.cls_token"
+REGISTER_TOKENS_WEIGHT = "vit.register_tokens"
+
+
+class CudaPatchEmbedExecutor:
+    """CudaPatchEmbedExecutor (patch_embed.rs:140-245) backed by the sm_100a path.
+
+    Uploads the patch filter, bias, CLS token, learned positions and (when the
+    model has them) register tokens once from the reference's `Weights` naming.
+    run() is the reference's run(image_nchw, height, width, position) for one
+    image: returns (gh, gw, tokens [1 + num_register + gh*gw, E]); position may be
+    None, in which case the interpolated table is built on the device and cached.
+    run_views() does several views in one call.  Errors raise.
+    """
+
+    def __init__(self, cfg: ModelConfig, weights: dict, device: int = 0, max_rows: int = 12 * 866):
+        self.cfg = cfg
+        self.ctx = Context(cfg.to_va(max_rows), device)
+        regs = weights.get(REGISTER_TOKENS_WEIGHT)
+        self.ctx.load_patch_embed(weights[PATCH_EMBED_WEIGHT], weights[PATCH_EMBED_BIAS],
+                                  weights[CLS_TOKEN_WEIGHT], weights[POS_EMBED_WEIGHT], regs, cfg.patch_size)
+
+    def run(self, image_nchw, height, width, position=None):
+        tokens = self.ctx.prepare_tokens_host(image_nchw, height, width, position)[0]
+        p = self.cfg.patch_size
+        return height // p, width // p, tokens
+
+    def run_views(self, images, height, width):
+        return self.ctx.prepare_tokens_host(images, height, width)
 
 
 def mlp_params_from_weights(weights: dict, i: int) -> dict:
