@@ -8,7 +8,9 @@ resident in HBM) -> QKV UMMA with QK-norm/RoPE epilogue -> fused flash attention
 output projection (F32).  With --gpus N > 1 the window's queries are split into N
 equal token slices (one process per GPU); the QKV epilogue stores every K'/V tile
 into the peers' windows over NVLink (NCCL all-gather where that is unavailable).
-The line also reports one whole block (attention + LN2/MLP) under "block".
+The line also reports one whole block (attention + LN2/MLP) under "block", the
+12-block window under "window", and the token input side (patch projection and
+position/CLS assembly of every view) under "tokens".
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -435,6 +437,37 @@ def run_ours(args):
                           "va_backbone_device_sharded (max over ranks)"}
     ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
 
+    # ---- token input side: this rank's views of 504x336 images -> tokens (patch
+    # projection GEMM + position/CLS/register assembly), no communication.
+    pw = syn.patch_embed_weights(wl.embed, 14, 37, wl.n_special - 1, seed=0)
+    ctx.load_patch_embed(pw["weight"], pw["bias"], pw["cls"], pw["pos_embed"], pw["registers"], 14)
+    v0, vrows = va.shard_views(wl.views, n_tok, world, rank)
+    my_views = vrows // n_tok
+    img_h, img_w = wl.gh * 14, wl.gw * 14
+    imgs = torch.from_numpy(syn.images(my_views, img_h, img_w, seed=rank)).cuda()
+    tk_out = torch.empty(vrows, wl.embed, device="cuda")
+    ctx.prepare_tokens_device(imgs, my_views, img_h, img_w, tk_out, stream=sp)  # builds the cached table
+    tok_ms = []
+    for i in range(args.warmup + args.steps):
+        flush_buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ctx.prepare_tokens_device(imgs, my_views, img_h, img_w, tk_out, stream=sp)
+        b.record(stream)
+        if i >= args.warmup:
+            tok_ms.append((a, b))
+    barrier()
+    ctx.check_device()
+    tok_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in tok_ms))
+    patches = wl.views * wl.gh * wl.gw
+    # image F32 read + token F32 write (+ the bf16 patch rows written and read back)
+    tok_bytes = wl.views * 3 * img_h * img_w * 4 + wl.rows * wl.embed * 4 + 2 * patches * 640 * 2
+    tokens = {"ms": round(tok_ms, 4), "bytes": tok_bytes,
+              "gbs": round(tok_bytes / (tok_ms * 1e-3) / 1e9, 1),
+              "gemm_tflops": round(2.0 * patches * 588 * wl.embed / (tok_ms * 1e-3) / 1e12, 1),
+              "what": "prepare_tokens of every view on device: patchify -> tcgen05 projection with "
+                      "bias + position epilogue -> CLS/register rows (max over ranks)"}
+
     # ---- dominant kernel alone (K2), same shapes, CUDA events on its stream
     # Q/K ~ N(0,1) per channel like QK-normalised rows; V bf16 (production path).
     g = torch.Generator(device="cuda").manual_seed(rank)
@@ -530,7 +563,7 @@ def run_ours(args):
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
                     "va_attention_host_sharded (C ABI, pinned host in/out, per rank)",
                     "max_abs_vs_device_path": e2e_diff},
-            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window,
+            "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

@@ -1229,7 +1229,12 @@ int va_prepare_tokens_device(va_ctx* c, const float* image, int views, int heigh
   const int E = c->cfg.embed_dim, n_special = 1 + p.n_register;
   const int n_tok = n_special + static_cast<int>(n_patches);
   __nv_bfloat16* rows = p.rows ? p.rows : c->x;
-  VA_CUDA(c, va::launch_patchify(image, views, height, width, p.patch, p.kp, rows, st));
+  const bool band = va::patchify_band_fits(width, p.patch, p.kp) && (reinterpret_cast<uintptr_t>(image) & 15) == 0;
+  if (band)
+    VA_CUDA(c, va::launch_patchify_band(image, views, height, width, p.patch, p.kp, rows, p.cls, pos, p.regs,
+                                        p.n_register, n_tok, E, tokens, st));
+  else
+    VA_CUDA(c, va::launch_patchify(image, views, height, width, p.patch, p.kp, rows, st));
   va::PatchEpilogueArgs ea{};
   ea.bias = p.bias;
   ea.pos = pos;
@@ -1240,7 +1245,8 @@ int va_prepare_tokens_device(va_ctx* c, const float* image, int views, int heigh
   ea.n_special = n_special;
   ea.embed = E;
   VA_CUDA(c, va::launch_patch_gemm(rows, p.w_t, p.kp, ea, c->err, st));
-  VA_CUDA(c, va::launch_token_specials(p.cls, pos, p.regs, p.n_register, views, n_tok, E, tokens, st));
+  if (!band)
+    VA_CUDA(c, va::launch_token_specials(p.cls, pos, p.regs, p.n_register, views, n_tok, E, tokens, st));
   return VA_OK;
 }
 

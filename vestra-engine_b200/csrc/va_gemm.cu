@@ -302,11 +302,19 @@ struct ProjEpilogue {
 };
 
 // Patch projection (patch_embed.rs:53-133 + pos_embed.rs:254-300): + bias + the
-// patch's interpolated position, F32 rows written straight to the token rows
-// (a view's patch rows follow its n_special rows, so a 128-row tile can end in one
-// view and continue in the next, which a TMA box cannot follow).
+// patch's interpolated position.  A tile whose 128 rows lie in one view is staged
+// as SWIZZLE_128B F32 tiles and sent by TMA through a 3-D map (columns, patch,
+// view) over the token rows after each view's specials; a tile that crosses a
+// view boundary (a box cannot follow the jump over the next view's special rows)
+// writes its rows directly.
 struct PatchEpilogue {
   PatchEpilogueArgs a;
+  CUtensorMap map_out;  // F32 (E, n_patches, views), strides (E, n_tok*E) floats, box 32 x 128 x 1
+
+  __device__ __forceinline__ bool one_view(int m0) const {
+    const int last = min(m0 + kBM - 1, a.rows - 1);
+    return m0 / a.n_patches == last / a.n_patches;
+  }
 
   __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const {
     if (t < 128) cbuf[t] = a.bias[n0 + t];
@@ -314,32 +322,57 @@ struct PatchEpilogue {
 
   template <int BN>
   __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
-                                      const float* cbuf, uint32_t, bool valid) const {
+                                      const float* cbuf, uint32_t out_smem, bool valid) const {
     static_assert(BN == 128, "patch tiles are 128 columns wide");
     const int m = m0 + r;
     const int view = m / a.n_patches, p = m - view * a.n_patches;
+    const bool staged = one_view(m0);
 #pragma unroll 1
     for (int j = 0; j < 2; ++j) {
       const int chunk = half * 2 + j;  // 32 columns
       float x[32];
       tmem_ld32(tmem_row + chunk * 32, x);  // warp-collective: every lane loads
-      if (!valid) continue;
       const int col = n0 + chunk * 32;
-      const float4* pos = reinterpret_cast<const float4*>(a.pos + static_cast<size_t>(1 + p) * a.embed + col);
-      float4* out = reinterpret_cast<float4*>(
-          a.out + (static_cast<size_t>(view) * a.n_tok + a.n_special + p) * a.embed + col);
-      const float* bias = cbuf + chunk * 32;
+      if (valid) {
+        const float4* pos = reinterpret_cast<const float4*>(a.pos + static_cast<size_t>(1 + p) * a.embed + col);
+        const float* bias = cbuf + chunk * 32;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 q = __ldg(pos + i);
-        out[i] = make_float4(x[4 * i] + bias[4 * i] + q.x, x[4 * i + 1] + bias[4 * i + 1] + q.y,
-                             x[4 * i + 2] + bias[4 * i + 2] + q.z, x[4 * i + 3] + bias[4 * i + 3] + q.w);
+        for (int i = 0; i < 8; ++i) {
+          const float4 q = __ldg(pos + i);
+          x[4 * i] = x[4 * i] + bias[4 * i] + q.x;
+          x[4 * i + 1] = x[4 * i + 1] + bias[4 * i + 1] + q.y;
+          x[4 * i + 2] = x[4 * i + 2] + bias[4 * i + 2] + q.z;
+          x[4 * i + 3] = x[4 * i + 3] + bias[4 * i + 3] + q.w;
+        }
+      }
+      if (staged) {
+        // Rows past the last patch are clipped by the store; their values are unused.
+        const uint32_t tile = out_smem + chunk * kOutTileBytes;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_shared_v4(tile + sw128_offset(r, c),
+                       make_uint4(__float_as_uint(x[4 * c]), __float_as_uint(x[4 * c + 1]),
+                                  __float_as_uint(x[4 * c + 2]), __float_as_uint(x[4 * c + 3])));
+      } else if (valid) {
+        float4* out = reinterpret_cast<float4*>(
+            a.out + (static_cast<size_t>(view) * a.n_tok + a.n_special + p) * a.embed + col);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]);
       }
     }
   }
 
   __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
-  __device__ __forceinline__ void store(int, int, int, uint32_t) const {}
+
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+    if (!one_view(m0)) return;
+    const int view = m0 / a.n_patches, p0 = m0 - view * a.n_patches;
+    for (int j = 0; j < 2; ++j) {
+      const int chunk = half * 2 + j;
+      tma_store_3d(&map_out, out_smem + chunk * kOutTileBytes, n0 + chunk * 32, p0, view);
+    }
+    bulk_commit_group();
+  }
 };
 
 template <int BN, int STAGES>
@@ -546,6 +579,11 @@ cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, 
     return cudaErrorInvalidValue;
   PatchEpilogue e{};
   e.a = epi;
+  const int views = epi.rows / epi.n_patches;
+  if (!encode_tma_3d_f32_strided(&e.map_out, epi.out + static_cast<size_t>(epi.n_special) * epi.embed,
+                                 epi.embed, epi.n_patches, views, static_cast<uint64_t>(epi.embed) * 4,
+                                 static_cast<uint64_t>(epi.n_tok) * epi.embed * 4, 32, kBM, 1))
+    return cudaErrorInvalidValue;
   return launch_gemm<128, 3>(a, w_t, epi.rows, epi.embed, k, e, err, st);
 }
 

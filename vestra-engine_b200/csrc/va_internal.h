@@ -126,6 +126,11 @@ bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
                        uint32_t box_inner, uint32_t box_outer);
 bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                         uint32_t b0, uint32_t b1, uint32_t b2);
+// F32 [d2][d1][d0] with explicit byte strides of dims 1 and 2 (rows of a view and
+// views), SWIZZLE_128B (box b0 * 4 bytes = 128).
+bool encode_tma_3d_f32_strided(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                               uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                               uint32_t b0, uint32_t b1, uint32_t b2);
 
 // Launchers return cudaSuccess or the launch error; kernels report device-side
 // failures through *err (see DevError in va_ptx.cuh).
@@ -162,6 +167,14 @@ cudaError_t launch_permute_views(const float* src, float* dst, const int* order,
 // index c*patch*patch + ky*patch + kx (the OIHW filter's flattening), zero past 3*patch^2.
 cudaError_t launch_patchify(const float* img, int views, int height, int width, int patch, int kp,
                             __nv_bfloat16* rows, cudaStream_t st);
+// Band form for patch 14 (kp 640) and width % 4 == 0 with the band in shared memory:
+// also writes every view's special rows (as launch_token_specials).
+constexpr int kPatchBandMaxSmem = 200 * 1024;
+bool patchify_band_fits(int width, int patch, int kp);
+cudaError_t launch_patchify_band(const float* img, int views, int height, int width, int patch, int kp,
+                                 __nv_bfloat16* rows, const float* cls, const float* pos,
+                                 const float* registers, int n_register, int n_tok, int embed,
+                                 float* tokens, cudaStream_t st);
 // Bicubic (a = -0.75) resampling of the learned [grid*grid + 1][E] table to
 // [1 + gh*gw][E], CLS row copied.
 cudaError_t launch_pos_interp(const float* pos_embed, int grid, int embed, int gh, int gw,

@@ -69,6 +69,23 @@ bool encode_tma_2d_f32(CUtensorMap* map, const void* base, uint64_t inner, uint6
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_tma_3d_f32_strided(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                               uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                               uint32_t b0, uint32_t b1, uint32_t b2) {
+  if (!get_encode() || base == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (d0 * 4) % 16 != 0 || stride1_bytes % 16 ||
+      stride2_bytes % 16)
+    return false;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_tma_3d_bf16(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                         uint32_t b0, uint32_t b1, uint32_t b2) {
   if (!get_encode() || base == nullptr) return false;
@@ -216,37 +233,119 @@ __global__ void permute_views_kernel(const float4* src, float4* dst, const int* 
 
 // Patch rows for the projection GEMM (patch_embed.rs:53-133: a conv with
 // kernel = stride = patch and no padding is one GEMM over these rows).  Thread =
-// 8 consecutive features of one patch row (one 16-byte store).
+// 8 consecutive features of one patch row (one 16-byte store).  kPatch > 0 fixes
+// the patch size at compile time so the feature -> (c, ky, kx) split is
+// multiply-shift arithmetic; kPatch = 0 reads it from `patch`.  32-bit indices
+// (the launcher checks the range).
+template <int kPatch>
 __global__ void patchify_kernel(const float* __restrict__ img, int views, int height, int width,
-                                int patch, int kp, __nv_bfloat16* __restrict__ rows) {
+                                int patch_rt, int kp_rt, __nv_bfloat16* __restrict__ rows) {
+  const int patch = kPatch > 0 ? kPatch : patch_rt;
+  const int kp = kPatch > 0 ? (3 * kPatch * kPatch + 63) / 64 * 64 : kp_rt;
   const int gw = width / patch, n_patches = (height / patch) * gw;
   const int vec_per_row = kp / 8;
-  const int64_t total = static_cast<int64_t>(views) * n_patches * vec_per_row;
+  const int total = views * n_patches * vec_per_row;
   const int pp = patch * patch, features = 3 * pp;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t m = i / vec_per_row;
-    const int k0 = static_cast<int>(i - m * vec_per_row) * 8;
-    const int view = static_cast<int>(m / n_patches), p = static_cast<int>(m - static_cast<int64_t>(view) * n_patches);
-    const int py = p / gw, px = p - py * gw;
-    float v[8];
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int m = i / vec_per_row;
+    const int k0 = (i - m * vec_per_row) * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (k0 < features) {
+      const int view = m / n_patches, p = m - view * n_patches;
+      const int py = p / gw, px = p - py * gw;
+      const float* base = img + (static_cast<size_t>(view) * 3 * height + py * patch) * width + px * patch;
+      float v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int k = k0 + e;
-      v[e] = 0.0f;
-      if (k < features) {
-        const int c = k / pp, rem = k - c * pp;
-        const int ky = rem / patch, kx = rem - ky * patch;
-        v[e] = __ldg(img + ((static_cast<size_t>(view) * 3 + c) * height + py * patch + ky) * width +
-                     px * patch + kx);
+      for (int e = 0; e < 8; ++e) {
+        const int k = k0 + e;
+        v[e] = 0.0f;
+        if (k < features) {
+          const int c = k / pp, rem = k - c * pp;
+          const int ky = rem / patch, kx = rem - ky * patch;
+          v[e] = __ldg(base + (static_cast<size_t>(c) * height + ky) * width + kx);
+        }
+      }
+      u.x = pack_bf16x2(v[0], v[1]);
+      u.y = pack_bf16x2(v[2], v[3]);
+      u.z = pack_bf16x2(v[4], v[5]);
+      u.w = pack_bf16x2(v[6], v[7]);
+    }
+    reinterpret_cast<uint4*>(rows)[i] = u;
+  }
+}
+
+// Band form of the same, for the usual shapes: one CTA per (view, row of patches)
+// reads the band's 3 x kPatch image rows once, coalesced, into shared memory, then
+// writes the band's gw patch rows as 16-byte groups of 8 features (thread = one
+// group of one patch, patches fastest: two-way bank conflicts at most).  The last
+// `views` CTAs write each view's special rows instead (CLS + its position,
+// registers), which saves a launch.
+template <int kPatch>
+__global__ void __launch_bounds__(256) patchify_band_kernel(
+    const float* __restrict__ img, int views, int height, int width, int kp,
+    __nv_bfloat16* __restrict__ rows, const float* __restrict__ cls, const float* __restrict__ pos,
+    const float* __restrict__ regs, int n_register, int n_tok, int embed, float* __restrict__ tokens) {
+  extern __shared__ float band[];  // [3 * kPatch][width]
+  constexpr int kPP = kPatch * kPatch, kFeat = 3 * kPP;
+  const int gh = height / kPatch, gw = width / kPatch;
+  const int b = blockIdx.x;
+  if (b >= views * gh) {
+    const int view = b - views * gh;
+    float* dst = tokens + static_cast<size_t>(view) * n_tok * embed;
+    for (int i = threadIdx.x; i < (1 + n_register) * embed; i += blockDim.x) {
+      const int row = i / embed, c = i - row * embed;
+      dst[i] = row == 0 ? __fadd_rn(cls[c], pos[c]) : regs[static_cast<size_t>(row - 1) * embed + c];
+    }
+    return;
+  }
+  const int view = b / gh, py = b - view * gh;
+  // The band's rows are contiguous per channel: channel c starts at image row
+  // py*kPatch and spans kPatch*width floats.  Eight loads per thread are in flight
+  // before their shared-memory stores.
+  const int chan_f4 = kPatch * width / 4, total_f4 = 3 * chan_f4;
+  constexpr int kUnroll = 8;
+  for (int i0 = threadIdx.x; i0 < total_f4; i0 += blockDim.x * kUnroll) {
+    float4 v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < total_f4) {
+        const int c = i / chan_f4, j = i - c * chan_f4;
+        v[u] = __ldg(reinterpret_cast<const float4*>(
+                         img + ((static_cast<size_t>(view) * 3 + c) * height + py * kPatch) * width) + j);
       }
     }
-    uint4 u;
-    u.x = pack_bf16x2(v[0], v[1]);
-    u.y = pack_bf16x2(v[2], v[3]);
-    u.z = pack_bf16x2(v[4], v[5]);
-    u.w = pack_bf16x2(v[6], v[7]);
-    reinterpret_cast<uint4*>(rows)[i] = u;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < total_f4) reinterpret_cast<float4*>(band)[i] = v[u];
+    }
+  }
+  __syncthreads();
+  const int groups = kp / 8;
+  __nv_bfloat16* out = rows + static_cast<size_t>(b) * gw * kp;  // patch rows of this band
+  for (int i = threadIdx.x; i < gw * groups; i += blockDim.x) {
+    const int g = i / gw, px = i - g * gw;
+    const int k0 = g * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (k0 < kFeat) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int k = k0 + e;
+        v[e] = 0.0f;
+        if (k < kFeat) {
+          const int c = k / kPP, rem = k - c * kPP;
+          const int ky = rem / kPatch, kx = rem - ky * kPatch;
+          v[e] = band[(c * kPatch + ky) * width + px * kPatch + kx];
+        }
+      }
+      u.x = pack_bf16x2(v[0], v[1]);
+      u.y = pack_bf16x2(v[2], v[3]);
+      u.z = pack_bf16x2(v[4], v[5]);
+      u.w = pack_bf16x2(v[6], v[7]);
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(px) * kp + k0) = u;
   }
 }
 
@@ -318,8 +417,36 @@ cudaError_t launch_patchify(const float* img, int views, int height, int width, 
       width <= 0 || kp % 8 || kp < 3 * patch * patch)
     return cudaErrorInvalidValue;
   const int64_t total = static_cast<int64_t>(views) * (height / patch) * (width / patch) * (kp / 8);
+  if (total >= (int64_t{1} << 31) || static_cast<int64_t>(views) * 3 * height * width >= (int64_t{1} << 40))
+    return cudaErrorInvalidValue;
   const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
-  patchify_kernel<<<blocks, 256, 0, st>>>(img, views, height, width, patch, kp, rows);
+  if (patch == 14 && kp == 640)
+    patchify_kernel<14><<<blocks, 256, 0, st>>>(img, views, height, width, patch, kp, rows);
+  else
+    patchify_kernel<0><<<blocks, 256, 0, st>>>(img, views, height, width, patch, kp, rows);
+  return cudaGetLastError();
+}
+
+bool patchify_band_fits(int width, int patch, int kp) {
+  return patch == 14 && kp == 640 && width % 4 == 0 &&
+         static_cast<int64_t>(3) * patch * width * 4 <= kPatchBandMaxSmem;
+}
+
+cudaError_t launch_patchify_band(const float* img, int views, int height, int width, int patch, int kp,
+                                 __nv_bfloat16* rows, const float* cls, const float* pos,
+                                 const float* registers, int n_register, int n_tok, int embed,
+                                 float* tokens, cudaStream_t st) {
+  if (!img || !rows || !cls || !pos || !tokens || views <= 0 || height <= 0 || height % patch ||
+      width % patch || !patchify_band_fits(width, patch, kp) || (reinterpret_cast<uintptr_t>(img) & 15) ||
+      (n_register > 0 && !registers) ||
+      n_tok != 1 + n_register + (height / patch) * (width / patch))
+    return cudaErrorInvalidValue;
+  const int smem = 3 * patch * width * 4;
+  auto kern = patchify_band_kernel<14>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<views * (height / patch) + views, 256, smem, st>>>(img, views, height, width, kp, rows, cls, pos,
+                                                            registers, n_register, n_tok, embed, tokens);
   return cudaGetLastError();
 }
 
