@@ -23,6 +23,9 @@
 // box row), which is exactly the UMMA K-major SW128 canonical layout.
 #include <math.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "va_internal.h"
 #include "va_ptx.cuh"
 
@@ -112,6 +115,9 @@ constexpr uint32_t kOutTileBytes = 16384;
 struct QkvEpilogue {
   QkvEpilogueArgs a;
   CUtensorMap map_out[3];  // Q, K, V: [rows][E] 2-byte, box 64 x 128
+
+  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
 
   // cbuf: [0, 256) bias of the tile's columns, [256, 320) gamma, [320, 384) beta of
   // the section's QK-norm (1 and 0 when the section has none).
@@ -206,6 +212,9 @@ struct Fc1Epilogue {
   Fc1EpilogueArgs a;
   CUtensorMap map_out;  // bf16 [rows][hidden], box 64 x 128
 
+  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
+
   __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const { cbuf[t] = a.bias[n0 + t]; }
 
   template <int BN>
@@ -245,6 +254,17 @@ struct Fc1Epilogue {
 struct ProjEpilogue {
   ProjEpilogueArgs a;
   CUtensorMap map_out;  // F32 [rows][embed], box 32 x 128
+  CUtensorMap map_res;  // the residual, same boxes (persistent kernel: prefetched by TMA)
+  int res_staged = 0;   // 1: the residual tile is already in the staging tiles when run() starts
+
+  // Bytes one half's store thread prefetches into its staging tiles per tile.
+  __device__ __forceinline__ uint32_t prefetch_bytes() const { return res_staged ? 2 * kOutTileBytes : 0; }
+  __device__ __forceinline__ void prefetch(int half, int m0, int n0, uint32_t out_smem, uint32_t bar) const {
+    for (int j = 0; j < 2; ++j) {
+      const int chunk = half * 2 + j;
+      tma_load_2d(out_smem + chunk * kOutTileBytes, &map_res, bar, n0 + chunk * 32, m0);
+    }
+  }
 
   // cbuf: [0, 128) bias (0 when absent), [128, 256) ls1 (1 when absent).
   __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const {
@@ -268,7 +288,17 @@ struct ProjEpilogue {
         const float* ls1 = cbuf + 128 + chunk * 32;
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[i] = (x[i] + bias[i]) * ls1[i];
-        if (a.residual) {
+        if (a.residual && res_staged) {
+          const uint32_t tile = out_smem + chunk * kOutTileBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = ld_shared_v4(tile + sw128_offset(r, c));
+            x[4 * c] += __uint_as_float(v.x);
+            x[4 * c + 1] += __uint_as_float(v.y);
+            x[4 * c + 2] += __uint_as_float(v.z);
+            x[4 * c + 3] += __uint_as_float(v.w);
+          }
+        } else if (a.residual) {
           const float4* res = reinterpret_cast<const float4*>(
               a.residual + static_cast<size_t>(m0 + r) * a.embed + n0 + chunk * 32);
 #pragma unroll
@@ -310,6 +340,9 @@ struct ProjEpilogue {
 struct PatchEpilogue {
   PatchEpilogueArgs a;
   CUtensorMap map_out;  // F32 (E, n_patches, views), strides (E, n_tok*E) floats, box 32 x 128 x 1
+
+  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
 
   __device__ __forceinline__ bool one_view(int m0) const {
     const int last = min(m0 + kBM - 1, a.rows - 1);
@@ -540,6 +573,266 @@ cudaError_t launch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, i
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Persistent form: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+//   warp 0      TMA producer over all tiles' K slabs (STAGES-deep ring)
+//   warp 1      TMEM owner + UMMA issuer; tile i accumulates into TMEM buffer i&1
+//   warps 2..9  epilogue of tile i from buffer i&1 while tile i+1 accumulates
+//               into the other; output tiles staged in their own 64 KB region
+// so neither the operand loads nor the epilogue wait for each other across tiles.
+// A tile is MT x 128 rows by BN columns: MT = 2 gives each loaded B slab twice the
+// UMMA work (two M=128 accumulators side by side in TMEM), which halves the B
+// traffic per FLOP of the narrow (N = E) projections; the epilogue then runs one
+// pass per 128-row half.
+// ---------------------------------------------------------------------------
+template <int BN, int MT, int STAGES>
+struct PersistentSmem {
+  static constexpr uint32_t kABytes = MT * kBM * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kStagingOffset = STAGES * kStageBytes;
+  static constexpr uint32_t kBarOffset = kStagingOffset + 4 * kOutTileBytes;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], final, prefetch[2]; then the TMEM
+  // slot and flags
+  static constexpr uint32_t kNumBars = 2 * STAGES + 7;
+  static constexpr uint32_t kSlotOffset = kBarOffset + 8 * kNumBars;
+  static constexpr uint32_t kConstOffset = kBarOffset + 256;
+  static constexpr uint32_t kBytes = kConstOffset + 2048;
+  static constexpr uint32_t kLaunchBytes = kBytes + 1024;
+  static_assert(kSlotOffset + 32 <= kConstOffset, "barrier region too small");
+  static_assert(kLaunchBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kStageBytes % 1024 == 0, "SW128 tiles need 1024-byte alignment");
+  static_assert(2 * MT * BN <= 512, "two accumulator buffers must fit in TMEM");
+};
+
+template <int BN, int MT, int STAGES, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_persistent(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b, int M, int K, int n_tiles_n,
+                         int num_tiles, const __grid_constant__ Epi epi, int* err) {
+  using L = PersistentSmem<BN, MT, STAGES>;
+  constexpr int kTileM = MT * kBM;
+  constexpr uint32_t kTmemCols = 2 * MT * BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = K / kBK;
+
+  const uint32_t bar0 = base_u32 + L::kBarOffset;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t final_bar = bar0 + 8u * (2 * STAGES + 4);
+  auto pre_bar = [&](int h) { return bar0 + 8u * (2 * STAGES + 5 + h); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kSlotOffset);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* issued = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* consumed = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* mma_started = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  auto sA = [&](int s) { return base_u32 + s * L::kStageBytes; };
+  auto sB = [&](int s) { return base_u32 + s * L::kStageBytes + L::kABytes; };
+  const uint32_t staging = base_u32 + L::kStagingOffset;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 256);
+    }
+    mbar_init(final_bar, 1);
+    mbar_init(pre_bar(0), 1);
+    mbar_init(pre_bar(1), 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    *mma_started = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles_n) * kTileM, n0 = (tile % n_tiles_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!(ok = mbar_wait(empty_bar(s), ph ^ 1, abort_flag, err, kDevTimeoutProducer))) break;
+          mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
+          tma_load_2d(sA(s), &map_a, full_bar(s), kb * kBK, m0);
+          tma_load_2d(sB(s), &map_b, full_bar(s), kb * kBK, n0);
+          *issued = g + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, false, false);
+      *mma_started = 1;
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        // The epilogue has drained this buffer (tile i-2).
+        if (!(ok = mbar_wait(tempty_bar(b), ((i >> 1) & 1) ^ 1, abort_flag, err, kDevTimeoutMma))) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * MT * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++g) {
+          const int s = g % STAGES;
+          const uint32_t ph = (g / STAGES) & 1;
+          if (!(ok = mbar_wait(full_bar(s), ph, abort_flag, err, kDevTimeoutMma))) break;
+          *consumed = g + 1;
+          tc_fence_after();
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              const uint64_t ad = sdesc_sw128(sA(s) + mt * kBM * 128 + k * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(sB(s) + k * 32, 16, 1024);
+              umma_ss(acc + mt * BN, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+          tc_commit(empty_bar(s));
+        }
+        if (ok) tc_commit(tfull_bar(b));
+      }
+      // Always committed: marks the moment every UMMA of this CTA has finished.
+      tc_commit(final_bar);
+    }
+  } else {
+    // Epilogue warps 2..9.  The tile loop has the same trip count for all 256
+    // threads and never exits early, so every named barrier completes; after an
+    // abort the work is skipped.
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+    const int row = quad * 32 + lane;
+    const int t = threadIdx.x - 64;
+    const bool store_thread = ((warp - 2) & 3) == 0 && lane == 0;
+    float* cbuf = reinterpret_cast<float*>(smem + L::kConstOffset);
+    const uint32_t pre_bytes = epi.prefetch_bytes();
+    int i = 0, pre_uses = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
+      const int b = i & 1;
+      const int n0 = (tile % n_tiles_n) * BN;
+      bool ok = true;
+      for (int pass = 0; pass < MT; ++pass) {
+        const int m0 = (tile / n_tiles_n) * kTileM + pass * kBM;
+        // A second half that starts past the last row has nothing to load or store.
+        const bool rows_here = m0 < M;
+        const bool pre = pre_bytes != 0 && rows_here;
+        // The previous pass's stores have read the staging tiles, and every thread
+        // is done with its constants and its peer copies.
+        if (store_thread) bulk_wait_all_read();
+        named_bar_sync(1, 256);
+        // Operands of the epilogue that do not depend on the accumulator (the
+        // residual tile) start loading into this half's staging tiles now.
+        if (pre && store_thread) {
+          mbar_arrive_expect_tx(pre_bar(half), pre_bytes);
+          epi.prefetch(half, m0, n0, staging, pre_bar(half));
+        }
+        if (pass == 0) epi.stage(cbuf, n0, t);
+        named_bar_sync(1, 256);
+        if (pass == 0) {
+          ok = mbar_wait(tfull_bar(b), (i >> 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+        }
+        // Waited for even after an abort: the copy must land before the CTA exits.
+        if (pre) drain_wait(pre_bar(half), (pre_uses++) & 1);
+        if (ok) {
+          tc_fence_after();
+          epi.template run<BN>(tmem + b * MT * BN + pass * BN + (static_cast<uint32_t>(quad * 32) << 16), row,
+                               m0, n0, half, cbuf, staging, (m0 + row) < M);
+          if (pass == MT - 1) {
+            tc_fence_before();
+            mbar_arrive(tempty_bar(b));
+          }
+        }
+        fence_proxy_async_smem();  // the staged tiles are read by the TMA store
+        named_bar_sync(2 + half, 128);
+        if (ok && rows_here && store_thread) epi.store(half, m0, n0, staging);
+        if (ok && rows_here) epi.peer_copy(half, t - 128 * half, m0, M, n0, staging);
+      }
+    }
+    if (store_thread) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (*abort_flag)
+      for (int g = *consumed; g < *issued; ++g) drain_wait(full_bar(g % STAGES), (g / STAGES) & 1);
+    if (*mma_started) drain_wait(final_bar, 0);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int device_sms() {
+  static int sms = [] {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+  }();
+  return sms;
+}
+
+template <int BN, int MT, int STAGES, class Epi>
+cudaError_t launch_gemm_persistent(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K,
+                                   const Epi& epi, int* err, cudaStream_t st) {
+  if (M <= 0 || N % BN != 0 || K % kBK != 0 || K <= 0) return cudaErrorInvalidValue;
+  CUtensorMap map_a, map_b;
+  if (!encode_tma_2d_bf16(&map_a, a, K, M, kBK, MT * kBM)) return cudaErrorInvalidValue;
+  if (!encode_tma_2d_bf16(&map_b, b, K, N, kBK, BN)) return cudaErrorInvalidValue;
+  using L = PersistentSmem<BN, MT, STAGES>;
+  auto kern = gemm_bf16_persistent<BN, MT, STAGES, Epi>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       L::kLaunchBytes);
+  if (e != cudaSuccess) return e;
+  const int n_tiles_n = N / BN;
+  const int num_tiles = n_tiles_n * ((M + MT * kBM - 1) / (MT * kBM));
+  const int grid = std::min(num_tiles, device_sms());
+  kern<<<grid, kGemmThreads, L::kLaunchBytes, st>>>(map_a, map_b, M, K, n_tiles_n, num_tiles, epi, err);
+  return cudaGetLastError();
+}
+
+bool gemm_per_tile() {
+  static const bool per_tile = std::getenv("VA_GEMM_PER_TILE") != nullptr;
+  return per_tile;
+}
+
+// One place picks the kernel form for every GEMM of the path.
+template <int BN, int STAGES_TILE, int MT, int STAGES_PERSIST, class Epi>
+cudaError_t run_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K, const Epi& epi,
+                     int* err, cudaStream_t st) {
+  if (gemm_per_tile()) return launch_gemm<BN, STAGES_TILE>(a, b, M, N, K, epi, err, st);
+  return launch_gemm_persistent<BN, MT, STAGES_PERSIST>(a, b, M, N, K, epi, err, st);
+}
+
 }  // namespace
 
 cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t, int rows,
@@ -551,7 +844,7 @@ cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t
       !encode_tma_2d_bf16(&e.map_out[1], epi.k_out, embed, rows, 64, kBM) ||
       !encode_tma_2d_bf16(&e.map_out[2], epi.v_out, embed, rows, 64, kBM))
     return cudaErrorInvalidValue;
-  return launch_gemm<256, 2>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
+  return run_gemm<256, 2, 1, 3>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
 }
 
 cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
@@ -560,7 +853,7 @@ cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, in
   Fc1Epilogue e{};
   e.a = epi;
   if (!encode_tma_2d_bf16(&e.map_out, epi.out, n, m, 64, kBM)) return cudaErrorInvalidValue;
-  return launch_gemm<256, 2>(a, w_t, m, n, k, e, err, st);
+  return run_gemm<256, 2, 1, 3>(a, w_t, m, n, k, e, err, st);
 }
 
 cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
@@ -569,7 +862,11 @@ cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, i
   ProjEpilogue e{};
   e.a = epi;
   if (!encode_tma_2d_f32(&e.map_out, epi.out, n, m, 32, kBM)) return cudaErrorInvalidValue;
-  return launch_gemm<128, 3>(a, w_t, m, n, k, e, err, st);
+  if (epi.residual && !gemm_per_tile()) {
+    if (!encode_tma_2d_f32(&e.map_res, epi.residual, n, m, 32, kBM)) return cudaErrorInvalidValue;
+    e.res_staged = 1;
+  }
+  return run_gemm<128, 3, 2, 3>(a, w_t, m, n, k, e, err, st);
 }
 
 cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int k,
@@ -584,7 +881,7 @@ cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, 
                                  epi.embed, epi.n_patches, views, static_cast<uint64_t>(epi.embed) * 4,
                                  static_cast<uint64_t>(epi.n_tok) * epi.embed * 4, 32, kBM, 1))
     return cudaErrorInvalidValue;
-  return launch_gemm<128, 3>(a, w_t, epi.rows, epi.embed, k, e, err, st);
+  return run_gemm<128, 3, 2, 3>(a, w_t, epi.rows, epi.embed, k, e, err, st);
 }
 
 }  // namespace va
