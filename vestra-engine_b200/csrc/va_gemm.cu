@@ -830,6 +830,12 @@ template <int BN, int STAGES_TILE, int MT, int STAGES_PERSIST, class Epi>
 cudaError_t run_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K, const Epi& epi,
                      int* err, cudaStream_t st) {
   if (gemm_per_tile()) return launch_gemm<BN, STAGES_TILE>(a, b, M, N, K, epi, err, st);
+  if constexpr (MT == 2) {
+    // 256-row tiles only when they still fill every SM; a short call (one chunk of
+    // the host pipeline, one rank's slice) keeps twice as many 128-row tiles.
+    if (static_cast<int64_t>((M + 2 * kBM - 1) / (2 * kBM)) * (N / BN) < device_sms())
+      return launch_gemm_persistent<BN, 1, 4>(a, b, M, N, K, epi, err, st);
+  }
   return launch_gemm_persistent<BN, MT, STAGES_PERSIST>(a, b, M, N, K, epi, err, st);
 }
 
