@@ -497,10 +497,10 @@ def run_ours(args):
     variants = {}
     if args.variants:
         to_tf = lambda ms: round(flash_flops / (ms * 1e-3) / 1e12, 2)  # noqa: E731
-        for form in (0, 2, 3, 5, 6):
+        for form in (0, 2, 3, 5, 6, 7):
             for p in range(3):
-                name = {3: f"w20_poly{p}", 5: f"w20ord_poly{p}",
-                        6: f"w20nosplit_poly{p}"}.get(form, f"form{form}_poly{p}")
+                name = {3: f"w20_poly{p}", 5: f"w20ord_poly{p}", 6: f"w20nosplit_poly{p}",
+                        7: f"w20splitp_poly{p}"}.get(form, f"form{form}_poly{p}")
                 variants[name] = to_tf(time_flash(vw, p + 8 * form))
         variants["f16_p"] = to_tf(time_flash(vw.to(torch.float16)))
     peak_tflops, _, peak_kind = load_peaks()

@@ -77,8 +77,8 @@ struct FlashSmem {
   static constexpr uint32_t kV = kK + kStages * kTileBytes;      // V ring
   static constexpr uint32_t kBar = kV + kStages * kTileBytes;
   // barriers: q_full, kv_full[S], kv_empty[S], then per tile s_full, s_free,
-  // p_full, pv_done, o_final, ex_done
-  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 12;
+  // p_full, pv_done, o_final, ex_done, p_full_hi, pv_done_hi
+  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 16;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kBytes = kMisc + 64;
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;
@@ -168,6 +168,9 @@ struct Ctl {
   __device__ uint32_t pv_done(int t) const { return bar(7 + 2 * kStages + t); }
   __device__ uint32_t o_final(int t) const { return bar(9 + 2 * kStages + t); }
   __device__ uint32_t ex_done(int t) const { return bar(11 + 2 * kStages + t); }
+  // Split P hand-off: p_full / pv_done then cover keys 0..63 of the tile, these 64..127.
+  __device__ uint32_t p_full_hi(int t) const { return bar(13 + 2 * kStages + t); }
+  __device__ uint32_t pv_done_hi(int t) const { return bar(15 + 2 * kStages + t); }
   __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(smem + FlashSmem::kMisc); }
   __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 4); }
   __device__ volatile int* kv_issued() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 8); }
@@ -213,6 +216,8 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int s
       mbar_init(c.pv_done(t), 1);
       mbar_init(c.o_final(t), 1);
       mbar_init(c.ex_done(t), softmax_threads);
+      mbar_init(c.p_full_hi(t), softmax_threads);
+      mbar_init(c.pv_done_hi(t), 1);
     }
     *c.abort_flag() = 0;
     *c.kv_issued() = 0;
@@ -262,7 +267,10 @@ __device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const 
 // and each group of 4 (QK) or 8 (PV) UMMAs is issued from one asm block, so the
 // issuing thread spends few instructions per UMMA while the softmax warps of its
 // sub-partition compete for issue slots.
-template <bool kF16>
+// kSplitP: P arrives in two halves of 64 keys (p_full, then p_full_hi) and PV runs as
+// two groups of 4 UMMAs committed separately (pv_done, pv_done_hi), so the PV of the
+// first half overlaps the exponentials of the second.
+template <bool kF16, bool kSplitP = false>
 __device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32_t tmem, int t,
                                              int* err) {
   constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
@@ -296,8 +304,19 @@ __device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32
     ok = mbar_wait(c.p_full(t), j & 1, abort_flag, err, kDevTimeoutMma);
     if (!ok) break;
     tc_fence_after();
-    umma_ts_k128_mn(tO, tP, dv0 + s * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
-    tc_commit(c.pv_done(t));
+    if constexpr (kSplitP) {
+      umma_ts_k64_mn(tO, tP, dv0 + s * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
+      tc_commit(c.pv_done(t));
+      ok = mbar_wait(c.p_full_hi(t), j & 1, abort_flag, err, kDevTimeoutMma);
+      if (!ok) break;
+      tc_fence_after();
+      // Keys 64..127: P columns 32..63, V rows 64..127 (64 rows of 128 B = 512 units).
+      umma_ts_k64_mn(tO, tP + 32, dv0 + s * kStageStep + 512, idesc_pv, 1u);
+      tc_commit(c.pv_done_hi(t));
+    } else {
+      umma_ts_k128_mn(tO, tP, dv0 + s * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
+      tc_commit(c.pv_done(t));
+    }
     tc_commit(c.kv_empty(s));  // K(j) and V(j) read by this tile's UMMAs
     if (j + 2 < g.num_kv) ok = qk(j + 2);
   }
@@ -554,11 +573,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // "rows" layout.
 // kSplit: the kernel has the split-tail merge (a launch with splits == 1 uses the
 // instance without it, which keeps fewer values live).
-template <int kPoly, bool kOrder, bool kSplit = true>
+// kSplitP: P is handed to the PV UMMAs in two halves of 64 keys (see run_mma_tile).
+template <int kPoly, bool kOrder, bool kSplit = true, bool kSplitP = false>
 __global__ void __launch_bounds__(kW20Threads, 1)
     flash_fwd_d64_w20_kernel(const __grid_constant__ CUtensorMap map_q,
                              const __grid_constant__ CUtensorMap map_k,
                              const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  static_assert(!(kOrder && kSplitP), "the turn-taking exchange assumes one P hand-off per step");
   const Ctl c = make_ctl();
   const Geom g = make_geom<kSplit>(fa);
   const int warp = threadIdx.x >> 5;
@@ -571,7 +592,7 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     if (warp == 0) {
       if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
     } else if (warp < 3) {
-      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false>(c, g, tmem, warp - 1, err);
+      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false, kSplitP>(c, g, tmem, warp - 1, err);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));
@@ -636,8 +657,8 @@ __global__ void __launch_bounds__(kW20Threads, 1)
         }
         uint32_t pk[32];  // 16x128b order: block k: (row 0 pair k), (row 1 pair k)
         uint64_t acc0 = 0, acc1 = 0;
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
+        // Column block k (keys 8k..8k+7 of this thread's pairs) -> pk, row sums.
+        auto exp_block = [&](int k) {
           float x0, x1, x2, x3, p0, p1, p2, p3;
           f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k], s[4 * k + 1]), sc2, ng0), x0, x1);
           f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k + 2], s[4 * k + 3]), sc2, ng1), x2, x3);
@@ -657,19 +678,8 @@ __global__ void __launch_bounds__(kW20Threads, 1)
           acc1 = (k == 0) ? q1 : f32x2_add(acc1, q1);
           pk[2 * k] = pack_bf16x2(p0, p1);
           pk[2 * k + 1] = pack_bf16x2(p2, p3);
-        }
-        if (kOrder && g.nq == 2) mbar_arrive(c.ex_done(t));
-        float u0, u1, v0, v1;
-        f32x2_unpack(acc0, u0, u1);
-        f32x2_unpack(acc1, v0, v1);
-        if (j > 0) {
-          ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        tmem_st_16x128b_x16(tP, pk);
-        if (j > 0 && __any_sync(0xffffffffu, grow0 || grow1)) {
+        };
+        auto rescale_o = [&]() {
           float o[32];  // block k: o[4k..4k+1] row 0, o[4k+2..4k+3] row 1
           tmem_ld_16x256b_x8(tO, o);
           uint32_t w[32];
@@ -681,7 +691,61 @@ __global__ void __launch_bounds__(kW20Threads, 1)
             w[4 * k + 3] = __float_as_uint(o[4 * k + 3] * al1);
           }
           tmem_st_16x256b_x8(tO, w);
+        };
+        if constexpr (kSplitP) {
+          // Keys 0..63 first: once PV(j-1) has read those P columns (all of PV(j-1)
+          // when O is rescaled), store them and let PV(j) start on them while the
+          // exponentials of keys 64..127 run.
+          const bool any_grow = j > 0 && __any_sync(0xffffffffu, grow0 || grow1);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) exp_block(k);
+          if (j > 0) {
+            ok = mbar_wait(any_grow ? c.pv_done_hi(t) : c.pv_done(t), (j - 1) & 1, abort_flag, err,
+                           kDevTimeoutConsumer);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          tmem_st_16x128b_x8(tP, pk);
+          if (any_grow) rescale_o();
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(c.p_full(t));
+#pragma unroll
+          for (int k = 8; k < 16; ++k) exp_block(k);
+          if (j > 0 && !any_grow) {
+            ok = mbar_wait(c.pv_done_hi(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          tmem_st_16x128b_x8(tP + 32, pk + 16);
+          tmem_wait_st();
+          float u0, u1, v0, v1;
+          f32x2_unpack(acc0, u0, u1);
+          f32x2_unpack(acc1, v0, v1);
+          l0 = l0 * al0 + (u0 + u1);
+          l1 = l1 * al1 + (v0 + v1);
+          m0 = mn0;
+          m1 = mn1;
+          tc_fence_before();
+          mbar_arrive(c.p_full_hi(t));
+          continue;
         }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) exp_block(k);
+        if (kOrder && g.nq == 2) mbar_arrive(c.ex_done(t));
+        float u0, u1, v0, v1;
+        f32x2_unpack(acc0, u0, u1);
+        f32x2_unpack(acc1, v0, v1);
+        if (j > 0) {
+          ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tmem_st_16x128b_x16(tP, pk);
+        if (j > 0 && __any_sync(0xffffffffu, grow0 || grow1)) rescale_o();
         tmem_wait_st();
         l0 = l0 * al0 + (u0 + u1);
         l1 = l1 * al1 + (v0 + v1);
@@ -837,13 +901,19 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
   static const Kern w20_nosplit[3] = {flash_fwd_d64_w20_kernel<0, false, false>,
                                       flash_fwd_d64_w20_kernel<1, false, false>,
                                       flash_fwd_d64_w20_kernel<2, false, false>};
+  // form 7: P handed over in two halves (with and without the split-tail merge)
+  static const Kern w20_sp[2][3] = {
+      {flash_fwd_d64_w20_kernel<0, false, false, true>, flash_fwd_d64_w20_kernel<1, false, false, true>,
+       flash_fwd_d64_w20_kernel<2, false, false, true>},
+      {flash_fwd_d64_w20_kernel<0, false, true, true>, flash_fwd_d64_w20_kernel<1, false, true, true>,
+       flash_fwd_d64_w20_kernel<2, false, true, true>}};
   Kern kern;
   int threads = kRowsThreads;
   bool w20_kernel = false, no_split = false;
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (fa.poly_per8 < 0 || poly > 2 || form > 6) return cudaErrorInvalidValue;
-    w20_kernel = form == 3 || form == 5 || form == 6;
+    if (fa.poly_per8 < 0 || poly > 2 || form > 7) return cudaErrorInvalidValue;
+    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7;
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
@@ -888,9 +958,10 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = fa.splits > 1 ? w20[form == 5][poly]
-             : form == 5   ? w20[1][poly]
-                           : w20_nosplit[poly];
+      kern = form == 7      ? w20_sp[fa.splits > 1][poly]
+             : fa.splits > 1 ? w20[form == 5][poly]
+             : form == 5     ? w20[1][poly]
+                             : w20_nosplit[poly];
       threads = kW20Threads;
       // setmaxnreg.inc draws on the registers the CTA launched with.
       cudaFuncAttributes attr;

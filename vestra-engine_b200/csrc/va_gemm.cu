@@ -85,6 +85,25 @@ __device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, 
   }
 }
 
+// erf(x) by Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
+//   erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2),  t = 1 / (1 + p x),
+// x >= 0, odd extension for x < 0, |error| <= 1.5e-7 (about 5e-7 evaluated in F32;
+// GELU's absolute error then stays below 4e-7, far under the bf16 rounding of the
+// fc1 output it feeds).  One reciprocal and one exp2 on MUFU plus a short FMA chain.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float ax = fabsf(x);
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, ax, 1.0f)));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  float e;  // exp(-x^2) = 2^(-x^2 log2 e)
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-ax * ax * 1.4426950408889634f));
+  return copysignf(fmaf(-poly, e, 1.0f), x);
+}
+
 // bf16 (or f16) of 8 consecutive values as one 16-byte chunk.
 __device__ __forceinline__ uint4 pack8(const float* x, bool f16) {
   uint4 u;
@@ -231,7 +250,7 @@ struct Fc1Epilogue {
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           const float z = x[i] + cbuf[hh * 64 + i];
-          x[i] = 0.5f * z * (1.0f + erff(z * 0.70710678118654752f));
+          x[i] = 0.5f * z * (1.0f + erf_as7126(z * 0.70710678118654752f));
         }
       }
       const uint32_t tile = out_smem + hh * kOutTileBytes;

@@ -305,6 +305,26 @@ __device__ __forceinline__ void umma_ts_k128_mn(uint32_t d_tmem, uint32_t a_tmem
       : "memory");
 }
 
+// Half of the above: 4 UMMAs over 64 keys (P columns [a_tmem, a_tmem + 32), B rows of
+// the descriptor's first 64 keys).  `accumulate` applies to the first UMMA only.
+__device__ __forceinline__ void umma_ts_k64_mn(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b32 blo, bhi, ta, tb;\n\t.reg .b64 b;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "mov.b64 {blo, bhi}, %2;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "add.u32 ta, %1, 8;\n\tadd.u32 tb, blo, 128;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 16;\n\tadd.u32 tb, blo, 256;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t"
+      "add.u32 ta, %1, 24;\n\tadd.u32 tb, blo, 384;\n\tmov.b64 b, {tb, bhi};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], b, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Instruction descriptor, kind::f16 with bf16 A/B and f32 D.
 //   [4,6) D fmt (1 = f32)  [7,10) A fmt (1 = bf16)  [10,13) B fmt (1 = bf16)
 //   [15] A MN-major  [16] B MN-major  [17,23) N>>3  [24,29) M>>4
