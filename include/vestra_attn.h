@@ -276,7 +276,9 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
  * instead of MUFU; form 0, 1, 2, 4 = one softmax row per thread (instruction
  * formulations), form 3 = four threads per row (20 warps), form 5 = form 3 with
  * the two query tiles taking turns in the exponential section, form 6 = form 3
- * with the split tail off (one CTA per unit).  Query i is row
+ * with the split tail off (one CTA per unit), form 7 = form 3 with P handed over
+ * in two 64-key halves, variant 64 = 64-key half-steps with S and P
+ * double-buffered in TMEM.  Query i is row
  * q_offset + i of the key window.  seg_len = 0: every query attends to all kv_rows
  * keys; seg_len > 0: independent segments of seg_len tokens (q_offset and q_count
  * multiples of seg_len).  out bf16 [q_count, heads*64]. */

@@ -95,12 +95,13 @@ def test_flash_bf16_matches_oracle_core(ctx, oracle_mod, heads, seg, segs, v_dty
     assert_close(got, ref, what=f"flash h{heads} n{seg}x{segs}")
 
 
-@pytest.mark.parametrize("variant", [1, 16, 24, 25, 26, 32, 40, 41, 48, 56, 57])
+@pytest.mark.parametrize("variant", [1, 16, 24, 25, 26, 32, 40, 41, 48, 56, 57, 64])
 @pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 129, 1), (12, 866, 1), (4, 865, 3), (12, 1732, 1)])
 def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, segs, variant):
     # variant = (pairs of every 8 exponentials on the FMA pipe) + 8 * layout/formulation;
     # 24..26 are the 20-warp layout with 4 threads per row, 48 the same without the
-    # split tail, 56..57 the same with P handed over in two halves.
+    # split tail, 56..57 the same with P handed over in two halves, 64 the 64-key
+    # half-step form with S and P double-buffered.
     rows = seg * segs
     rng = np.random.default_rng(heads * 7 + seg)
     q, k, v = (bf16_round(rng.standard_normal((heads, rows, 64)).astype(np.float32)) for _ in range(3))

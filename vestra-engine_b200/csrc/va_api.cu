@@ -1519,8 +1519,8 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   fa.embed = heads * 64;
   fa.v_f16 = v_f16 ? 1 : 0;
   if (variant >= 0) {
-    if ((variant & 7) > 2 || (variant >> 3) > 7)
-      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..7)");
+    if ((variant & 7) > 2 || (variant >> 3) > 8 || ((variant >> 3) == 8 && (variant & 7) != 0))
+      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..7), or 64");
     fa.poly_per8 = variant;
   }
   set_split_workspace(c, &fa);

@@ -77,8 +77,8 @@ struct FlashSmem {
   static constexpr uint32_t kV = kK + kStages * kTileBytes;      // V ring
   static constexpr uint32_t kBar = kV + kStages * kTileBytes;
   // barriers: q_full, kv_full[S], kv_empty[S], then per tile s_full, s_free,
-  // p_full, pv_done, o_final, ex_done, p_full_hi, pv_done_hi
-  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 16;
+  // p_full, pv_done, o_final, ex_done, p_full_hi, pv_done_hi, s_full_b1, s_free_b1
+  static constexpr uint32_t kNumBars = 1 + 2 * kStages + 20;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
   static constexpr uint32_t kBytes = kMisc + 64;
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;
@@ -171,6 +171,12 @@ struct Ctl {
   // Split P hand-off: p_full / pv_done then cover keys 0..63 of the tile, these 64..127.
   __device__ uint32_t p_full_hi(int t) const { return bar(13 + 2 * kStages + t); }
   __device__ uint32_t pv_done_hi(int t) const { return bar(15 + 2 * kStages + t); }
+  // Half-step layout (64-key steps, S and P double-buffered): buffer b of tile t.
+  // Buffer 0 uses s_full / s_free / p_full / pv_done, buffer 1 the *_b1 / *_hi ones.
+  __device__ uint32_t hs_full(int t, int b) const { return b ? bar(17 + 2 * kStages + t) : s_full(t); }
+  __device__ uint32_t hs_free(int t, int b) const { return b ? bar(19 + 2 * kStages + t) : s_free(t); }
+  __device__ uint32_t hp_full(int t, int b) const { return b ? p_full_hi(t) : p_full(t); }
+  __device__ uint32_t hpv_done(int t, int b) const { return b ? pv_done_hi(t) : pv_done(t); }
   __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(smem + FlashSmem::kMisc); }
   __device__ volatile int* abort_flag() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 4); }
   __device__ volatile int* kv_issued() const { return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 8); }
@@ -218,6 +224,8 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int s
       mbar_init(c.ex_done(t), softmax_threads);
       mbar_init(c.p_full_hi(t), softmax_threads);
       mbar_init(c.pv_done_hi(t), 1);
+      mbar_init(c.hs_full(t, 1), 1);
+      mbar_init(c.hs_free(t, 1), softmax_threads);
     }
     *c.abort_flag() = 0;
     *c.kv_issued() = 0;
@@ -323,6 +331,57 @@ __device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32
   // Always committed, also after an abort: o_final(t) then marks the moment every
   // UMMA of this issuer has finished, which the teardown waits for before it frees
   // TMEM.
+  tc_commit(c.o_final(t));
+  *c.mma_done(t) = 1;
+}
+
+// UMMA issuer of query tile t for the half-step layout: 64-key steps h = 2j + b
+// (j = K/V stage, b = half), S_t and P_t double-buffered by b.  TMEM of tile t:
+// S_t[b] at 256t + 64b (64 fp32 columns), P_t[b] at 256t + 128 + 32b (32 columns of
+// bf16 pairs), O_t at 256t + 192.  Chain: QK(0), QK(1), then per h: PV(h), QK(h+2).
+// QK(h+2) waits only for the softmax to have loaded S(h) (one half-step back), PV(h)
+// for P(h); the softmax waits for PV(h-2) before reusing P buffer b.
+__device__ __forceinline__ void run_mma_tile_h64(const Ctl& c, const Geom& g, uint32_t tmem, int t,
+                                                 int* err) {
+  constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, 64, false, false);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileQ, kHeadDim, false, true);
+  constexpr uint64_t kStageStep = kTileBytes >> 4;  // descriptor start-field step per stage
+  constexpr uint64_t kHalfStep = (64 * 128) >> 4;   // 64 rows of 128 B
+  volatile int* abort_flag = c.abort_flag();
+  const uint64_t dq = sdesc_sw128(c.sQ(t), 16, 1024);
+  const uint64_t dk0 = sdesc_sw128(c.sK(0), 16, 1024);
+  const uint64_t dv0 = sdesc_sw128(c.sV(0), 8192, 1024);
+  const uint32_t base = tmem + t * 256;
+  const int H = 2 * g.num_kv;
+  auto qk = [&](int h) {
+    const int j = h >> 1, b = h & 1, s = j % kStages;
+    bool r = true;
+    if (b == 0) {
+      r = mbar_wait(c.kv_full(s), (j / kStages) & 1, abort_flag, err, kDevTimeoutMma);
+      if (r && t == 0) *c.kv_consumed() = j + 1;
+    }
+    if (r && h >= 2) r = mbar_wait(c.hs_free(t, b), (j - 1) & 1, abort_flag, err, kDevTimeoutMma);
+    if (r) {
+      tc_fence_after();
+      umma_ss_k64(base + 64 * b, dq, dk0 + s * kStageStep + b * kHalfStep, idesc_qk, 0u);
+      tc_commit(c.hs_full(t, b));
+    }
+    return r;
+  };
+  bool ok = mbar_wait(c.q_full(), 0, abort_flag, err, kDevTimeoutMma);
+  if (ok) ok = qk(0);
+  if (ok && H > 1) ok = qk(1);
+  for (int h = 0; ok && h < H; ++h) {
+    const int j = h >> 1, b = h & 1, s = j % kStages;
+    ok = mbar_wait(c.hp_full(t, b), j & 1, abort_flag, err, kDevTimeoutMma);
+    if (!ok) break;
+    tc_fence_after();
+    umma_ts_k64_mn(base + 192, base + 128 + 32 * b, dv0 + s * kStageStep + b * kHalfStep, idesc_pv,
+                   h > 0 ? 1u : 0u);
+    tc_commit(c.hpv_done(t, b));
+    if (b == 1) tc_commit(c.kv_empty(s));  // K(j) and V(j) read by this tile's UMMAs
+    if (h + 2 < H) ok = qk(h + 2);
+  }
   tc_commit(c.o_final(t));
   *c.mma_done(t) = 1;
 }
@@ -574,12 +633,14 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
 // kSplit: the kernel has the split-tail merge (a launch with splits == 1 uses the
 // instance without it, which keeps fewer values live).
 // kSplitP: P is handed to the PV UMMAs in two halves of 64 keys (see run_mma_tile).
-template <int kPoly, bool kOrder, bool kSplit = true, bool kSplitP = false>
+// kHalf: 64-key half-steps with S and P double-buffered in TMEM (run_mma_tile_h64).
+template <int kPoly, bool kOrder, bool kSplit = true, bool kSplitP = false, bool kHalf = false>
 __global__ void __launch_bounds__(kW20Threads, 1)
     flash_fwd_d64_w20_kernel(const __grid_constant__ CUtensorMap map_q,
                              const __grid_constant__ CUtensorMap map_k,
                              const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
   static_assert(!(kOrder && kSplitP), "the turn-taking exchange assumes one P hand-off per step");
+  static_assert(!kHalf || (kPoly == 0 && !kOrder && !kSplitP), "half steps: MUFU exponentials only");
   const Ctl c = make_ctl();
   const Geom g = make_geom<kSplit>(fa);
   const int warp = threadIdx.x >> 5;
@@ -592,7 +653,12 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     if (warp == 0) {
       if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
     } else if (warp < 3) {
-      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false, kSplitP>(c, g, tmem, warp - 1, err);
+      if (lane == 0 && warp - 1 < g.nq) {
+        if constexpr (kHalf)
+          run_mma_tile_h64(c, g, tmem, warp - 1, err);
+        else
+          run_mma_tile<false, kSplitP>(c, g, tmem, warp - 1, err);
+      }
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));
@@ -611,7 +677,97 @@ __global__ void __launch_bounds__(kW20Threads, 1)
       float m0 = -INFINITY, m1 = -INFINITY;     // rows lane/4 and lane/4 + 8
       float l0 = 0.f, l1 = 0.f;                 // partial sums over my columns
       bool ok = true;
-      for (int j = 0; j < g.num_kv; ++j) {
+      if constexpr (kHalf) {
+        const uint32_t tb = tmem + lane_off + t * 256;  // this warp's lanes of tile t
+        for (int h = 0; h < 2 * g.num_kv; ++h) {
+          const int j = h >> 1, b = h & 1;
+          ok = mbar_wait(c.hs_full(t, b), j & 1, abort_flag, err, kDevTimeoutConsumer);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          float s[32];  // block k (keys 64b + 8k..): s[4k..4k+1] row 0, s[4k+2..4k+3] row 1
+          tmem_ld_16x256b_x8(tb + 64 * b, s);
+          tc_fence_before();
+          mbar_arrive(c.hs_free(t, b));
+          if (j == g.num_kv - 1 && g.last_valid < kTileK) {
+            const int valid = g.last_valid - 64 * b;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (8 * k + c0 + (e & 1) >= valid) s[4 * k + e] = -INFINITY;
+          }
+          float a0 = max3f(s[0], s[1], s[4]), a1 = max3f(s[2], s[3], s[6]);
+          float b0 = max3f(s[5], s[8], s[9]), b1 = max3f(s[7], s[10], s[11]);
+#pragma unroll
+          for (int k = 3; k < 8; k += 2) {
+            a0 = max3f(a0, s[4 * k], s[4 * k + 1]);
+            a1 = max3f(a1, s[4 * k + 2], s[4 * k + 3]);
+            if (k + 1 < 8) {
+              b0 = max3f(b0, s[4 * k + 4], s[4 * k + 5]);
+              b1 = max3f(b1, s[4 * k + 6], s[4 * k + 7]);
+            }
+          }
+          float mx0 = fmaxf(a0, b0), mx1 = fmaxf(a1, b1);
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * sl2;
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * sl2;
+          const bool grow0 = mx0 > m0 + kRescaleLog2, grow1 = mx1 > m1 + kRescaleLog2;
+          const float mn0 = grow0 ? mx0 : m0, mn1 = grow1 ? mx1 : m1;
+          const float al0 = grow0 ? ex2(m0 - mn0) : 1.0f, al1 = grow1 ? ex2(m1 - mn1) : 1.0f;
+          const uint64_t ng0 = f32x2_pack(-mn0, -mn0), ng1 = f32x2_pack(-mn1, -mn1);
+          const bool any_grow = h > 0 && __any_sync(0xffffffffu, grow0 || grow1);
+          uint32_t pk[16];
+          uint64_t acc0 = 0, acc1 = 0;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            float x0, x1, x2, x3;
+            f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k], s[4 * k + 1]), sc2, ng0), x0, x1);
+            f32x2_unpack(f32x2_fma(f32x2_pack(s[4 * k + 2], s[4 * k + 3]), sc2, ng1), x2, x3);
+            const float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
+            const uint64_t q0 = f32x2_pack(p0, p1), q1 = f32x2_pack(p2, p3);
+            acc0 = (k == 0) ? q0 : f32x2_add(acc0, q0);
+            acc1 = (k == 0) ? q1 : f32x2_add(acc1, q1);
+            pk[2 * k] = pack_bf16x2(p0, p1);
+            pk[2 * k + 1] = pack_bf16x2(p2, p3);
+          }
+          // P buffer b was last read by PV(h-2); rescaling O needs every earlier PV,
+          // i.e. PV(h-1) (commits complete in issue order).
+          if (h >= 2 || any_grow) {
+            const int hw = any_grow ? h - 1 : h - 2;
+            ok = mbar_wait(c.hpv_done(t, hw & 1), (hw >> 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          tmem_st_16x128b_x8(tb + 128 + 32 * b, pk);
+          if (any_grow) {
+            float o[32];  // block k: o[4k..4k+1] row 0, o[4k+2..4k+3] row 1
+            tmem_ld_16x256b_x8(tO, o);
+            uint32_t w[32];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              w[4 * k] = __float_as_uint(o[4 * k] * al0);
+              w[4 * k + 1] = __float_as_uint(o[4 * k + 1] * al0);
+              w[4 * k + 2] = __float_as_uint(o[4 * k + 2] * al1);
+              w[4 * k + 3] = __float_as_uint(o[4 * k + 3] * al1);
+            }
+            tmem_st_16x256b_x8(tO, w);
+          }
+          tmem_wait_st();
+          float u0, u1, v0, v1;
+          f32x2_unpack(acc0, u0, u1);
+          f32x2_unpack(acc1, v0, v1);
+          l0 = l0 * al0 + (u0 + u1);
+          l1 = l1 * al1 + (v0 + v1);
+          m0 = mn0;
+          m1 = mn1;
+          tc_fence_before();
+          mbar_arrive(c.hp_full(t, b));
+        }
+      }
+      for (int j = 0; !kHalf && j < g.num_kv; ++j) {
         ok = mbar_wait(c.s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
@@ -902,6 +1058,9 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
                                       flash_fwd_d64_w20_kernel<1, false, false>,
                                       flash_fwd_d64_w20_kernel<2, false, false>};
   // form 7: P handed over in two halves (with and without the split-tail merge)
+  // form 8: 64-key half-steps, S and P double-buffered (MUFU exponentials only)
+  static const Kern w20_half[2] = {flash_fwd_d64_w20_kernel<0, false, false, false, true>,
+                                   flash_fwd_d64_w20_kernel<0, false, true, false, true>};
   static const Kern w20_sp[2][3] = {
       {flash_fwd_d64_w20_kernel<0, false, false, true>, flash_fwd_d64_w20_kernel<1, false, false, true>,
        flash_fwd_d64_w20_kernel<2, false, false, true>},
@@ -912,8 +1071,8 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
   bool w20_kernel = false, no_split = false;
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (fa.poly_per8 < 0 || poly > 2 || form > 7) return cudaErrorInvalidValue;
-    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7;
+    if (fa.poly_per8 < 0 || poly > 2 || form > 8 || (form == 8 && poly != 0)) return cudaErrorInvalidValue;
+    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7 || form == 8;
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
@@ -958,7 +1117,8 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = form == 7      ? w20_sp[fa.splits > 1][poly]
+      kern = form == 8      ? w20_half[fa.splits > 1]
+             : form == 7    ? w20_sp[fa.splits > 1][poly]
              : fa.splits > 1 ? w20[form == 5][poly]
              : form == 5     ? w20[1][poly]
                              : w20_nosplit[poly];
