@@ -407,7 +407,7 @@ def run_ours(args):
     # blocks exchange K'/V between the uneven slices.
     window = None
     n_tok = wl.rows // wl.views
-    if wl.views >= world and (world == 1 or ctx.exchange_mode() == "direct"):
+    if wl.views >= world and (world == 1 or ctx.exchange_mode().startswith("direct")):
         for layer in range(12):
             pl = syn.layer_weights(wl.embed, seed=0, layer=layer, norm1=True, mlp=True)
             ctx.load_layer(layer, pl)

@@ -259,7 +259,12 @@ int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
  * copied back chunk by chunk while later attention chunks compute.  Collective. */
 int va_attention_host_sharded(va_ctx* ctx, int layer, const float* ln1_local, float* out_local,
                               int64_t local_rows, int gh, int gw, int view_count, int global);
-/* 0: no communicator, 1: NCCL all-gather, 2: direct peer stores. */
+/* 0: no communicator, 1: NCCL all-gather, 2: direct peer stores from the QKV
+ * epilogue + barrier kernel, 3: direct, pushed by copy engines (one stream per peer,
+ * then a stream memory write of the call's epoch into the peer's flag array); the
+ * attention kernel starts on the rank's own key tiles and waits (bounded) for the
+ * peers' flags before the first tile that is not its own.  VA_KV_EXCHANGE=nccl or
+ * =sm at va_comm_init force modes 1 or 2. */
 int va_comm_exchange_mode(const va_ctx* ctx);
 /* ln1_local/out_local: device F32 [local_rows, E], this rank's rows
  * [rank*local_rows, (rank+1)*local_rows) of a window of nranks*local_rows tokens

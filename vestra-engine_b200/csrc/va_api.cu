@@ -149,6 +149,15 @@ struct va_ctx {
   va::Comm* comm = nullptr;    // set by va_comm_init (multi-GPU global blocks)
   // direct K'/V exchange over NVLink (va_comm_init; else NCCL all-gather)
   bool p2p = false;
+  // Copy-engine form of it: the QKV epilogue writes only this rank's rows; one
+  // stream per peer copies them into that peer's window and then raises this
+  // rank's flag there (a stream memory write, no SM involved); the attention kernel
+  // waits on the flags itself.  Else the epilogue stores to the peers (SM stores)
+  // and a barrier kernel follows.
+  bool ce = false;
+  cudaStream_t ce_st[va::kMaxPeers] = {};
+  cudaEvent_t ce_ev[va::kMaxPeers] = {};
+  cudaEvent_t ev_qkv = nullptr;
   int epoch = 0;
   void* peer_arena[va::kMaxRanks] = {};
   // token input side (va_load_patch_embed)
@@ -402,6 +411,9 @@ struct BranchSpec {
   int npeer;              // direct exchange: peers whose windows receive this slice
   __nv_bfloat16* peer_k[va::kMaxPeers];
   __nv_bfloat16* peer_v[va::kMaxPeers];
+  bool ce = false;        // copy-engine exchange (see va_ctx::ce)
+  int epoch = 0;
+  int* peer_flag[va::kMaxPeers] = {};  // this rank's flag in each peer's flag array
 };
 
 // In-place all-gather of this rank's K'/V slices into the window buffers.
@@ -424,6 +436,7 @@ void close_peers(va_ctx* c) {
     c->peer_arena[r] = nullptr;
   }
   c->p2p = false;
+  c->ce = false;
 }
 
 // Maps every peer's kv_arena into this process (CUDA IPC) for the direct K'/V
@@ -440,6 +453,8 @@ int setup_peers(va_ctx* c) {
   if (nranks < 2 || nranks > va::kMaxRanks) return VA_OK;
   const char* env = std::getenv("VA_KV_EXCHANGE");
   const bool forced_nccl = env && std::string(env) == "nccl";
+  // "sm": direct exchange by the QKV epilogue's stores (no copy-engine push).
+  const bool forced_sm = env && std::string(env) == "sm";
   struct Slot {
     cudaIpcMemHandle_t h;
     int ok;
@@ -478,20 +493,38 @@ int setup_peers(va_ctx* c) {
       c->peer_arena[r] = p;
     }
   }
-  // Second round: the direct exchange only if every rank mapped every peer.
+  // The copy-engine push needs stream memory writes into a peer's memory: write 0
+  // (the flags' value before any call) into this rank's slot of every peer.
+  int ce_ok = 0;
+  if (opened && !forced_sm) {
+    ce_ok = 1;
+    for (int r = 0; ce_ok && r < nranks; ++r) {
+      if (r == rank) continue;
+      int* slot = reinterpret_cast<int*>(static_cast<char*>(c->peer_arena[r]) + kArenaWindows * c->win_bytes) + rank;
+      ce_ok = va::stream_write_u32(c->stream, slot, 0u) ? 1 : 0;
+    }
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
+      cudaGetLastError();
+      ce_ok = 0;
+    }
+  }
+  // Second round: the direct exchange only if every rank mapped every peer, its
+  // copy-engine form only if every rank's stream writes worked.
   if (rc == VA_OK) {
     std::vector<Slot> flags(nranks);
     Slot f{};
-    f.ok = opened;
+    f.ok = opened | (ce_ok << 1);
     e = cudaMemcpy(dbuf + nranks, &f, sizeof(Slot), cudaMemcpyHostToDevice);
     if (e == cudaSuccess && !va::comm_allgather_bytes(c->comm, dbuf + nranks, dbuf, sizeof(Slot), c->stream, &err))
       rc = fail(c, VA_ERR_NCCL, err);
     if (e == cudaSuccess && rc == VA_OK) e = cudaStreamSynchronize(c->stream);
     if (e == cudaSuccess && rc == VA_OK)
       e = cudaMemcpy(flags.data(), dbuf, sizeof(Slot) * nranks, cudaMemcpyDeviceToHost);
-    bool all_ok = e == cudaSuccess && rc == VA_OK;
-    for (int r = 0; all_ok && r < nranks; ++r) all_ok = flags[r].ok != 0;
+    bool all_ok = e == cudaSuccess && rc == VA_OK, all_ce = all_ok;
+    for (int r = 0; all_ok && r < nranks; ++r) all_ok = (flags[r].ok & 1) != 0;
+    for (int r = 0; all_ce && r < nranks; ++r) all_ce = (flags[r].ok & 2) != 0;
     c->p2p = all_ok;
+    c->ce = all_ok && all_ce;
   }
   cudaFree(dbuf);
   if (!c->p2p) close_peers(c);
@@ -554,8 +587,8 @@ int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1,
   qa.q_out = c->q + r0 * E;
   qa.k_out = b.kwin + (b.row_offset + r0) * E;
   qa.v_out = b.vwin + (b.row_offset + r0) * E;
-  qa.npeer = b.npeer;
-  for (int p = 0; p < b.npeer; ++p) {
+  qa.npeer = b.ce ? 0 : b.npeer;
+  for (int p = 0; p < qa.npeer; ++p) {
     qa.peer_k[p] = b.peer_k[p] + (b.row_offset + r0) * E;
     qa.peer_v[p] = b.peer_v[p] + (b.row_offset + r0) * E;
   }
@@ -596,6 +629,14 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
   } else {
     fa.q_offset = static_cast<int>(b.row_offset + q0);
     fa.kv_rows = static_cast<int>(b.window_rows);
+    if (b.ce) {
+      fa.peer_flags = c->xflags;
+      fa.epoch = b.epoch;
+      fa.nranks = va::comm_size(c->comm);
+      fa.rank = va::comm_rank(c->comm);
+      fa.own_begin = static_cast<int>(b.row_offset);
+      fa.own_end = static_cast<int>(b.row_offset + b.rows);
+    }
   }
   set_split_workspace(c, &fa);
   VA_CUDA(c, va::launch_flash(c->q + q0 * E, kk, vv, fa, c->err, st));
@@ -634,17 +675,48 @@ bool prepare_exchange(va_ctx* c, BranchSpec* b, va::PeerBarrierArgs* pb) {
     char* pa = static_cast<char*>(c->peer_arena[r]);
     b->peer_k[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set) * win);
     b->peer_v[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set + 1) * win);
+    b->peer_flag[b->npeer] = reinterpret_cast<int*>(pa + kArenaWindows * win) + rank;
     ++b->npeer;
     pb->peer_flags[r] = reinterpret_cast<int*>(pa + kArenaWindows * win);
   }
+  b->ce = c->ce;
+  b->epoch = c->epoch;
   return true;
+}
+
+// The copy-engine push of this rank's K'/V rows (after its QKV on `st`): one copy
+// stream per peer, K then V, then this rank's flag in that peer's flag array.
+int push_rows(va_ctx* c, const BranchSpec& b, cudaStream_t st) {
+  const int E = c->cfg.embed_dim;
+  const size_t off = static_cast<size_t>(b.row_offset) * E;
+  const size_t bytes = static_cast<size_t>(b.rows) * E * sizeof(__nv_bfloat16);
+  VA_CUDA(c, cudaEventRecord(c->ev_qkv, st));
+  for (int p = 0; p < b.npeer; ++p) {
+    cudaStream_t cs = c->ce_st[p];
+    VA_CUDA(c, cudaStreamWaitEvent(cs, c->ev_qkv, 0));
+    VA_CUDA(c, cudaMemcpyAsync(b.peer_k[p] + off, b.kwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
+    VA_CUDA(c, cudaMemcpyAsync(b.peer_v[p] + off, b.vwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
+    if (!va::stream_write_u32(cs, b.peer_flag[p], static_cast<uint32_t>(b.epoch)))
+      return fail(c, VA_ERR_CUDA, "stream flag write to a peer failed");
+    VA_CUDA(c, cudaEventRecord(c->ce_ev[p], cs));
+  }
+  return VA_OK;
+}
+
+// `st` waits for every copy stream of the call (the copies read this rank's rows,
+// which the call after next overwrites).
+int join_push(va_ctx* c, const BranchSpec& b, cudaStream_t st) {
+  for (int p = 0; b.ce && p < b.npeer; ++p) VA_CUDA(c, cudaStreamWaitEvent(st, c->ce_ev[p], 0));
+  return VA_OK;
 }
 
 // The exchange step between the projection and the attention of a sharded call:
 // the direct exchange's barrier, or the NCCL all-gather.
 int exchange_step(va_ctx* c, const BranchSpec& b, bool direct, const va::PeerBarrierArgs& pb,
                   cudaStream_t st) {
-  if (direct) {
+  if (direct && b.ce) {
+    return push_rows(c, b, st);
+  } else if (direct) {
     VA_CUDA(c, va::launch_peer_barrier(pb, c->err, st));
   } else if (b.gather) {
     const int E = c->cfg.embed_dim;
@@ -671,6 +743,7 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
   if ((rc = exchange_step(c, b, direct, pb, st))) return rc;
   VA_CUDA(c, mark(3));
   if ((rc = stage_attn(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[4] : nullptr))) return rc;
+  if ((rc = join_push(c, b, st))) return rc;
   VA_CUDA(c, mark(5));
   c->phase_valid = prof;
   return VA_OK;
@@ -766,6 +839,11 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
     return bail(e);
   for (int i = 0; i <= kPhases; ++i)
     if ((e = cudaEventCreate(&c->ph_ev[i])) != cudaSuccess) return bail(e);
+  for (int p = 0; p < va::kMaxPeers; ++p) {
+    if ((e = cudaStreamCreateWithFlags(&c->ce_st[p], cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
+    if ((e = cudaEventCreateWithFlags(&c->ce_ev[p], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
+  }
+  if ((e = cudaEventCreateWithFlags(&c->ev_qkv, cudaEventDisableTiming)) != cudaSuccess) return bail(e);
   {
     const size_t slots = static_cast<size_t>(va::flash_part_slots(c->sms));
     if ((e = dmalloc(&c->part_o, slots * 128 * 64)) != cudaSuccess) return bail(e);
@@ -818,6 +896,14 @@ void va_destroy(va_ctx* c) {
   }
   for (int i = 0; i <= kPhases; ++i)
     if (c->ph_ev[i]) cudaEventDestroy(c->ph_ev[i]);
+  for (int p = 0; p < va::kMaxPeers; ++p) {
+    if (c->ce_st[p]) {
+      cudaStreamSynchronize(c->ce_st[p]);
+      cudaStreamDestroy(c->ce_st[p]);
+    }
+    if (c->ce_ev[p]) cudaEventDestroy(c->ce_ev[p]);
+  }
+  if (c->ev_qkv) cudaEventDestroy(c->ev_qkv);
   delete c;
 }
 
@@ -1069,6 +1155,7 @@ int host_call(va_ctx* c, int layer, BranchSpec b, int view_count, const float* l
       if ((rc = stage_attn(c, layer, b, outb[j], outb[j + 1], c->stream))) return finish(rc);
       VA_HOST(cudaEventRecord(c->ev_out[j], c->stream));
     }
+    if ((rc = join_push(c, b, c->stream))) return finish(rc);
   }
   for (int j = 0; j < n_out; ++j) {
     VA_HOST(cudaStreamWaitEvent(c->d2h, c->ev_out[j], 0));
@@ -1425,7 +1512,7 @@ int va_comm_init(va_ctx* c, const void* id, int nranks, int rank) {
 
 int va_comm_exchange_mode(const va_ctx* c) {
   if (!c || !c->comm) return 0;
-  return c->p2p ? 2 : 1;
+  return c->ce ? 3 : c->p2p ? 2 : 1;
 }
 
 int va_attention_device_sharded(va_ctx* c, int layer, const float* ln1_local, float* out_local,

@@ -101,6 +101,9 @@ __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) {
 struct Geom {
   int q0, q_end, k0, nq, num_kv, col, head;
   int last_valid;  // keys of the last 128-key tile inside the range (128: no masking)
+  // Key tiles are visited in the order k0 + ((j + rot) % num_kv) * 128; the range's
+  // last (possibly partial) tile is visited at iteration tail_iter.
+  int rot, tail_iter;
 };
 
 // This CTA's place in the split tail of a global launch: key range `split` of
@@ -140,6 +143,10 @@ __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
     g.k0 = t0 * kTileK;
     g.last_valid = min(fa.kv_rows, t1 * kTileK) - (t1 - 1) * kTileK;
     g.num_kv = t1 - t0;
+    // With peers still sending their rows, start at this rank's own first tile.
+    const int own_tile = (fa.own_begin + kTileK - 1) / kTileK;
+    g.rot = (fa.peer_flags && own_tile > t0 && own_tile < t1) ? own_tile - t0 : 0;
+    g.tail_iter = g.num_kv - 1 - g.rot;
   } else {
     const int q_seg0 = blockIdx.z * fa.seg_len;
     g.q_end = q_seg0 + fa.seg_len;
@@ -148,6 +155,8 @@ __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
     g.num_kv = (fa.seg_len + kTileK - 1) / kTileK;
     g.last_valid = fa.seg_len - (g.num_kv - 1) * kTileK;
     g.head = blockIdx.y;
+    g.rot = 0;
+    g.tail_iter = g.num_kv - 1;
   }
   g.nq = (g.q_end - g.q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
   g.col = g.head * kHeadDim;
@@ -249,21 +258,45 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int s
   return *c.tmem_slot();
 }
 
+// Waits (bounded) until every peer's rows of the key window have arrived.
+__device__ __forceinline__ bool wait_peer_rows(const FlashArgs& fa, volatile int* abort_flag, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int r = 0; r < fa.nranks; ++r) {
+    if (r == fa.rank) continue;
+    while (ld_acquire_sys(fa.peer_flags + r) < fa.epoch) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        report_error(err, kDevTimeoutPeer);
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+  return true;
+}
+
 // TMA producer (one thread).
-__device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const CUtensorMap* mq,
-                                             const CUtensorMap* mk, const CUtensorMap* mv,
-                                             int* err) {
+__device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const FlashArgs& fa,
+                                             const CUtensorMap* mq, const CUtensorMap* mk,
+                                             const CUtensorMap* mv, int* err) {
   // Every box starts inside the tensor; rows past its end are zero-filled.
   mbar_arrive_expect_tx(c.q_full(), g.nq * kTileBytes);
   tma_load_2d(c.sQ(0), mq, c.q_full(), g.col, g.q0);
   if (g.nq == 2) tma_load_2d(c.sQ(1), mq, c.q_full(), g.col, g.q0 + kTileQ);
+  bool peers_in = fa.peer_flags == nullptr;
   for (int j = 0; j < g.num_kv; ++j) {
     const int s = j % kStages;
     const uint32_t ph = (j / kStages) & 1;
+    const int row = g.k0 + ((j + g.rot) % g.num_kv) * kTileK;
+    if (!peers_in && !(row >= fa.own_begin && row + kTileK <= fa.own_end)) {
+      if (!wait_peer_rows(fa, c.abort_flag(), err)) break;
+      peers_in = true;
+    }
     if (!mbar_wait(c.kv_empty(s), ph ^ 1, c.abort_flag(), err, kDevTimeoutProducer)) break;
     mbar_arrive_expect_tx(c.kv_full(s), 2 * kTileBytes);
-    tma_load_2d(c.sK(s), mk, c.kv_full(s), g.col, g.k0 + j * kTileK);
-    tma_load_2d(c.sV(s), mv, c.kv_full(s), g.col, g.k0 + j * kTileK);
+    tma_load_2d(c.sK(s), mk, c.kv_full(s), g.col, row);
+    tma_load_2d(c.sV(s), mv, c.kv_full(s), g.col, row);
     *c.kv_issued() = j + 1;
   }
 }
@@ -502,7 +535,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
   volatile int* abort_flag = c.abort_flag();
 
   if (warp == 0) {
-    if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
+    if (lane == 0) run_producer(c, g, fa, &map_q, &map_k, &map_v, err);
   } else if (warp < 3) {
     if (lane == 0 && warp - 1 < g.nq) run_mma_tile<kF16>(c, g, tmem, warp - 1, err);
   } else if (warp >= 4) {
@@ -527,7 +560,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1)
         tmem_ld128(tS, s);
         tc_fence_before();
         mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
-        const bool tail = j == g.num_kv - 1 && g.last_valid < kTileK;
+        const bool tail = j == g.tail_iter && g.last_valid < kTileK;
         if (tail) {
           const int valid = g.last_valid;
 #pragma unroll
@@ -651,7 +684,7 @@ __global__ void __launch_bounds__(kW20Threads, 1)
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kW20LowRegs));
     if (warp == 0) {
-      if (lane == 0) run_producer(c, g, &map_q, &map_k, &map_v, err);
+      if (lane == 0) run_producer(c, g, fa, &map_q, &map_k, &map_v, err);
     } else if (warp < 3) {
       if (lane == 0 && warp - 1 < g.nq) {
         if constexpr (kHalf)
@@ -689,7 +722,7 @@ __global__ void __launch_bounds__(kW20Threads, 1)
           tmem_ld_16x256b_x8(tb + 64 * b, s);
           tc_fence_before();
           mbar_arrive(c.hs_free(t, b));
-          if (j == g.num_kv - 1 && g.last_valid < kTileK) {
+          if (j == g.tail_iter && g.last_valid < kTileK) {
             const int valid = g.last_valid - 64 * b;
 #pragma unroll
             for (int k = 0; k < 8; ++k)
@@ -776,7 +809,7 @@ __global__ void __launch_bounds__(kW20Threads, 1)
         tmem_ld_16x256b_x16(tS, s);
         tc_fence_before();
         mbar_arrive(c.s_free(t));
-        const bool tail = j == g.num_kv - 1 && g.last_valid < kTileK;
+        const bool tail = j == g.tail_iter && g.last_valid < kTileK;
         if (tail) {
           const int valid = g.last_valid;
 #pragma unroll

@@ -113,10 +113,26 @@ struct FlashArgs {
   // Filled in by launch_flash (kernel-side view of the plan).
   int n_full = 0;
   int splits = 1;
+  // Copy-engine K'/V exchange of a sharded global block: key rows outside this
+  // rank's own rows [own_begin, own_end) arrive from the peers; peer r's rows are in
+  // place once peer_flags[r] >= epoch (written by r's copy stream).  The producer
+  // starts at the first key tile of its own rows and waits (bounded) for every peer
+  // before the first tile that is not entirely its own.  nullptr: nothing to wait for.
+  const int* peer_flags = nullptr;
+  int epoch = 0;
+  int nranks = 0;
+  int rank = 0;
+  int own_begin = 0;
+  int own_end = 0;
 };
 // Slots a context provides for the split tail: rem < sms units, at most 4 key
 // ranges each, two query tiles per CTA.
 inline int flash_part_slots(int sms) { return 2 * 4 * sms; }
+
+// Stream memory write (driver entry point cuStreamWriteValue32, no -lcuda needed):
+// `value` lands at `addr` (this GPU's or a mapped peer's memory) once the stream's
+// earlier work is done, behind a memory fence.  False when unavailable or refused.
+bool stream_write_u32(cudaStream_t st, int* addr, uint32_t value);
 
 // Tensor-map encoding through the driver entry point (no -lcuda needed).
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

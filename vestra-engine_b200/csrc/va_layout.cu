@@ -41,6 +41,25 @@ bool get_encode() {
 }
 }  // namespace
 
+namespace {
+PFN_cuStreamWriteValue32_v11070 g_write32 = nullptr;
+std::once_flag g_write32_once;
+}  // namespace
+
+bool stream_write_u32(cudaStream_t st, int* addr, uint32_t value) {
+  std::call_once(g_write32_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_write32 = reinterpret_cast<PFN_cuStreamWriteValue32_v11070>(fn);
+  });
+  if (!g_write32 || !addr) return false;
+  // Default flags: the write is preceded by a memory fence over the stream's earlier work.
+  return g_write32(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(addr), value,
+                   CU_STREAM_WRITE_VALUE_DEFAULT) == CUDA_SUCCESS;
+}
+
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer) {
   if (!get_encode() || base == nullptr) return false;

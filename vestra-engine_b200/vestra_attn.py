@@ -339,8 +339,10 @@ class Context:
         return out
 
     def exchange_mode(self) -> str:
-        """How K'/V reach the other ranks: "none", "nccl" or "direct" (peer stores)."""
-        return ("none", "nccl", "direct")[self.lib.va_comm_exchange_mode(self.h)]
+        """How K'/V reach the other ranks: "none", "nccl", "direct" (the QKV epilogue
+        stores into the peers' windows) or "direct-ce" (copy engines push each rank's
+        rows, the attention kernel waits on per-peer flags)."""
+        return ("none", "nccl", "direct", "direct-ce")[self.lib.va_comm_exchange_mode(self.h)]
 
     def attention_device_sharded(self, layer, ln1_local, out_local, gh, gw, view_count, global_, stream=0):
         self.check(self.lib.va_attention_device_sharded(self.h, layer, _ptr(ln1_local), _ptr(out_local),
