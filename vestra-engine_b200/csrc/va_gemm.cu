@@ -59,27 +59,29 @@ __device__ __forceinline__ void head_layernorm(float* x, const float* g, const f
 }
 
 // 2D RoPE of one 64-wide head row: channels [0,32) rotate with y, [32,64) with x.
+// The (cos, sin) rows are read two pairs per 16-byte load (rows are 128-byte aligned).
 __device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, int pairing) {
 #pragma unroll
   for (int axis = 0; axis < 2; ++axis) {
     const int p = axis == 0 ? pos.x : pos.y;
-    const float2* row = cs + p * 16;
+    const float4* row = reinterpret_cast<const float4*>(cs + p * 16);
     float* seg = x + axis * 32;
-    if (pairing == 0) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 c = __ldg(row + i);
-        const float a = seg[i], bb = seg[i + 16];
-        seg[i] = a * c.x - bb * c.y;
-        seg[i + 16] = bb * c.x + a * c.y;
-      }
-    } else {
+    for (int h = 0; h < 8; ++h) {
+      const float4 cc = __ldg(row + h);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 c = __ldg(row + i);
-        const float a = seg[2 * i], bb = seg[2 * i + 1];
-        seg[2 * i] = a * c.x - bb * c.y;
-        seg[2 * i + 1] = bb * c.x + a * c.y;
+      for (int e = 0; e < 2; ++e) {
+        const int i = 2 * h + e;
+        const float cx = e ? cc.z : cc.x, sy = e ? cc.w : cc.y;
+        if (pairing == 0) {
+          const float a = seg[i], bb = seg[i + 16];
+          seg[i] = a * cx - bb * sy;
+          seg[i + 16] = bb * cx + a * sy;
+        } else {
+          const float a = seg[2 * i], bb = seg[2 * i + 1];
+          seg[2 * i] = a * cx - bb * sy;
+          seg[2 * i + 1] = bb * cx + a * sy;
+        }
       }
     }
   }
