@@ -123,7 +123,8 @@ struct va_ctx {
   };
   PosEntry pos_cache[4];
   uint64_t pos_clock = 0;
-  float2* rope_cs = nullptr;   // [rope_npos][16]
+  float2* rope_cs = nullptr;   // [rope_npos][16] (Op::Attention operand preparation)
+  float2* rope_cs_t = nullptr; // the same values i-major, [16][rope_npos] (QKV epilogue)
   int rope_npos = 0;
   int* err = nullptr;          // device error word
   cudaStream_t stream = nullptr;
@@ -312,9 +313,15 @@ int ensure_rope_table(va_ctx* c, int npos) {
       t[static_cast<size_t>(p) * 16 + i] = make_float2(static_cast<float>(std::cos(ang)),
                                                       static_cast<float>(std::sin(ang)));
     }
+  std::vector<float2> tt(t.size());
+  for (int p = 0; p < n; ++p)
+    for (int i = 0; i < 16; ++i) tt[static_cast<size_t>(i) * n + p] = t[static_cast<size_t>(p) * 16 + i];
   dfree(c->rope_cs);
+  dfree(c->rope_cs_t);
   VA_CUDA(c, dmalloc(&c->rope_cs, t.size()));
   VA_CUDA(c, cudaMemcpy(c->rope_cs, t.data(), t.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  VA_CUDA(c, dmalloc(&c->rope_cs_t, tt.size()));
+  VA_CUDA(c, cudaMemcpy(c->rope_cs_t, tt.data(), tt.size() * sizeof(float2), cudaMemcpyHostToDevice));
   c->rope_npos = n;
   return VA_OK;
 }
@@ -582,7 +589,8 @@ int stage_qkv(va_ctx* c, int layer, const BranchSpec& b, int64_t r0, int64_t r1,
   qa.k_b = qk ? w.kn_b : nullptr;
   qa.qk_eps = c->cfg.qk_norm_eps;
   qa.pos = b.pos ? b.pos + b.row_offset + r0 : nullptr;
-  qa.rope_cs = c->rope_cs;
+  qa.rope_cs = c->rope_cs_t;
+  qa.rope_npos = c->rope_npos;
   qa.rope_pairing = c->cfg.rope_pairing;
   qa.q_out = c->q + r0 * E;
   qa.k_out = b.kwin + (b.row_offset + r0) * E;
@@ -880,6 +888,7 @@ void va_destroy(va_ctx* c) {
   dfree(c->pos);
   for (auto& e : c->pos_cache) dfree(e.dev);
   dfree(c->rope_cs);
+  dfree(c->rope_cs_t);
   dfree(c->err);
   dfree(c->op_buf);
   dfree(c->op_pos);

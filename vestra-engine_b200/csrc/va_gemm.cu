@@ -59,29 +59,25 @@ __device__ __forceinline__ void head_layernorm(float* x, const float* g, const f
 }
 
 // 2D RoPE of one 64-wide head row: channels [0,32) rotate with y, [32,64) with x.
-// The (cos, sin) rows are read two pairs per 16-byte load (rows are 128-byte aligned).
-__device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, int pairing) {
+// The table is i-major ([16][npos]): the 32 rows of a warp are consecutive tokens, so
+// their positions are equal (y) or consecutive (x within a row of patches) and each
+// load of one frequency touches one or two cache lines across the warp.
+__device__ __forceinline__ void head_rope(float* x, int2 pos, const float2* cs, int npos, int pairing) {
 #pragma unroll
   for (int axis = 0; axis < 2; ++axis) {
-    const int p = axis == 0 ? pos.x : pos.y;
-    const float4* row = reinterpret_cast<const float4*>(cs + p * 16);
+    const float2* col = cs + (axis == 0 ? pos.x : pos.y);
     float* seg = x + axis * 32;
 #pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      const float4 cc = __ldg(row + h);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int i = 2 * h + e;
-        const float cx = e ? cc.z : cc.x, sy = e ? cc.w : cc.y;
-        if (pairing == 0) {
-          const float a = seg[i], bb = seg[i + 16];
-          seg[i] = a * cx - bb * sy;
-          seg[i + 16] = bb * cx + a * sy;
-        } else {
-          const float a = seg[2 * i], bb = seg[2 * i + 1];
-          seg[2 * i] = a * cx - bb * sy;
-          seg[2 * i + 1] = bb * cx + a * sy;
-        }
+    for (int i = 0; i < 16; ++i) {
+      const float2 c = __ldg(col + i * npos);
+      if (pairing == 0) {
+        const float a = seg[i], bb = seg[i + 16];
+        seg[i] = a * c.x - bb * c.y;
+        seg[i + 16] = bb * c.x + a * c.y;
+      } else {
+        const float a = seg[2 * i], bb = seg[2 * i + 1];
+        seg[2 * i] = a * c.x - bb * c.y;
+        seg[2 * i + 1] = bb * c.x + a * c.y;
       }
     }
   }
@@ -180,7 +176,7 @@ struct QkvEpilogue {
           x[4 * i + 3] += v.w;
         }
         if (norm) head_layernorm(x, cbuf + 256, cbuf + 320, a.qk_eps);
-        if (rope) head_rope(x, pos, a.rope_cs, a.rope_pairing);
+        if (rope) head_rope(x, pos, a.rope_cs, a.rope_npos, a.rope_pairing);
       }
       const uint32_t tile = out_smem + hh * kOutTileBytes;
 #pragma unroll

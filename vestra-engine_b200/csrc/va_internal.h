@@ -20,7 +20,8 @@ struct QkvEpilogueArgs {
   const float* k_g; const float* k_b;
   float qk_eps;
   const int2* pos;                     // [rows] (y, x) integer positions (nullptr: no RoPE)
-  const float2* rope_cs;               // [n_pos][16] (cos, sin) of pos * base^(-2i/32)
+  const float2* rope_cs;               // [16][rope_npos] (cos, sin) of pos * base^(-2i/32), i-major
+  int rope_npos;
   int rope_pairing;                    // 0 rotate-half, 1 interleaved
   __nv_bfloat16* q_out;                // [rows][E], head h at columns [64h, 64h+64)
   __nv_bfloat16* k_out;                // [rows][E] (may be a rank's slice of a gathered buffer)
