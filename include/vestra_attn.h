@@ -333,6 +333,13 @@ int va_phase_times(va_ctx* ctx, float* ms_out /* [5] */);
  * then returns VA_ERR_DEVICE exactly as a stalled attention launch would, and the
  * context stays usable.  Any other status means the mechanism is broken. */
 int va_selftest_bounded_wait(va_ctx* ctx, int64_t limit_us);
+/* Self-test of the attention kernel's wait for peer rows (the copy-engine K'/V
+ * exchange) on one GPU: a 1-head, 256-key launch as rank 0 of 2 owning the first
+ * 128 keys, with rank 1's flag set to peer_flag against epoch 1.  peer_flag >= 1:
+ * VA_OK and *out_max_abs = max |difference| to the same launch without a peer
+ * (0: same key order).  peer_flag 0: the kernel gives up after its 2 s wait limit
+ * and the call returns VA_ERR_DEVICE; the context stays usable. */
+int va_selftest_peer_wait(va_ctx* ctx, int peer_flag, float* out_max_abs);
 
 #ifdef __cplusplus
 }

@@ -51,3 +51,22 @@ def test_bounded_wait_reports_timeout_and_context_recovers(ctx, oracle_mod):
 def test_selftest_limits_are_checked_on_the_host(ctx):
     assert ctx.selftest_bounded_wait(0) == va.VA_ERR_INVALID
     assert ctx.selftest_bounded_wait(2_000_000) == va.VA_ERR_INVALID
+
+
+def test_attention_waits_for_peer_rows_and_gives_up_without_them(ctx):
+    # The copy-engine exchange's consumer side on one GPU: with the peer's flag
+    # raised the kernel runs and matches the launch without a peer bit for bit;
+    # with a flag that nothing raises its producer gives up after the 2 s limit,
+    # the call reports VA_ERR_DEVICE (kDevTimeoutPeer), and the context recovers.
+    rc, diff = ctx.selftest_peer_wait(1)
+    assert rc == va.VA_OK, ctx.last_error()
+    assert diff == 0.0, diff
+    t = time.perf_counter()
+    rc, _ = ctx.selftest_peer_wait(0)
+    dt = time.perf_counter() - t
+    assert rc == va.VA_ERR_DEVICE, rc
+    assert "timed out" in ctx.last_error()
+    assert 1.5 < dt < 20.0, dt
+    ctx.check_device()
+    rc, diff = ctx.selftest_peer_wait(1)
+    assert rc == va.VA_OK and diff == 0.0, (rc, diff, ctx.last_error())

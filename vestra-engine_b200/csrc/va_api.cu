@@ -1801,4 +1801,72 @@ int va_selftest_bounded_wait(va_ctx* c, int64_t limit_us) {
   return read_device_error(c);
 }
 
+int va_selftest_peer_wait(va_ctx* c, int peer_flag, float* out_max_abs) {
+  if (!c) return VA_ERR_INVALID;
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaStreamSynchronize(c->stream));
+  int rc = read_device_error(c);
+  if (rc) return rc;
+  // One head, 256 keys of which this "rank 0 of 2" owns the first 128; rank 1's flag
+  // is `peer_flag` against epoch 1.  Inputs are a fixed pattern; the result is
+  // compared with the same launch without a peer.
+  const int rows = 256, cols = 64;
+  std::vector<uint16_t> h(static_cast<size_t>(rows) * cols);
+  for (size_t i = 0; i < h.size(); ++i) h[i] = f32_to_bf16_rne(std::sin(0.37f * static_cast<float>(i)));
+  __nv_bfloat16 *qkv = nullptr, *o1 = nullptr, *o2 = nullptr;
+  int* flags = nullptr;
+  auto release = [&]() {
+    cudaStreamSynchronize(c->stream);
+    dfree(qkv);
+    dfree(o1);
+    dfree(o2);
+    dfree(flags);
+  };
+  cudaError_t e = dmalloc(&qkv, h.size());
+  if (e == cudaSuccess) e = dmalloc(&o1, h.size());
+  if (e == cudaSuccess) e = dmalloc(&o2, h.size());
+  if (e == cudaSuccess) e = dmalloc(&flags, va::kMaxRanks);
+  if (e == cudaSuccess) e = cudaMemcpy(qkv, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(flags, 0, va::kMaxRanks * sizeof(int));
+  if (e == cudaSuccess && peer_flag) e = cudaMemcpy(flags + 1, &peer_flag, sizeof(int), cudaMemcpyHostToDevice);
+  va::FlashArgs fa{};
+  fa.q_count = rows;
+  fa.kv_rows = rows;
+  fa.heads = 1;
+  fa.embed = cols;
+  fa.scale_log2 = static_cast<float>(1.0 / 8.0 * 1.4426950408889634);
+  fa.o_tok = o1;
+  if (e == cudaSuccess) e = va::launch_flash(qkv, qkv, qkv, fa, c->err, c->stream);
+  fa.o_tok = o2;
+  fa.peer_flags = flags;
+  fa.epoch = 1;
+  fa.nranks = 2;
+  fa.rank = 0;
+  fa.own_begin = 0;
+  fa.own_end = 128;
+  if (e == cudaSuccess) e = va::launch_flash(qkv, qkv, qkv, fa, c->err, c->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e != cudaSuccess) {
+    release();
+    return cuda_fail(c, e, "peer-wait self-test");
+  }
+  rc = read_device_error(c);
+  if (rc == VA_OK && out_max_abs) {
+    std::vector<uint16_t> a(h.size()), b(h.size());
+    cudaMemcpy(a.data(), o1, a.size() * 2, cudaMemcpyDeviceToHost);
+    cudaMemcpy(b.data(), o2, b.size() * 2, cudaMemcpyDeviceToHost);
+    float m = 0.f;
+    for (size_t i = 0; i < a.size(); ++i) {
+      uint32_t ua = static_cast<uint32_t>(a[i]) << 16, ub = static_cast<uint32_t>(b[i]) << 16;
+      float fa_, fb_;
+      std::memcpy(&fa_, &ua, 4);
+      std::memcpy(&fb_, &ub, 4);
+      m = std::max(m, std::fabs(fa_ - fb_));
+    }
+    *out_max_abs = m;
+  }
+  release();
+  return rc;
+}
+
 }  // extern "C"

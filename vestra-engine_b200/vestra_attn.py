@@ -42,6 +42,7 @@ EXPORTED = [
     "va_attention_host_sharded",
     "va_op_attention_noalloc",
     "va_load_patch_embed", "va_prepare_tokens_device", "va_prepare_tokens_host", "va_pos_embed_device",
+    "va_selftest_peer_wait",
 ]
 
 
@@ -123,6 +124,7 @@ def load_library(path: str = LIB_PATH):
         "va_prepare_tokens_device": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp, _vp], c_int),
         "va_prepare_tokens_host": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp], c_int),
         "va_pos_embed_device": ([_vp, c_int, c_int, _vp, _vp], c_int),
+        "va_selftest_peer_wait": ([_vp, c_int, _f32p], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -383,6 +385,13 @@ class Context:
         """Runs the failure-detection self-test; returns the raw status (VA_ERR_DEVICE
         when the bounded wait gave up as designed)."""
         return self.lib.va_selftest_bounded_wait(self.h, int(limit_us))
+
+    def selftest_peer_wait(self, peer_flag: int):
+        """The attention kernel's wait for peer rows on one GPU (see the header):
+        returns (raw status, max |difference| to the launch without a peer)."""
+        m = ctypes.c_float(-1.0)
+        rc = self.lib.va_selftest_peer_wait(self.h, int(peer_flag), ctypes.byref(m))
+        return rc, m.value
 
     def load_patch_embed(self, weight_oihw, bias, cls_token, pos_embed, register_tokens=None, patch=14,
                          interp_offset=0.1):
