@@ -6,8 +6,9 @@ per view, 10,392-token window, E=768, 12 heads x 64), FLOPs = 4 * N^2 * d * head
 A step is one global attention sub-block over the whole window: LN1 output (F32,
 resident in HBM) -> QKV UMMA with QK-norm/RoPE epilogue -> fused flash attention ->
 output projection (F32).  With --gpus N > 1 the window's queries are split into N
-equal token slices (one process per GPU); the QKV epilogue stores every K'/V tile
-into the peers' windows over NVLink (NCCL all-gather where that is unavailable).
+equal token slices (one process per GPU); each rank's K'/V rows reach the peers'
+windows over NVLink by copy engines, and the attention kernel waits on per-peer flags
+(epilogue peer stores, or an NCCL all-gather, where that is unavailable).
 The line also reports one whole block (attention + LN2/MLP) under "block", the
 12-block window under "window", and the token input side (patch projection and
 position/CLS assembly of every view) under "tokens".
@@ -528,6 +529,25 @@ def run_ours(args):
         e2e_s += time.perf_counter() - t
     barrier()
     e2e_s = max_over_ranks(e2e_s)
+    # The same bytes over PCIe with nothing else running: the H2D of the step's input
+    # and the D2H of its output, one after the other (a global block's outputs all
+    # depend on its last input row, so this sum bounds e2e from below).
+    d_in = torch.empty(h_in.shape, dtype=h_in.dtype, device="cuda")
+    h_tmp = torch.empty_like(h_in).pin_memory()  # h_out keeps the e2e result checked below
+    copy_ms = []
+    for _ in range(3 + args.steps):
+        ca, cb, cc = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        ca.record(stream)
+        d_in.copy_(h_in, non_blocking=True)
+        cb.record(stream)
+        h_tmp.copy_(d_in, non_blocking=True)
+        cc.record(stream)
+        cc.synchronize()
+        copy_ms.append((ca.elapsed_time(cb), cb.elapsed_time(cc)))
+    copy_ms = copy_ms[3:]
+    h2d_ms = max_over_ranks(statistics.median(c[0] for c in copy_ms))
+    d2h_ms = max_over_ranks(statistics.median(c[1] for c in copy_ms))
+    del d_in, h_tmp
     e2e_value = flops / (e2e_s / args.steps) / 1e12
     # parity of the host path against the device path on this input.  The host path
     # attends its queries in wave-sized chunks, the device path in one launch whose
@@ -563,7 +583,13 @@ def run_ours(args):
                     "h2d_bytes_per_step": int(wl.rows * wl.embed * 4), "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),
                     "path": "va_attention_host (C ABI, pinned host in/out)" if world == 1 else
                     "va_attention_host_sharded (C ABI, pinned host in/out, per rank)",
-                    "max_abs_vs_device_path": e2e_diff},
+                    "max_abs_vs_device_path": e2e_diff,
+                    "pcie_floor_ms": {"h2d": round(h2d_ms, 4), "d2h": round(d2h_ms, 4),
+                                      "sum": round(h2d_ms + d2h_ms, 4),
+                                      "h2d_gbs": round(h_in.numel() * 4 / (h2d_ms * 1e-3) / 1e9, 1),
+                                      "d2h_gbs": round(h_in.numel() * 4 / (d2h_ms * 1e-3) / 1e9, 1),
+                                      "what": "the step's input H2D then its output D2H alone, per rank "
+                                              "(median); a global block's outputs need its last input row"}},
             "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
