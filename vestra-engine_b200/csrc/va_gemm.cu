@@ -133,8 +133,8 @@ struct QkvEpilogue {
   QkvEpilogueArgs a;
   CUtensorMap map_out[3];  // Q, K, V: [rows][E] 2-byte, box 64 x 128
 
-  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
-  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
+  __device__ __forceinline__ uint32_t prefetch_bytes(int = 1) const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t, int = 0, int = 1) const {}
 
   // cbuf: [0, 256) bias of the tile's columns, [256, 320) gamma, [320, 384) beta of
   // the section's QK-norm (1 and 0 when the section has none).
@@ -152,7 +152,8 @@ struct QkvEpilogue {
 
   template <int BN>
   __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
-                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+                                      const float* cbuf, uint32_t out_smem, bool valid, int cp = 0,
+                                      int ncp = 1) const {
     static_assert(BN == 256, "QKV tiles are 4 heads wide");
     const int section = n0 / a.embed;  // 0 = Q, 1 = K, 2 = V
     const bool norm = section < 2 && (section == 0 ? a.q_g : a.k_g) != nullptr;
@@ -212,7 +213,8 @@ struct QkvEpilogue {
     __threadfence_system();
   }
 
-  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem, int cp = 0,
+                                        int ncp = 1) const {
     const int section = n0 / a.embed;
     const int h0 = (n0 - section * a.embed) / 64;
     for (int j = 0; j < 2; ++j) {
@@ -229,14 +231,15 @@ struct Fc1Epilogue {
   Fc1EpilogueArgs a;
   CUtensorMap map_out;  // bf16 [rows][hidden], box 64 x 128
 
-  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
-  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
+  __device__ __forceinline__ uint32_t prefetch_bytes(int = 1) const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t, int = 0, int = 1) const {}
 
   __device__ __forceinline__ void stage(float* cbuf, int n0, int t) const { cbuf[t] = a.bias[n0 + t]; }
 
   template <int BN>
   __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
-                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+                                      const float* cbuf, uint32_t out_smem, bool valid, int cp = 0,
+                                      int ncp = 1) const {
     static_assert(BN == 256, "fc1 tiles are 256 columns wide");
 #pragma unroll 1
     for (int j = 0; j < 2; ++j) {
@@ -259,7 +262,8 @@ struct Fc1Epilogue {
 
   __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
 
-  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem, int cp = 0,
+                                        int ncp = 1) const {
     for (int j = 0; j < 2; ++j) {
       const int hh = half * 2 + j;
       tma_store_2d(&map_out, out_smem + hh * kOutTileBytes, n0 + hh * 64, m0);
@@ -274,12 +278,19 @@ struct ProjEpilogue {
   CUtensorMap map_res;  // the residual, same boxes (persistent kernel: prefetched by TMA)
   int res_staged = 0;   // 1: the residual tile is already in the staging tiles when run() starts
 
-  // Bytes one half's store thread prefetches into its staging tiles per tile.
-  __device__ __forceinline__ uint32_t prefetch_bytes() const { return res_staged ? 2 * kOutTileBytes : 0; }
-  __device__ __forceinline__ void prefetch(int half, int m0, int n0, uint32_t out_smem, uint32_t bar) const {
+  // Column passes: with ncp = 2 a pass handles one of each half's two 32-column
+  // chunks and the staging area holds two tiles (slot = half); with ncp = 1 all four
+  // chunks at once (slot = chunk).
+  // Bytes one half's store thread prefetches into its staging tiles per pass.
+  __device__ __forceinline__ uint32_t prefetch_bytes(int ncp = 1) const {
+    return res_staged ? (2 / ncp) * kOutTileBytes : 0;
+  }
+  __device__ __forceinline__ void prefetch(int half, int m0, int n0, uint32_t out_smem, uint32_t bar,
+                                           int cp = 0, int ncp = 1) const {
     for (int j = 0; j < 2; ++j) {
-      const int chunk = half * 2 + j;
-      tma_load_2d(out_smem + chunk * kOutTileBytes, &map_res, bar, n0 + chunk * 32, m0);
+      if (ncp == 2 && j != cp) continue;
+      const int chunk = half * 2 + j, slot = ncp == 1 ? chunk : half;
+      tma_load_2d(out_smem + slot * kOutTileBytes, &map_res, bar, n0 + chunk * 32, m0);
     }
   }
 
@@ -293,11 +304,14 @@ struct ProjEpilogue {
 
   template <int BN>
   __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
-                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+                                      const float* cbuf, uint32_t out_smem, bool valid, int cp = 0,
+                                      int ncp = 1) const {
     static_assert(BN == 128, "projection tiles are 128 columns wide");
 #pragma unroll 1
     for (int j = 0; j < 2; ++j) {
+      if (ncp == 2 && j != cp) continue;
       const int chunk = half * 2 + j;  // 32 columns
+      const int slot = ncp == 1 ? chunk : half;
       float x[32];
       tmem_ld32(tmem_row + chunk * 32, x);
       if (valid) {
@@ -306,7 +320,7 @@ struct ProjEpilogue {
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[i] = (x[i] + bias[i]) * ls1[i];
         if (a.residual && res_staged) {
-          const uint32_t tile = out_smem + chunk * kOutTileBytes;
+          const uint32_t tile = out_smem + slot * kOutTileBytes;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint4 v = ld_shared_v4(tile + sw128_offset(r, c));
@@ -328,7 +342,7 @@ struct ProjEpilogue {
           }
         }
       }
-      const uint32_t tile = out_smem + chunk * kOutTileBytes;
+      const uint32_t tile = out_smem + slot * kOutTileBytes;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         st_shared_v4(tile + sw128_offset(r, c),
@@ -339,10 +353,12 @@ struct ProjEpilogue {
 
   __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
 
-  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem, int cp = 0,
+                                        int ncp = 1) const {
     for (int j = 0; j < 2; ++j) {
-      const int chunk = half * 2 + j;
-      tma_store_2d(&map_out, out_smem + chunk * kOutTileBytes, n0 + chunk * 32, m0);
+      if (ncp == 2 && j != cp) continue;
+      const int chunk = half * 2 + j, slot = ncp == 1 ? chunk : half;
+      tma_store_2d(&map_out, out_smem + slot * kOutTileBytes, n0 + chunk * 32, m0);
     }
     bulk_commit_group();
   }
@@ -358,8 +374,8 @@ struct PatchEpilogue {
   PatchEpilogueArgs a;
   CUtensorMap map_out;  // F32 (E, n_patches, views), strides (E, n_tok*E) floats, box 32 x 128 x 1
 
-  __device__ __forceinline__ uint32_t prefetch_bytes() const { return 0; }
-  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t) const {}
+  __device__ __forceinline__ uint32_t prefetch_bytes(int = 1) const { return 0; }
+  __device__ __forceinline__ void prefetch(int, int, int, uint32_t, uint32_t, int = 0, int = 1) const {}
 
   __device__ __forceinline__ bool one_view(int m0) const {
     const int last = min(m0 + kBM - 1, a.rows - 1);
@@ -372,14 +388,17 @@ struct PatchEpilogue {
 
   template <int BN>
   __device__ __forceinline__ void run(uint32_t tmem_row, int r, int m0, int n0, int half,
-                                      const float* cbuf, uint32_t out_smem, bool valid) const {
+                                      const float* cbuf, uint32_t out_smem, bool valid, int cp = 0,
+                                      int ncp = 1) const {
     static_assert(BN == 128, "patch tiles are 128 columns wide");
     const int m = m0 + r;
     const int view = m / a.n_patches, p = m - view * a.n_patches;
     const bool staged = one_view(m0);
 #pragma unroll 1
     for (int j = 0; j < 2; ++j) {
+      if (ncp == 2 && j != cp) continue;
       const int chunk = half * 2 + j;  // 32 columns
+      const int slot = ncp == 1 ? chunk : half;
       float x[32];
       tmem_ld32(tmem_row + chunk * 32, x);  // warp-collective: every lane loads
       const int col = n0 + chunk * 32;
@@ -397,7 +416,7 @@ struct PatchEpilogue {
       }
       if (staged) {
         // Rows past the last patch are clipped by the store; their values are unused.
-        const uint32_t tile = out_smem + chunk * kOutTileBytes;
+        const uint32_t tile = out_smem + slot * kOutTileBytes;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           st_shared_v4(tile + sw128_offset(r, c),
@@ -414,12 +433,14 @@ struct PatchEpilogue {
 
   __device__ __forceinline__ void peer_copy(int, int, int, int, int, uint32_t) const {}
 
-  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem) const {
+  __device__ __forceinline__ void store(int half, int m0, int n0, uint32_t out_smem, int cp = 0,
+                                        int ncp = 1) const {
     if (!one_view(m0)) return;
     const int view = m0 / a.n_patches, p0 = m0 - view * a.n_patches;
     for (int j = 0; j < 2; ++j) {
-      const int chunk = half * 2 + j;
-      tma_store_3d(&map_out, out_smem + chunk * kOutTileBytes, n0 + chunk * 32, p0, view);
+      if (ncp == 2 && j != cp) continue;
+      const int chunk = half * 2 + j, slot = ncp == 1 ? chunk : half;
+      tma_store_3d(&map_out, out_smem + slot * kOutTileBytes, n0 + chunk * 32, p0, view);
     }
     bulk_commit_group();
   }
@@ -602,19 +623,20 @@ cudaError_t launch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, i
 // traffic per FLOP of the narrow (N = E) projections; the epilogue then runs one
 // pass per 128-row half.
 // ---------------------------------------------------------------------------
-template <int BN, int MT, int STAGES>
+template <int BN, int MT, int STAGES, int CP>
 struct PersistentSmem {
   static constexpr uint32_t kABytes = MT * kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kStagingOffset = STAGES * kStageBytes;
-  static constexpr uint32_t kBarOffset = kStagingOffset + 4 * kOutTileBytes;
+  // CP column passes per 128-row pass: the staging area holds 4 / CP output tiles.
+  static constexpr uint32_t kBarOffset = kStagingOffset + (4 / CP) * kOutTileBytes;
   // full[S], empty[S], tmem_full[2], tmem_empty[2], final, prefetch[2]; then the TMEM
   // slot and flags
   static constexpr uint32_t kNumBars = 2 * STAGES + 7;
   static constexpr uint32_t kSlotOffset = kBarOffset + 8 * kNumBars;
   static constexpr uint32_t kConstOffset = kBarOffset + 256;
-  static constexpr uint32_t kBytes = kConstOffset + 2048;
+  static constexpr uint32_t kBytes = kConstOffset + 1536;  // 384 per-column constants
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;
   static_assert(kSlotOffset + 32 <= kConstOffset, "barrier region too small");
   static_assert(kLaunchBytes <= 227 * 1024, "shared memory budget");
@@ -622,12 +644,12 @@ struct PersistentSmem {
   static_assert(2 * MT * BN <= 512, "two accumulator buffers must fit in TMEM");
 };
 
-template <int BN, int MT, int STAGES, class Epi>
+template <int BN, int MT, int STAGES, int CP, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_persistent(const __grid_constant__ CUtensorMap map_a,
                          const __grid_constant__ CUtensorMap map_b, int M, int K, int n_tiles_n,
                          int num_tiles, const __grid_constant__ Epi epi, int* err) {
-  using L = PersistentSmem<BN, MT, STAGES>;
+  using L = PersistentSmem<BN, MT, STAGES, CP>;
   constexpr int kTileM = MT * kBM;
   constexpr uint32_t kTmemCols = 2 * MT * BN;
   extern __shared__ uint8_t smem_raw[];
@@ -746,13 +768,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int t = threadIdx.x - 64;
     const bool store_thread = ((warp - 2) & 3) == 0 && lane == 0;
     float* cbuf = reinterpret_cast<float*>(smem + L::kConstOffset);
-    const uint32_t pre_bytes = epi.prefetch_bytes();
+    const uint32_t pre_bytes = epi.prefetch_bytes(CP);
     int i = 0, pre_uses = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
       const int b = i & 1;
       const int n0 = (tile % n_tiles_n) * BN;
       bool ok = true;
-      for (int pass = 0; pass < MT; ++pass) {
+      for (int sub = 0; sub < MT * CP; ++sub) {
+        const int pass = sub / CP, cp = sub % CP;  // 128-row pass, column pass
         const int m0 = (tile / n_tiles_n) * kTileM + pass * kBM;
         // A second half that starts past the last row has nothing to load or store.
         const bool rows_here = m0 < M;
@@ -765,11 +788,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // residual tile) start loading into this half's staging tiles now.
         if (pre && store_thread) {
           mbar_arrive_expect_tx(pre_bar(half), pre_bytes);
-          epi.prefetch(half, m0, n0, staging, pre_bar(half));
+          epi.prefetch(half, m0, n0, staging, pre_bar(half), cp, CP);
         }
-        if (pass == 0) epi.stage(cbuf, n0, t);
+        if (sub == 0) epi.stage(cbuf, n0, t);
         named_bar_sync(1, 256);
-        if (pass == 0) {
+        if (sub == 0) {
           ok = mbar_wait(tfull_bar(b), (i >> 1) & 1, abort_flag, err, kDevTimeoutConsumer);
           ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
         }
@@ -778,15 +801,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) {
           tc_fence_after();
           epi.template run<BN>(tmem + b * MT * BN + pass * BN + (static_cast<uint32_t>(quad * 32) << 16), row,
-                               m0, n0, half, cbuf, staging, (m0 + row) < M);
-          if (pass == MT - 1) {
+                               m0, n0, half, cbuf, staging, (m0 + row) < M, cp, CP);
+          if (sub == MT * CP - 1) {
             tc_fence_before();
             mbar_arrive(tempty_bar(b));
           }
         }
         fence_proxy_async_smem();  // the staged tiles are read by the TMA store
         named_bar_sync(2 + half, 128);
-        if (ok && rows_here && store_thread) epi.store(half, m0, n0, staging);
+        if (ok && rows_here && store_thread) epi.store(half, m0, n0, staging, cp, CP);
         if (ok && rows_here) epi.peer_copy(half, t - 128 * half, m0, M, n0, staging);
       }
     }
@@ -818,15 +841,15 @@ int device_sms() {
   return sms;
 }
 
-template <int BN, int MT, int STAGES, class Epi>
+template <int BN, int MT, int STAGES, int CP, class Epi>
 cudaError_t launch_gemm_persistent(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K,
                                    const Epi& epi, int* err, cudaStream_t st) {
   if (M <= 0 || N % BN != 0 || K % kBK != 0 || K <= 0) return cudaErrorInvalidValue;
   CUtensorMap map_a, map_b;
   if (!encode_tma_2d_bf16(&map_a, a, K, M, kBK, MT * kBM)) return cudaErrorInvalidValue;
   if (!encode_tma_2d_bf16(&map_b, b, K, N, kBK, BN)) return cudaErrorInvalidValue;
-  using L = PersistentSmem<BN, MT, STAGES>;
-  auto kern = gemm_bf16_persistent<BN, MT, STAGES, Epi>;
+  using L = PersistentSmem<BN, MT, STAGES, CP>;
+  auto kern = gemm_bf16_persistent<BN, MT, STAGES, CP, Epi>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kLaunchBytes);
   if (e != cudaSuccess) return e;
@@ -843,7 +866,7 @@ bool gemm_per_tile() {
 }
 
 // One place picks the kernel form for every GEMM of the path.
-template <int BN, int STAGES_TILE, int MT, int STAGES_PERSIST, class Epi>
+template <int BN, int STAGES_TILE, int MT, int STAGES_PERSIST, int CP, class Epi>
 cudaError_t run_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int N, int K, const Epi& epi,
                      int* err, cudaStream_t st) {
   if (gemm_per_tile()) return launch_gemm<BN, STAGES_TILE>(a, b, M, N, K, epi, err, st);
@@ -851,9 +874,9 @@ cudaError_t run_gemm(const __nv_bfloat16* a, const __nv_bfloat16* b, int M, int 
     // 256-row tiles only when they still fill every SM; a short call (one chunk of
     // the host pipeline, one rank's slice) keeps twice as many 128-row tiles.
     if (static_cast<int64_t>((M + 2 * kBM - 1) / (2 * kBM)) * (N / BN) < device_sms())
-      return launch_gemm_persistent<BN, 1, 4>(a, b, M, N, K, epi, err, st);
+      return launch_gemm_persistent<BN, 1, 4, 1>(a, b, M, N, K, epi, err, st);
   }
-  return launch_gemm_persistent<BN, MT, STAGES_PERSIST>(a, b, M, N, K, epi, err, st);
+  return launch_gemm_persistent<BN, MT, STAGES_PERSIST, CP>(a, b, M, N, K, epi, err, st);
 }
 
 }  // namespace
@@ -867,7 +890,7 @@ cudaError_t launch_qkv_gemm(const __nv_bfloat16* x, const __nv_bfloat16* w_qkv_t
       !encode_tma_2d_bf16(&e.map_out[1], epi.k_out, embed, rows, 64, kBM) ||
       !encode_tma_2d_bf16(&e.map_out[2], epi.v_out, embed, rows, 64, kBM))
     return cudaErrorInvalidValue;
-  return run_gemm<256, 2, 1, 3>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
+  return run_gemm<256, 2, 1, 3, 1>(x, w_qkv_t, rows, 3 * embed, embed, e, err, st);
 }
 
 cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
@@ -876,7 +899,7 @@ cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, in
   Fc1Epilogue e{};
   e.a = epi;
   if (!encode_tma_2d_bf16(&e.map_out, epi.out, n, m, 64, kBM)) return cudaErrorInvalidValue;
-  return run_gemm<256, 2, 1, 3>(a, w_t, m, n, k, e, err, st);
+  return run_gemm<256, 2, 1, 3, 1>(a, w_t, m, n, k, e, err, st);
 }
 
 cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
@@ -889,7 +912,7 @@ cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, i
     if (!encode_tma_2d_f32(&e.map_res, epi.residual, n, m, 32, kBM)) return cudaErrorInvalidValue;
     e.res_staged = 1;
   }
-  return run_gemm<128, 3, 2, 3>(a, w_t, m, n, k, e, err, st);
+  return run_gemm<128, 3, 2, 4, 2>(a, w_t, m, n, k, e, err, st);
 }
 
 cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int k,
@@ -904,7 +927,9 @@ cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, 
                                  epi.embed, epi.n_patches, views, static_cast<uint64_t>(epi.embed) * 4,
                                  static_cast<uint64_t>(epi.n_tok) * epi.embed * 4, 32, kBM, 1))
     return cudaErrorInvalidValue;
-  return run_gemm<128, 3, 2, 3>(a, w_t, epi.rows, epi.embed, k, e, err, st);
+  // K = 640: a short main loop per tile, so the epilogue (position reads, row stores)
+  // bounds it; one column pass keeps the epilogue to two passes per tile.
+  return run_gemm<128, 3, 2, 3, 1>(a, w_t, epi.rows, epi.embed, k, e, err, st);
 }
 
 }  // namespace va
