@@ -436,6 +436,29 @@ def run_ours(args):
                   "views_per_rank": [va.shard_views(wl.views, n_tok, world, r)[1] // n_tok for r in range(world)],
                   "what": "12 whole blocks (attention + MLP) of the S=12 window on device, "
                           "va_backbone_device_sharded (max over ranks)"}
+        if world == 1:
+            # The same window captured once into a CUDA graph and replayed: what the
+            # route costs without host-side launch work.
+            gs = torch.cuda.Stream()
+            gs.wait_stream(stream)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=gs):
+                ctx.backbone_device_sharded(tw, v0, wl.rows, wl.gh, wl.gw, wl.views, 0, 12, 4,
+                                            stream=gs.cuda_stream)
+            graph_ms = []
+            for i in range(3 + max(3, args.steps // 2)):
+                flush_buf.zero_()
+                tw.copy_(xw)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                graph.replay()
+                b.record(stream)
+                if i >= 3:
+                    graph_ms.append((a, b))
+            torch.cuda.synchronize()
+            ctx.check_device()
+            window["graph_ms"] = round(statistics.mean(a.elapsed_time(b) for a, b in graph_ms), 3)
+            del graph
     ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
 
     # ---- token input side: this rank's views of 504x336 images -> tokens (patch

@@ -88,3 +88,45 @@ def test_backbone_route_matches_blockwise_oracle(oracle_mod):
             _close(caps[layer][1].cpu().numpy(), ref_caps[layer][1], f"cam capture {layer}")
     finally:
         c.close()
+
+
+def test_backbone_route_replays_from_a_cuda_graph():
+    """The device route issues only stream-ordered work once its position tables are
+    built, so a whole layer range can be captured into a CUDA graph and replayed:
+    the replay gives the eager result bit for bit."""
+    wl = syn.CONFIGS["cfg2_s2_global"]
+    views, n_special = wl.views, wl.n_special
+    first, last = 2, 8
+    c = va.Context(va.default_config(max_rows=wl.rows, num_register=n_special - 1, depth=12,
+                                     rope_start=ROPE_START, qknorm_start=QK_START), 0)
+    try:
+        for layer in range(first, last):
+            p = syn.layer_weights(E, seed=40, layer=layer, bias=True, norm1=True, perturb_norm=True,
+                                  ls1=True, mlp=True, ls2=True)
+            c.load_layer(layer, p)
+            c.load_mlp(layer, p)
+        x0 = torch.from_numpy(syn.hidden_states(wl.rows, E, seed=41)).cuda()
+        camera = torch.from_numpy(syn.camera_tokens(E, seed=41)).cuda()
+        side = torch.cuda.Stream()
+        t = x0.clone()
+        with torch.cuda.stream(side):  # eager run (also builds the cached tables)
+            c.backbone_device(t, wl.gh, wl.gw, views, first, last, ALT, camera_dev=camera,
+                              stream=side.cuda_stream)
+        torch.cuda.synchronize()
+        c.check_device()
+        eager = t.clone()
+
+        tg = x0.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            c.backbone_device(tg, wl.gh, wl.gw, views, first, last, ALT, camera_dev=camera,
+                              stream=side.cuda_stream)
+        for _ in range(2):
+            tg.copy_(x0)
+            g.replay()
+        torch.cuda.synchronize()
+        c.check_device()
+        assert torch.equal(tg, eager), float((tg - eager).abs().max())
+        del g
+    finally:
+        c.close()
