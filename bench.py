@@ -434,7 +434,7 @@ def run_ours(args):
         window = {"ms": round(win_ms, 3), "blocks": 12, "global_blocks": [5, 7, 9, 11],
                   "attention_flops": attn_win, "attention_tflops": round(attn_win / (win_ms * 1e-3) / 1e12, 1),
                   "views_per_rank": [va.shard_views(wl.views, n_tok, world, r)[1] // n_tok for r in range(world)],
-                  "what": "12 whole blocks (attention + MLP) of the S=12 window on device, "
+                  "what": f"12 whole blocks (attention + MLP) of the S={wl.views} window on device, "
                           "va_backbone_device_sharded (max over ranks)"}
         if world == 1:
             # The same window captured once into a CUDA graph and replayed: what the
