@@ -10,8 +10,9 @@ equal token slices (one process per GPU); each rank's K'/V rows reach the peers'
 windows over NVLink by copy engines, and the attention kernel waits on per-peer flags
 (epilogue peer stores, or an NCCL all-gather, where that is unavailable).
 The line also reports one whole block (attention + LN2/MLP) under "block", the
-12-block window under "window", and the token input side (patch projection and
-position/CLS assembly of every view) under "tokens".
+12-block window under "window", the token input side (patch projection and
+position/CLS assembly of every view) under "tokens", and the load of a Q8_0 model
+file into the device operands under "gguf".
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -581,6 +582,32 @@ def run_ours(args):
     if e2e_diff > 2e-2:
         raise SystemExit(f"e2e output differs from the device-path output (max abs {e2e_diff})")
 
+    # ---- model file: a 12-block DA3 GGUF of this width (Q8_0 linear weights, F32
+    # vectors, the patch embedding) read and converted into a fresh context's device
+    # operands by va_load_model_gguf (host wall clock, median; one GPU only).
+    gguf_section = None
+    if world == 1:
+        import tempfile
+        data = syn.gguf_model(embed=wl.embed, depth=12, heads=wl.heads, grid=37, dtype="q8_0", seed=0)
+        gctx = va.Context(va.default_config(embed_dim=wl.embed, num_heads=wl.heads, depth=12, max_rows=1024), 0)
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "model.gguf")
+            with open(path, "wb") as f:
+                f.write(data)
+            load_ms, sent = [], 0
+            with va.GgufFile(path) as gf:
+                for _ in range(4):
+                    t0 = time.perf_counter()
+                    sent = gctx.load_gguf(gf)
+                    load_ms.append((time.perf_counter() - t0) * 1e3)
+        gctx.close()
+        load_ms = statistics.median(load_ms[1:])
+        gguf_section = {"ms": round(load_ms, 2), "file_bytes": len(data), "stored_bytes": sent,
+                        "gbs": round(sent / (load_ms * 1e-3) / 1e9, 2),
+                        "what": "va_load_model_gguf of a 12-block Q8_0 model file of this width (page-cache "
+                                "resident): stored bytes -> pinned staging -> H2D -> device decode into the "
+                                "bf16/F32 operands; host wall clock, median of 3 after one warm-up"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, sample = cpu_attention_sample(wl, args.cpu_seconds)
@@ -614,6 +641,7 @@ def run_ours(args):
                                       "what": "the step's input H2D then its output D2H alone, per rank "
                                               "(median); a global block's outputs need its last input row"}},
             "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
+            "gguf": gguf_section,
             "gpu_launches": 4 * args.steps,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

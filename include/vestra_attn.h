@@ -39,6 +39,10 @@ extern "C" {
 #define VA_ERR_STATE 4   /* e.g. layer weights not loaded */
 #define VA_ERR_NCCL 5    /* communicator failure */
 #define VA_ERR_CAPACITY 6 /* request larger than a fixed-size buffer (va_op_attention_noalloc) */
+#define VA_ERR_IO 7       /* GGUF: the file could not be opened or mapped (GgufError::Io) */
+#define VA_ERR_FORMAT 8   /* GGUF: BadMagic, UnsupportedVersion or Malformed */
+#define VA_ERR_NOT_FOUND 9 /* GGUF: TensorNotFound, or a metadata key absent / of another type */
+#define VA_ERR_DTYPE 10   /* GGUF: UnsupportedDtype (tensor types other than F32, F16, Q8_0) */
 
 typedef struct va_ctx va_ctx;
 
@@ -340,6 +344,129 @@ int va_selftest_bounded_wait(va_ctx* ctx, int64_t limit_us);
  * (0: same key order).  peer_flag 0: the kernel gives up after its 2 s wait limit
  * and the call returns VA_ERR_DEVICE; the context stays usable. */
 int va_selftest_peer_wait(va_ctx* ctx, int peer_flag, float* out_max_abs);
+
+/* ------------------------------------------------------------------ GGUF model files
+ * The reference's crates/da-gguf reader (reader.rs, meta.rs, q8_0.rs), ModelConfig::
+ * from_gguf (config.rs:219-264) and weights_from_gguf (engine.rs:110-126).  The
+ * reader parses a read-only mapping of the file on the host; tensor data is
+ * converted to F32 / bf16 on the GPU.  Messages of failing va_gguf_* calls are in
+ * va_gguf_last_error() (per thread), worded like the reference's GgufError. */
+typedef struct va_gguf va_gguf;
+
+/* Kinds of metadata values, the MetaValue variants (meta.rs:1-12).  uint8/uint16
+ * keys read as U32, int8/int16 as I32 (an int8 byte zero-extended, as the reference
+ * does), int64 as U64 (bit pattern), float64 as F32; arrays of other element types
+ * are skipped and not listed. */
+#define VA_META_U32 0
+#define VA_META_I32 1
+#define VA_META_F32 2
+#define VA_META_U64 3
+#define VA_META_BOOL 4
+#define VA_META_STR 5
+#define VA_META_ARR_U32 6
+#define VA_META_ARR_I32 7
+#define VA_META_ARR_F32 8
+#define VA_META_ARR_STR 9
+
+/* GGML tensor types the reader converts (reader.rs:52-55). */
+#define VA_GGML_F32 0
+#define VA_GGML_F16 1
+#define VA_GGML_Q8_0 8
+
+/* GgufFile::open (reader.rs:213-266): versions 2 and 3, `general.alignment` (u32)
+ * or 32.  VA_ERR_IO, VA_ERR_FORMAT ("bad magic", "unsupported gguf version N",
+ * "malformed: ...").  The mapping lives until va_gguf_close. */
+int va_gguf_open(const char* path, va_gguf** out);
+void va_gguf_close(va_gguf* g);
+const char* va_gguf_last_error(void);
+int va_gguf_version(const va_gguf* g, uint32_t* version);
+
+/* Metadata in file order; a key that occurs twice answers with its first entry
+ * (meta.rs:16-18).  Keys and names are looked up as NUL-terminated strings; the
+ * enumerators also give their byte length (a key may hold a NUL byte, which makes
+ * it reachable by enumeration only).  Getters coerce like meta.rs: u32 accepts I32 (bit cast), i32
+ * accepts U32, arr_i32 accepts ARR_U32; otherwise an absent key or another kind is
+ * VA_ERR_NOT_FOUND (the reference's None).  Strings stay owned by the file handle.
+ * Array getters copy min(count, cap) values and return VA_ERR_CAPACITY when cap <
+ * count (out may be NULL to query the count). */
+int va_gguf_meta_count(const va_gguf* g, int64_t* n);
+int va_gguf_meta_entry(const va_gguf* g, int64_t i, const char** key, int64_t* key_len, int* kind);
+int va_gguf_meta_u32(const va_gguf* g, const char* key, uint32_t* out);
+int va_gguf_meta_i32(const va_gguf* g, const char* key, int32_t* out);
+int va_gguf_meta_f32(const va_gguf* g, const char* key, float* out);
+int va_gguf_meta_u64(const va_gguf* g, const char* key, uint64_t* out);
+int va_gguf_meta_bool(const va_gguf* g, const char* key, int* out);
+int va_gguf_meta_str(const va_gguf* g, const char* key, const char** s, int64_t* len);
+int va_gguf_meta_arr_u32(const va_gguf* g, const char* key, uint32_t* out, int64_t cap, int64_t* count);
+int va_gguf_meta_arr_i32(const va_gguf* g, const char* key, int32_t* out, int64_t cap, int64_t* count);
+int va_gguf_meta_arr_f32(const va_gguf* g, const char* key, float* out, int64_t cap, int64_t* count);
+/* Element i of a string array (s/len may be NULL to query only the count). */
+int va_gguf_meta_arr_str(const va_gguf* g, const char* key, int64_t i, const char** s, int64_t* len,
+                         int64_t* count);
+
+/* Tensors in file order (tensor_names, meta.rs:90-92).  shape is outer -> inner
+ * (stored dims reversed, reader.rs:300); VA_ERR_CAPACITY when shape_cap < ndims. */
+int va_gguf_tensor_count(const va_gguf* g, int64_t* n);
+int va_gguf_tensor_name(const va_gguf* g, int64_t i, const char** name, int64_t* name_len);
+int va_gguf_tensor_info(const va_gguf* g, const char* name, int* dtype, int* ndims, int64_t* shape,
+                        int shape_cap, uint64_t* offset);
+/* The checks of tensor_f32 / tensor_q8_0 (reader.rs:279-376), in their order:
+ * VA_ERR_NOT_FOUND "tensor not found: X"; Q8_0 element count not a multiple of 32
+ * and data past the end of the file: VA_ERR_FORMAT; other types: VA_ERR_DTYPE.
+ * On success: element count and the stored bytes inside the mapping (a Q8_0 tensor's
+ * 34-byte blocks, tensor_q8_0's view). */
+int va_gguf_tensor_check(const va_gguf* g, const char* name, int64_t* numel, const void** data,
+                         int64_t* nbytes);
+/* tensor_f32 on the GPU: the tensor's F32 values into out (device, numel floats);
+ * with transpose2d a rank-2 [rows, cols] tensor comes out [cols, rows], as
+ * weights_from_gguf stores it.  Runs on `stream` of the current device and returns
+ * when the values are written.  Q8_0 and F16 values are exact in F32, so the result
+ * equals the reference's host decoding bit for bit. */
+int va_gguf_tensor_device(const va_gguf* g, const char* name, int transpose2d, float* out, void* stream);
+/* The same conversion with the values copied back to host memory (out holds cap
+ * floats; VA_ERR_CAPACITY when the tensor has more): tensor_f32's result, computed
+ * on the current device.  Synchronous. */
+int va_gguf_tensor_f32(const va_gguf* g, const char* name, int transpose2d, float* out, int64_t cap);
+
+/* ModelConfig (config.rs:146-...) as read by ModelConfig::from_gguf: arch must be
+ * "depthanything3" (else VA_ERR_INVALID), required keys missing or of another kind
+ * are VA_ERR_NOT_FOUND "missing required gguf metadata key: K" (first in the
+ * struct's order), img.mean/img.std of a length other than 3 are VA_ERR_FORMAT;
+ * defaults: ffn_type "mlp", alt_start -1, cat_token 1, head_max_depth 0,
+ * head_pos_embed 1; image_size from img.resize_target, else image_size. */
+#define VA_MAX_OUT_LAYERS 16
+typedef struct va_model_config {
+  char arch[32];
+  uint32_t patch_size, image_size, embed_dim, depth, num_heads, head_dim, mlp_hidden, num_register;
+  int32_t rope_start, qknorm_start;
+  float rope_freq, ln_eps;
+  int32_t out_layers[VA_MAX_OUT_LAYERS];
+  int32_t n_out_layers;
+  char ffn_type[16];
+  int32_t alt_start, cat_token;
+  uint32_t head_features;
+  float head_max_depth;
+  int32_t head_pos_embed;
+  float img_mean[3], img_std[3];
+  char img_resize_mode[32];
+  uint32_t cam_dim_in;
+} va_model_config;
+int va_gguf_model_config(const va_gguf* g, va_model_config* cfg);
+
+/* weights_from_gguf + every va_load_* of the context in one pass, without host F32
+ * copies: each tensor's stored bytes go to the GPU (two pinned staging buffers) and
+ * one kernel writes the context's operand directly (F32 vectors; bf16 K-major
+ * matrices, where a rank-2 tensor's GGUF order [out, in] already is the operand
+ * and a flat tensor, which the reference reads as [in, out], is transposed).  For
+ * each block i < depth with vit.blk.{i}.attn_qkv.weight: the va_load_layer set
+ * (norm1, attn_qkv, attn_qnorm/knorm, attn_proj, ls1; absent optional tensors as
+ * NULL), and with vit.blk.{i}.mlp_fc1.weight the va_load_mlp set; with
+ * vit.patch_embed.weight the va_load_patch_embed set (patch_embed weight/bias,
+ * cls_token, pos_embed, register_tokens when num_register > 0); vit.norm.* when
+ * present.  Shapes are checked against the context (VA_ERR_INVALID); GGUF errors as
+ * above with the message in va_last_error.  *uploaded_bytes (optional) = stored
+ * bytes sent.  Synchronous. */
+int va_load_model_gguf(va_ctx* ctx, const va_gguf* g, int64_t* uploaded_bytes);
 
 #ifdef __cplusplus
 }

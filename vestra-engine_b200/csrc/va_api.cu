@@ -27,6 +27,7 @@ namespace {
 
 struct LayerWeights {
   bool loaded = false;
+  bool in_arena = false;               // buffers carved from the model-file arena (not freed one by one)
   __nv_bfloat16* w_qkv_t = nullptr;   // [3E][E]
   __nv_bfloat16* w_proj_t = nullptr;  // [E][E]
   float* qkv_b = nullptr;             // [3E]
@@ -47,6 +48,7 @@ constexpr int kArenaWindows = 6;  // three key/value window pairs
 // MLP sub-block of one block (vit_block.rs:131-236): LN2, fc1 (+GELU), fc2 (+ls2).
 struct MlpWeights {
   bool loaded = false;
+  bool in_arena = false;
   int hidden = 0;
   float* norm2_w = nullptr;           // [E]
   float* norm2_b = nullptr;
@@ -60,6 +62,7 @@ struct MlpWeights {
 // Patch projection and token assembly (patch_embed.rs:33-36, pos_embed.rs:23-39).
 struct PatchEmbedWeights {
   bool loaded = false;
+  bool in_arena = false;  // w_t, bias, cls, pos, regs from the model-file arena (rows is always its own)
   int patch = 0;
   int kp = 0;          // 3*patch^2 rounded up to the GEMM's 64-wide K slab
   int grid = 0;        // side of the learned position grid
@@ -95,6 +98,11 @@ struct va_ctx {
   float* local_snap = nullptr;    // [cap][E] tokens after the last local block before a global one
   float* vit_norm_w = nullptr;    // [E] final-norm affine of the captures
   float* vit_norm_b = nullptr;
+  bool vit_norm_in_arena = false;
+  // Weights read from a model file (va_load_model_gguf) live in a few large chunks
+  // carved in order, so a load makes a handful of allocations instead of one per tensor.
+  std::vector<void*> weight_chunks;
+  size_t chunk_used = 0, chunk_cap = 0;
   int64_t cap = 0;  // workspace rows
   __nv_bfloat16* x = nullptr;  // [cap][E] LN1 output, bf16
   __nv_bfloat16* q = nullptr;  // [cap][E] this rank's queries, token-major
@@ -229,40 +237,61 @@ int upload_vec(va_ctx* c, float** dst, const float* src, size_t n) {
   return VA_OK;
 }
 
+// Frees a device buffer the set owns, or forgets one carved from the weight arena.
+template <class T>
+void release(T*& p, bool in_arena) {
+  if (in_arena)
+    p = nullptr;
+  else
+    dfree(p);
+}
+
 void free_layer(LayerWeights& l) {
-  dfree(l.w_qkv_t);
-  dfree(l.w_proj_t);
-  dfree(l.qkv_b);
-  dfree(l.proj_b);
-  dfree(l.ls1);
-  dfree(l.norm1_w);
-  dfree(l.norm1_b);
-  dfree(l.qn_g);
-  dfree(l.qn_b);
-  dfree(l.kn_g);
-  dfree(l.kn_b);
+  const bool a = l.in_arena;
+  release(l.w_qkv_t, a);
+  release(l.w_proj_t, a);
+  release(l.qkv_b, a);
+  release(l.proj_b, a);
+  release(l.ls1, a);
+  release(l.norm1_w, a);
+  release(l.norm1_b, a);
+  release(l.qn_g, a);
+  release(l.qn_b, a);
+  release(l.kn_g, a);
+  release(l.kn_b, a);
+  l.in_arena = false;
   l.loaded = false;
 }
 
 void free_mlp(MlpWeights& m) {
-  dfree(m.norm2_w);
-  dfree(m.norm2_b);
-  dfree(m.w_fc1_t);
-  dfree(m.fc1_b);
-  dfree(m.w_fc2_t);
-  dfree(m.fc2_b);
-  dfree(m.ls2);
+  const bool a = m.in_arena;
+  release(m.norm2_w, a);
+  release(m.norm2_b, a);
+  release(m.w_fc1_t, a);
+  release(m.fc1_b, a);
+  release(m.w_fc2_t, a);
+  release(m.fc2_b, a);
+  release(m.ls2, a);
+  m.in_arena = false;
   m.loaded = false;
+}
+
+void free_vit_norm(va_ctx* c) {
+  release(c->vit_norm_w, c->vit_norm_in_arena);
+  release(c->vit_norm_b, c->vit_norm_in_arena);
+  c->vit_norm_in_arena = false;
 }
 
 void free_patch_embed(va_ctx* c) {
   PatchEmbedWeights& p = c->pe;
-  dfree(p.w_t);
-  dfree(p.bias);
-  dfree(p.cls);
-  dfree(p.pos);
-  dfree(p.regs);
+  const bool a = p.in_arena;
+  release(p.w_t, a);
+  release(p.bias, a);
+  release(p.cls, a);
+  release(p.pos, a);
+  release(p.regs, a);
   dfree(p.rows);
+  p.in_arena = false;
   p.loaded = false;
   for (auto& e : c->pe_cache) {
     dfree(e.dev);
@@ -873,10 +902,11 @@ void va_destroy(va_ctx* c) {
   for (auto& l : c->layers) free_layer(l);
   for (auto& m : c->mlps) free_mlp(m);
   free_patch_embed(c);
+  free_vit_norm(c);
+  for (void* chunk : c->weight_chunks) cudaFree(chunk);
+  c->weight_chunks.clear();
   dfree(c->hbuf);
   dfree(c->local_snap);
-  dfree(c->vit_norm_w);
-  dfree(c->vit_norm_b);
   dfree(c->x);
   dfree(c->q);
   close_peers(c);
@@ -1239,8 +1269,7 @@ int va_load_vit_norm(va_ctx* c, const float* norm_w, const float* norm_b) {
   if (!c || !norm_w || !norm_b) return VA_ERR_INVALID;
   VA_CUDA(c, cudaSetDevice(c->device));
   VA_CUDA(c, cudaDeviceSynchronize());
-  dfree(c->vit_norm_w);
-  dfree(c->vit_norm_b);
+  free_vit_norm(c);
   int rc;
   if ((rc = upload_vec(c, &c->vit_norm_w, norm_w, c->cfg.embed_dim))) return rc;
   return upload_vec(c, &c->vit_norm_b, norm_b, c->cfg.embed_dim);
@@ -1287,6 +1316,226 @@ int va_load_patch_embed(va_ctx* c, const float* weight_oihw, const float* bias,
   p.n_register = num_register;
   p.offset = interp_offset;
   p.loaded = true;
+  return VA_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// One model file's tensors into the context's buffers (va_load_model_gguf).  The
+// reference first builds host `Weights` (weights_from_gguf, engine.rs:110-126: a
+// rank-2 tensor transposed, any other rank as stored) and the executors read
+// linear weights from there as [in, out]; every conversion below writes what that
+// content gives, directly in the device layout.
+struct GgufLoad {
+  va_ctx* c;
+  const va_gguf* g;
+  va::GgufStager st;
+
+  // Next 256-byte-aligned piece of the weight arena, opening a new chunk of at
+  // least 64 MiB when the current one is full.
+  template <class T>
+  int carve(T** p, size_t count) {
+    const size_t bytes = (std::max<size_t>(count, 1) * sizeof(T) + 255) & ~static_cast<size_t>(255);
+    if (c->weight_chunks.empty() || c->chunk_used + bytes > c->chunk_cap) {
+      const size_t cap = std::max<size_t>(bytes, size_t(64) << 20);
+      void* m = nullptr;
+      VA_CUDA(c, cudaMalloc(&m, cap));
+      c->weight_chunks.push_back(m);
+      c->chunk_used = 0;
+      c->chunk_cap = cap;
+    }
+    *p = reinterpret_cast<T*>(static_cast<char*>(c->weight_chunks.back()) + c->chunk_used);
+    c->chunk_used += bytes;
+    return VA_OK;
+  }
+
+  int find(const std::string& name, bool required, va::GgufTensorRef* t, bool* present) {
+    const int rc = va::gguf_tensor_ref(g, name.c_str(), t);
+    *present = rc == VA_OK;
+    if (rc == VA_ERR_NOT_FOUND && !required) return VA_OK;
+    return rc ? fail(c, rc, va::gguf_message()) : VA_OK;
+  }
+
+  // F32 values of the Weights entry (n of them); NULL when absent and optional.
+  int vec(const std::string& name, int64_t n, bool required, float** dst) {
+    *dst = nullptr;
+    va::GgufTensorRef t;
+    bool present;
+    int rc = find(name, required, &t, &present);
+    if (rc || !present) return rc;
+    if (t.numel != n)
+      return fail(c, VA_ERR_INVALID, name + ": " + std::to_string(t.numel) + " values, expected " + std::to_string(n));
+    int rc2;
+    if ((rc2 = carve(dst, static_cast<size_t>(n)))) return rc2;
+    if (t.ndims == 2)
+      VA_CUDA(c, st.convert(t, t.shape[0], t.shape[1], t.shape[0], true, false, *dst));
+    else
+      VA_CUDA(c, st.convert(t, 1, n, n, false, false, *dst));
+    return VA_OK;
+  }
+
+  // Linear weight in -> out features as the bf16 K-major operand [out][in]: a
+  // rank-2 tensor's stored [out, in] is that operand; flat content is [in, out].
+  int linear(const std::string& name, int64_t in, int64_t out, __nv_bfloat16** dst) {
+    va::GgufTensorRef t;
+    bool present;
+    int rc = find(name, true, &t, &present);
+    if (rc) return rc;
+    if (t.numel != in * out || (t.ndims == 2 && (t.shape[0] != out || t.shape[1] != in)))
+      return fail(c, VA_ERR_INVALID, name + ": shape does not match [" + std::to_string(out) + ", " +
+                                         std::to_string(in) + "]");
+    if ((rc = carve(dst, static_cast<size_t>(in * out)))) return rc;
+    if (t.ndims == 2)
+      VA_CUDA(c, st.convert(t, out, in, in, false, true, *dst));
+    else
+      VA_CUDA(c, st.convert(t, in, out, in, true, true, *dst));
+    return VA_OK;
+  }
+
+  int layer(int i) {
+    const int E = c->cfg.embed_dim, hd = c->cfg.head_dim;
+    const std::string p = "vit.blk." + std::to_string(i) + ".";
+    LayerWeights& l = c->layers[i];
+    free_layer(l);
+    l.in_arena = true;
+    int rc;
+    if ((rc = linear(p + "attn_qkv.weight", E, 3 * E, &l.w_qkv_t))) return rc;
+    if ((rc = vec(p + "attn_qkv.bias", 3 * E, true, &l.qkv_b))) return rc;
+    if ((rc = linear(p + "attn_proj.weight", E, E, &l.w_proj_t))) return rc;
+    if ((rc = vec(p + "attn_proj.bias", E, true, &l.proj_b))) return rc;
+    if ((rc = vec(p + "ls1", E, false, &l.ls1))) return rc;
+    if ((rc = vec(p + "norm1.weight", E, false, &l.norm1_w))) return rc;
+    if ((rc = vec(p + "norm1.bias", E, false, &l.norm1_b))) return rc;
+    if ((rc = vec(p + "attn_qnorm.weight", hd, false, &l.qn_g))) return rc;
+    if ((rc = vec(p + "attn_qnorm.bias", hd, false, &l.qn_b))) return rc;
+    if ((rc = vec(p + "attn_knorm.weight", hd, false, &l.kn_g))) return rc;
+    if ((rc = vec(p + "attn_knorm.bias", hd, false, &l.kn_b))) return rc;
+    if ((l.qn_g == nullptr) != (l.kn_g == nullptr) || (l.qn_g && (!l.qn_b || !l.kn_b)))
+      return fail(c, VA_ERR_INVALID, p + "attn_qnorm/attn_knorm tensors must be given together");
+    if ((l.norm1_w == nullptr) != (l.norm1_b == nullptr))
+      return fail(c, VA_ERR_INVALID, p + "norm1 weight and bias must be given together");
+    l.loaded = true;
+    return VA_OK;
+  }
+
+  int mlp(int i, const va::GgufTensorRef& fc1) {
+    const int E = c->cfg.embed_dim;
+    const std::string p = "vit.blk." + std::to_string(i) + ".";
+    const int64_t hidden = fc1.numel / E;
+    if (fc1.numel % E != 0 || hidden <= 0 || hidden % 256 != 0 || hidden > (1 << 20))
+      return fail(c, VA_ERR_INVALID, p + "mlp_fc1.weight: hidden width must be a positive multiple of 256");
+    MlpWeights& m = c->mlps[i];
+    free_mlp(m);
+    m.in_arena = true;
+    if (hidden > c->hidden_cap) {
+      dfree(c->hbuf);
+      VA_CUDA(c, dmalloc(&c->hbuf, static_cast<size_t>(c->cap) * hidden));
+      c->hidden_cap = static_cast<int>(hidden);
+    }
+    int rc;
+    if ((rc = vec(p + "norm2.weight", E, true, &m.norm2_w))) return rc;
+    if ((rc = vec(p + "norm2.bias", E, true, &m.norm2_b))) return rc;
+    if ((rc = linear(p + "mlp_fc1.weight", E, hidden, &m.w_fc1_t))) return rc;
+    if ((rc = vec(p + "mlp_fc1.bias", hidden, true, &m.fc1_b))) return rc;
+    if ((rc = linear(p + "mlp_fc2.weight", hidden, E, &m.w_fc2_t))) return rc;
+    if ((rc = vec(p + "mlp_fc2.bias", E, true, &m.fc2_b))) return rc;
+    if ((rc = vec(p + "ls2", E, false, &m.ls2))) return rc;
+    m.hidden = static_cast<int>(hidden);
+    m.loaded = true;
+    return VA_OK;
+  }
+
+  // va_load_patch_embed's set (patch_embed.rs:150-198, pos_embed.rs:89-106).
+  int patch_embed(const va::GgufTensorRef& w) {
+    const int E = c->cfg.embed_dim;
+    const int64_t features = w.numel / E;
+    const int patch = static_cast<int>(std::lround(std::sqrt(static_cast<double>(features) / 3.0)));
+    if (w.numel % E != 0 || patch <= 0 || 3LL * patch * patch != features || features > 4096 ||
+        (w.ndims == 4 && (w.shape[0] != E || w.shape[1] != 3 || w.shape[2] != patch || w.shape[3] != patch)) ||
+        (w.ndims == 2 && w.shape[1] != E))
+      return fail(c, VA_ERR_INVALID, "vit.patch_embed.weight: shape is not [embed_dim, 3, p, p]");
+    free_patch_embed(c);
+    PatchEmbedWeights& p = c->pe;
+    p.in_arena = true;
+    const int kp = static_cast<int>((features + 63) / 64 * 64);
+    int rc;
+    if ((rc = carve(&p.w_t, static_cast<size_t>(E) * kp))) return rc;
+    if (kp > features) VA_CUDA(c, st.zero(p.w_t, static_cast<size_t>(E) * kp * sizeof(__nv_bfloat16)));
+    // OIHW content [E][3*p*p] is the K-major operand, padded to kp columns.
+    if (w.ndims == 2)
+      VA_CUDA(c, st.convert(w, w.shape[0], w.shape[1], kp, true, true, p.w_t));
+    else
+      VA_CUDA(c, st.convert(w, E, features, kp, false, true, p.w_t));
+    if ((rc = vec("vit.patch_embed.bias", E, true, &p.bias))) return rc;
+    if ((rc = vec("vit.cls_token", E, true, &p.cls))) return rc;
+    va::GgufTensorRef pos;
+    bool present;
+    if ((rc = find("vit.pos_embed", true, &pos, &present))) return rc;
+    const int64_t pos_rows = pos.numel / E;
+    const int grid = static_cast<int>(std::llround(std::sqrt(static_cast<double>(std::max<int64_t>(pos_rows - 1, 0)))));
+    if (pos.numel % E != 0 || pos_rows < 2 || static_cast<int64_t>(grid) * grid != pos_rows - 1)
+      return fail(c, VA_ERR_INVALID, "vit.pos_embed: patch-row count is not a perfect square");
+    if ((rc = vec("vit.pos_embed", pos.numel, true, &p.pos))) return rc;
+    const int nr = c->cfg.num_register;
+    if (nr > 0 && (rc = vec("vit.register_tokens", static_cast<int64_t>(nr) * E, true, &p.regs))) return rc;
+    if (kp > E) VA_CUDA(c, dmalloc(&p.rows, static_cast<size_t>(c->cap) * kp));
+    p.patch = patch;
+    p.kp = kp;
+    p.grid = grid;
+    p.n_register = nr;
+    p.offset = 0.1f;
+    p.loaded = true;
+    return VA_OK;
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int va_load_model_gguf(va_ctx* c, const va_gguf* g, int64_t* uploaded_bytes) {
+  if (!c) return VA_ERR_INVALID;
+  if (!g) return fail(c, VA_ERR_INVALID, "null model file");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  VA_CUDA(c, cudaDeviceSynchronize());  // earlier calls may still read the weights being replaced
+  // A model file replaces everything the previous one loaded: release the sets that
+  // still point into the old arena, then the arena itself.
+  for (auto& l : c->layers)
+    if (l.in_arena) free_layer(l);
+  for (auto& m : c->mlps)
+    if (m.in_arena) free_mlp(m);
+  if (c->pe.in_arena) free_patch_embed(c);
+  if (c->vit_norm_in_arena) free_vit_norm(c);
+  for (void* chunk : c->weight_chunks) cudaFree(chunk);
+  c->weight_chunks.clear();
+  c->chunk_used = c->chunk_cap = 0;
+  GgufLoad L{c, g, {}};
+  int rc;
+  va::GgufTensorRef t;
+  for (int i = 0; i < c->cfg.depth; ++i) {
+    const std::string p = "vit.blk." + std::to_string(i) + ".";
+    if (va::gguf_tensor_ref(g, (p + "attn_qkv.weight").c_str(), &t) == VA_ERR_NOT_FOUND) continue;
+    if ((rc = L.layer(i))) return rc;
+    rc = va::gguf_tensor_ref(g, (p + "mlp_fc1.weight").c_str(), &t);
+    if (rc == VA_ERR_NOT_FOUND) continue;
+    if (rc) return fail(c, rc, va::gguf_message());
+    if ((rc = L.mlp(i, t))) return rc;
+  }
+  rc = va::gguf_tensor_ref(g, "vit.patch_embed.weight", &t);
+  if (rc != VA_ERR_NOT_FOUND) {
+    if (rc) return fail(c, rc, va::gguf_message());
+    if ((rc = L.patch_embed(t))) return rc;
+  }
+  if (va::gguf_tensor_ref(g, "vit.norm.weight", &t) != VA_ERR_NOT_FOUND) {
+    free_vit_norm(c);
+    c->vit_norm_in_arena = true;
+    if ((rc = L.vec("vit.norm.weight", c->cfg.embed_dim, true, &c->vit_norm_w))) return rc;
+    if ((rc = L.vec("vit.norm.bias", c->cfg.embed_dim, true, &c->vit_norm_b))) return rc;
+  }
+  VA_CUDA(c, L.st.finish());
+  if (uploaded_bytes) *uploaded_bytes = static_cast<int64_t>(L.st.uploaded);
   return VA_OK;
 }
 

@@ -6,7 +6,10 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
+
+struct va_gguf;
 
 namespace va {
 
@@ -203,5 +206,44 @@ cudaError_t launch_token_specials(const float* cls, const float* pos, const floa
 // Patch projection GEMM: a = patch rows [rows][k] bf16, w_t = filter [E][k] bf16.
 cudaError_t launch_patch_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int k,
                               const PatchEpilogueArgs& epi, int* err, cudaStream_t st);
+
+// ---- GGUF model files (va_gguf.cu) ----
+// One tensor of an open file after the checks of the reference's tensor_f32.
+struct GgufTensorRef {
+  int dtype;            // 0 F32, 1 F16, 8 Q8_0
+  int ndims;
+  int64_t shape[8];     // outer -> inner (stored dims reversed); 1 past ndims
+  int64_t numel;
+  const uint8_t* data;  // the stored bytes inside the file mapping
+  size_t bytes;
+};
+// VA_OK, VA_ERR_NOT_FOUND (absent), or the failing check's code; message in gguf_message().
+int gguf_tensor_ref(const va_gguf* g, const char* name, GgufTensorRef* out);
+const char* gguf_message();
+// Stored bytes (device copy, 256-byte aligned) -> F32 or bf16.  Not transposed:
+// dst[r*ld + c] = value(r*cols + c); transposed: dst[c*ld + r] = value(r*cols + c).
+cudaError_t launch_gguf_convert(const uint8_t* src, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                                bool transpose, bool out_bf16, void* dst, cudaStream_t st);
+// Streams tensors to the device through two pinned staging buffers on its own
+// stream: the host copy of one tensor overlaps the upload and conversion of the last.
+class GgufStager {
+ public:
+  ~GgufStager();
+  cudaError_t convert(const GgufTensorRef& t, int64_t rows, int64_t cols, int64_t ld, bool transpose,
+                      bool out_bf16, void* dst);
+  cudaError_t zero(void* dst, size_t bytes);  // cudaMemsetAsync on the staging stream
+  cudaError_t finish();  // waits for every conversion issued so far
+  size_t uploaded = 0;   // stored bytes sent to the device
+ private:
+  cudaError_t reserve(size_t bytes);
+  void release();
+  cudaStream_t stream_ = nullptr;
+  cudaEvent_t ev_[2] = {};
+  uint8_t* pinned_[2] = {};
+  uint8_t* raw_[2] = {};
+  bool used_[2] = {};
+  size_t cap_ = 0;
+  int slot_ = 0;
+};
 
 }  // namespace va

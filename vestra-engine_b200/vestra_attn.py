@@ -25,7 +25,12 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_build", "libvestra_attn.so")
 
-VA_OK, VA_ERR_INVALID, VA_ERR_CUDA, VA_ERR_DEVICE, VA_ERR_STATE, VA_ERR_NCCL, VA_ERR_CAPACITY = range(7)
+(VA_OK, VA_ERR_INVALID, VA_ERR_CUDA, VA_ERR_DEVICE, VA_ERR_STATE, VA_ERR_NCCL, VA_ERR_CAPACITY, VA_ERR_IO,
+ VA_ERR_FORMAT, VA_ERR_NOT_FOUND, VA_ERR_DTYPE) = range(11)
+# va_gguf metadata kinds (the MetaValue variants) and GGML tensor types
+(META_U32, META_I32, META_F32, META_U64, META_BOOL, META_STR, META_ARR_U32, META_ARR_I32, META_ARR_F32,
+ META_ARR_STR) = range(10)
+GGML_F32, GGML_F16, GGML_Q8_0 = 0, 1, 8
 NOALLOC_MAX_ELEMS = 1 << 21  # heads * n * 64 limit of va_op_attention_noalloc
 
 # Every symbol include/vestra_attn.h declares (checked by tests/test_abi.py).
@@ -43,6 +48,12 @@ EXPORTED = [
     "va_op_attention_noalloc",
     "va_load_patch_embed", "va_prepare_tokens_device", "va_prepare_tokens_host", "va_pos_embed_device",
     "va_selftest_peer_wait",
+    "va_gguf_open", "va_gguf_close", "va_gguf_last_error", "va_gguf_version", "va_gguf_meta_count",
+    "va_gguf_meta_entry", "va_gguf_meta_u32", "va_gguf_meta_i32", "va_gguf_meta_f32", "va_gguf_meta_u64",
+    "va_gguf_meta_bool", "va_gguf_meta_str", "va_gguf_meta_arr_u32", "va_gguf_meta_arr_i32",
+    "va_gguf_meta_arr_f32", "va_gguf_meta_arr_str", "va_gguf_tensor_count", "va_gguf_tensor_name",
+    "va_gguf_tensor_info", "va_gguf_tensor_check", "va_gguf_tensor_device", "va_gguf_tensor_f32",
+    "va_gguf_model_config", "va_load_model_gguf",
 ]
 
 
@@ -60,6 +71,26 @@ class VaConfig(ctypes.Structure):
         ("depth", ctypes.c_int32), ("num_register", ctypes.c_int32), ("rope_start", ctypes.c_int32),
         ("qknorm_start", ctypes.c_int32), ("rope_freq", ctypes.c_float), ("ln_eps", ctypes.c_float),
         ("qk_norm_eps", ctypes.c_float), ("rope_pairing", ctypes.c_int32), ("max_rows", ctypes.c_int32),
+    ]
+
+
+class VaModelConfig(ctypes.Structure):
+    """va_model_config: ModelConfig as ModelConfig::from_gguf reads it (config.rs:146-264)."""
+
+    _fields_ = [
+        ("arch", ctypes.c_char * 32),
+        ("patch_size", ctypes.c_uint32), ("image_size", ctypes.c_uint32), ("embed_dim", ctypes.c_uint32),
+        ("depth", ctypes.c_uint32), ("num_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+        ("mlp_hidden", ctypes.c_uint32), ("num_register", ctypes.c_uint32),
+        ("rope_start", ctypes.c_int32), ("qknorm_start", ctypes.c_int32),
+        ("rope_freq", ctypes.c_float), ("ln_eps", ctypes.c_float),
+        ("out_layers", ctypes.c_int32 * 16), ("n_out_layers", ctypes.c_int32),
+        ("ffn_type", ctypes.c_char * 16),
+        ("alt_start", ctypes.c_int32), ("cat_token", ctypes.c_int32),
+        ("head_features", ctypes.c_uint32), ("head_max_depth", ctypes.c_float), ("head_pos_embed", ctypes.c_int32),
+        ("img_mean", ctypes.c_float * 3), ("img_std", ctypes.c_float * 3),
+        ("img_resize_mode", ctypes.c_char * 32),
+        ("cam_dim_in", ctypes.c_uint32),
     ]
 
 
@@ -125,6 +156,33 @@ def load_library(path: str = LIB_PATH):
         "va_prepare_tokens_host": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp], c_int),
         "va_pos_embed_device": ([_vp, c_int, c_int, _vp, _vp], c_int),
         "va_selftest_peer_wait": ([_vp, c_int, _f32p], c_int),
+        "va_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(_vp)], c_int),
+        "va_gguf_close": ([_vp], None),
+        "va_gguf_last_error": ([], ctypes.c_char_p),
+        "va_gguf_version": ([_vp, ctypes.POINTER(ctypes.c_uint32)], c_int),
+        "va_gguf_meta_count": ([_vp, ctypes.POINTER(i64)], c_int),
+        "va_gguf_meta_entry": ([_vp, i64, ctypes.POINTER(_vp), ctypes.POINTER(i64), _i32p], c_int),
+        "va_gguf_meta_u32": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32)], c_int),
+        "va_gguf_meta_i32": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32)], c_int),
+        "va_gguf_meta_f32": ([_vp, ctypes.c_char_p, _f32p], c_int),
+        "va_gguf_meta_u64": ([_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)], c_int),
+        "va_gguf_meta_bool": ([_vp, ctypes.c_char_p, _i32p], c_int),
+        "va_gguf_meta_str": ([_vp, ctypes.c_char_p, ctypes.POINTER(_vp), ctypes.POINTER(i64)], c_int),
+        "va_gguf_meta_arr_u32": ([_vp, ctypes.c_char_p, _vp, i64, ctypes.POINTER(i64)], c_int),
+        "va_gguf_meta_arr_i32": ([_vp, ctypes.c_char_p, _vp, i64, ctypes.POINTER(i64)], c_int),
+        "va_gguf_meta_arr_f32": ([_vp, ctypes.c_char_p, _vp, i64, ctypes.POINTER(i64)], c_int),
+        "va_gguf_meta_arr_str": ([_vp, ctypes.c_char_p, i64, ctypes.POINTER(_vp), ctypes.POINTER(i64),
+                                  ctypes.POINTER(i64)], c_int),
+        "va_gguf_tensor_count": ([_vp, ctypes.POINTER(i64)], c_int),
+        "va_gguf_tensor_name": ([_vp, i64, ctypes.POINTER(_vp), ctypes.POINTER(i64)], c_int),
+        "va_gguf_tensor_info": ([_vp, ctypes.c_char_p, _i32p, _i32p, ctypes.POINTER(i64), c_int,
+                                 ctypes.POINTER(ctypes.c_uint64)], c_int),
+        "va_gguf_tensor_check": ([_vp, ctypes.c_char_p, ctypes.POINTER(i64), ctypes.POINTER(_vp),
+                                  ctypes.POINTER(i64)], c_int),
+        "va_gguf_tensor_device": ([_vp, ctypes.c_char_p, c_int, _vp, _vp], c_int),
+        "va_gguf_tensor_f32": ([_vp, ctypes.c_char_p, c_int, _vp, i64], c_int),
+        "va_gguf_model_config": ([_vp, ctypes.POINTER(VaModelConfig)], c_int),
+        "va_load_model_gguf": ([_vp, _vp, ctypes.POINTER(i64)], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -188,6 +246,15 @@ class ModelConfig:
                               qknorm_start=self.qknorm_start, rope_freq=self.rope_freq, ln_eps=self.ln_eps,
                               qk_norm_eps=qk_norm_eps, rope_pairing=rope_pairing, max_rows=max_rows)
 
+    @classmethod
+    def from_gguf(cls, g: "GgufFile") -> "ModelConfig":
+        """ModelConfig::from_gguf (config.rs:219-264), the fields of this path."""
+        m = g.model_config()
+        return cls(embed_dim=m["embed_dim"], num_heads=m["num_heads"], head_dim=m["head_dim"], depth=m["depth"],
+                   num_register=m["num_register"], rope_start=m["rope_start"], qknorm_start=m["qknorm_start"],
+                   rope_freq=m["rope_freq"], ln_eps=m["ln_eps"], alt_start=m["alt_start"],
+                   patch_size=m["patch_size"])
+
     def is_global(self, layer_idx: int) -> bool:
         """backbone.rs:459-460 / :770-771."""
         return self.alt_start >= 0 and layer_idx >= self.alt_start and layer_idx % 2 == 1
@@ -232,7 +299,7 @@ class Context:
         """p: norm2_w/b [E], fc1_w [E,H], fc1_b [H], fc2_w [H,E], fc2_b [E], optional ls2 [E]."""
         keep = {k: _f32(v) for k, v in p.items() if v is not None}
         g = lambda k: _ptr(keep.get(k))  # noqa: E731
-        hidden = keep["fc1_w"].shape[1]
+        hidden = keep["fc1_w"].size // self.cfg.embed_dim  # [E, hidden], or flat as the reference's Weights
         self.check(self.lib.va_load_mlp(self.h, layer, hidden, g("norm2_w"), g("norm2_b"), g("fc1_w"),
                                         g("fc1_b"), g("fc2_w"), g("fc2_b"), g("ls2")))
 
@@ -256,6 +323,17 @@ class Context:
     def load_vit_norm(self, w, b):
         w, b = _f32(w), _f32(b)
         self.check(self.lib.va_load_vit_norm(self.h, _ptr(w), _ptr(b)))
+
+    def load_gguf(self, g: "GgufFile") -> int:
+        """Every block / patch-embedding / final-norm tensor of an open model file
+        straight into the device operands (va_load_model_gguf).  Returns the stored
+        bytes uploaded."""
+        n = ctypes.c_int64(0)
+        self.check(self.lib.va_load_model_gguf(self.h, g.h, ctypes.byref(n)))
+        if PATCH_EMBED_WEIGHT in g.tensor_names():
+            _, shape, _ = g.tensor_info(PATCH_EMBED_WEIGHT)
+            self._patch = int(round((int(np.prod(shape)) // self.cfg.embed_dim // 3) ** 0.5))
+        return n.value
 
     def backbone_device(self, tokens_dev, gh, gw, view_count, first_layer, last_layer, alt_start,
                         camera_dev=None, out_layers=(), cat_token=True, stream=0):
@@ -433,7 +511,22 @@ class Context:
         return self.lib.va_last_error(self.h).decode()
 
 
-class CudaAttentionExecutor:
+class _FromGguf:
+    """Engine::load's route (engine.rs:110-126, :323) for the executor classes."""
+
+    @classmethod
+    def from_gguf(cls, path, device: int = 0, max_rows: int = 12 * 866):
+        """The config and every tensor the context holds, from a model file,
+        converted on the device (va_load_model_gguf)."""
+        with GgufFile(path) as g:
+            self = cls.__new__(cls)
+            self.cfg = ModelConfig.from_gguf(g)
+            self.ctx = Context(self.cfg.to_va(max_rows), device)
+            self.ctx.load_gguf(g)
+        return self
+
+
+class CudaAttentionExecutor(_FromGguf):
     """AttentionExecutor (vit_block.rs:95-105) backed by the sm_100a path.
 
     Built from the reference's `Weights` naming (dict name -> F32 array, linear
@@ -457,7 +550,7 @@ class CudaAttentionExecutor:
         return self.ctx.attention_host(layer_idx, ln1, gh, gw, view_count, global_)
 
 
-class CudaTransformerTailExecutor:
+class CudaTransformerTailExecutor(_FromGguf):
     """TransformerTailExecutor (vit_block.rs:110-129) backed by the sm_100a path.
 
     Uploads every block's attention and MLP weights once from the reference's
@@ -490,7 +583,7 @@ CLS_TOKEN_WEIGHT = "vit.cls_token"
 REGISTER_TOKENS_WEIGHT = "vit.register_tokens"
 
 
-class CudaPatchEmbedExecutor:
+class CudaPatchEmbedExecutor(_FromGguf):
     """CudaPatchEmbedExecutor (patch_embed.rs:140-245) backed by the sm_100a path.
 
     Uploads the patch filter, bias, CLS token, learned positions and (when the
@@ -515,6 +608,220 @@ class CudaPatchEmbedExecutor:
 
     def run_views(self, images, height, width):
         return self.ctx.prepare_tokens_host(images, height, width)
+
+
+class GgufFile:
+    """GgufFile (crates/da-gguf reader.rs / meta.rs) over the library's va_gguf_*.
+
+    The header, metadata and tensor infos are parsed on the host over a read-only
+    mapping of the file; tensor values are converted on the GPU (tensor_f32).
+    Getters return None where the reference's return Option::None (absent key or
+    another kind).  Errors raise VestraError with the reference's GgufError text.
+    """
+
+    def __init__(self, path):
+        self.lib = load_library()
+        h = _vp()
+        rc = self.lib.va_gguf_open(os.fsencode(path), ctypes.byref(h))
+        if rc != VA_OK:
+            raise VestraError(rc, self.lib.va_gguf_last_error().decode())
+        self.h = h
+        self.path = path
+
+    open = classmethod(lambda cls, path: cls(path))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.va_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _raise(self, rc):
+        raise VestraError(rc, self.lib.va_gguf_last_error().decode())
+
+    @property
+    def version(self) -> int:
+        v = ctypes.c_uint32()
+        self.lib.va_gguf_version(self.h, ctypes.byref(v))
+        return v.value
+
+    # ---- metadata (meta.rs:14-92)
+    def _scalar(self, fn, ctype, key):
+        v = ctype()
+        rc = fn(self.h, key.encode(), ctypes.byref(v))
+        if rc == VA_ERR_NOT_FOUND:
+            return None
+        if rc:
+            self._raise(rc)
+        return v.value
+
+    def meta_u32(self, key):
+        return self._scalar(self.lib.va_gguf_meta_u32, ctypes.c_uint32, key)
+
+    def meta_i32(self, key):
+        return self._scalar(self.lib.va_gguf_meta_i32, ctypes.c_int32, key)
+
+    def meta_f32(self, key):
+        return self._scalar(self.lib.va_gguf_meta_f32, ctypes.c_float, key)
+
+    def meta_u64(self, key):
+        return self._scalar(self.lib.va_gguf_meta_u64, ctypes.c_uint64, key)
+
+    def meta_bool(self, key):
+        v = self._scalar(self.lib.va_gguf_meta_bool, ctypes.c_int, key)
+        return None if v is None else bool(v)
+
+    def meta_str(self, key):
+        s, n = _vp(), ctypes.c_int64()
+        rc = self.lib.va_gguf_meta_str(self.h, key.encode(), ctypes.byref(s), ctypes.byref(n))
+        if rc == VA_ERR_NOT_FOUND:
+            return None
+        if rc:
+            self._raise(rc)
+        return ctypes.string_at(s.value, n.value).decode()
+
+    def _arr(self, fn, dtype, key):
+        n = ctypes.c_int64()
+        rc = fn(self.h, key.encode(), None, 0, ctypes.byref(n))
+        if rc == VA_ERR_NOT_FOUND:
+            return None
+        if rc:
+            self._raise(rc)
+        out = np.zeros(n.value, dtype)
+        if n.value:
+            rc = fn(self.h, key.encode(), out.ctypes.data, n.value, ctypes.byref(n))
+            if rc:
+                self._raise(rc)
+        return out.tolist()
+
+    def meta_arr_u32(self, key):
+        return self._arr(self.lib.va_gguf_meta_arr_u32, np.uint32, key)
+
+    def meta_arr_i32(self, key):
+        return self._arr(self.lib.va_gguf_meta_arr_i32, np.int32, key)
+
+    def meta_arr_f32(self, key):
+        return self._arr(self.lib.va_gguf_meta_arr_f32, np.float32, key)
+
+    def meta_arr_str(self, key):
+        n = ctypes.c_int64()
+        rc = self.lib.va_gguf_meta_arr_str(self.h, key.encode(), 0, None, None, ctypes.byref(n))
+        if rc == VA_ERR_NOT_FOUND:
+            return None
+        if rc:
+            self._raise(rc)
+        out = []
+        for i in range(n.value):
+            s, ln = _vp(), ctypes.c_int64()
+            self.lib.va_gguf_meta_arr_str(self.h, key.encode(), i, ctypes.byref(s), ctypes.byref(ln), None)
+            out.append(ctypes.string_at(s.value, ln.value).decode())
+        return out
+
+    _GETTER = {META_U32: "meta_u32", META_I32: "meta_i32", META_F32: "meta_f32", META_U64: "meta_u64",
+               META_BOOL: "meta_bool", META_STR: "meta_str", META_ARR_U32: "meta_arr_u32",
+               META_ARR_I32: "meta_arr_i32", META_ARR_F32: "meta_arr_f32", META_ARR_STR: "meta_arr_str"}
+
+    @property
+    def kv(self):
+        """[(key, kind, value)] in file order (GgufFile::kv)."""
+        n = ctypes.c_int64()
+        self.lib.va_gguf_meta_count(self.h, ctypes.byref(n))
+        out = []
+        for i in range(n.value):
+            k, ln, kind = _vp(), ctypes.c_int64(), ctypes.c_int()
+            self.lib.va_gguf_meta_entry(self.h, i, ctypes.byref(k), ctypes.byref(ln), ctypes.byref(kind))
+            out.append((ctypes.string_at(k.value, ln.value).decode(), kind.value))
+        # a repeated key answers with its first entry (meta.rs:16-18); a key holding a
+        # NUL byte cannot be looked up by name and lists None
+        return [(k, kind, None if "\0" in k else getattr(self, self._GETTER[kind])(k)) for k, kind in out]
+
+    # ---- tensors
+    def tensor_names(self):
+        n = ctypes.c_int64()
+        self.lib.va_gguf_tensor_count(self.h, ctypes.byref(n))
+        names = []
+        for i in range(n.value):
+            s, ln = _vp(), ctypes.c_int64()
+            self.lib.va_gguf_tensor_name(self.h, i, ctypes.byref(s), ctypes.byref(ln))
+            names.append(ctypes.string_at(s.value, ln.value).decode())
+        return names
+
+    def tensor_info(self, name):
+        """(dtype, shape outer -> inner, offset)."""
+        dt, nd, off = ctypes.c_int(), ctypes.c_int(), ctypes.c_uint64()
+        shape = (ctypes.c_int64 * 16)()
+        rc = self.lib.va_gguf_tensor_info(self.h, name.encode(), ctypes.byref(dt), ctypes.byref(nd), shape, 16,
+                                          ctypes.byref(off))
+        if rc:
+            self._raise(rc)
+        return dt.value, list(shape[:nd.value]), off.value
+
+    def tensor_bytes(self, name) -> bytes:
+        """The stored bytes after tensor_f32's checks."""
+        n, data, nb = ctypes.c_int64(), _vp(), ctypes.c_int64()
+        rc = self.lib.va_gguf_tensor_check(self.h, name.encode(), ctypes.byref(n), ctypes.byref(data),
+                                           ctypes.byref(nb))
+        if rc:
+            self._raise(rc)
+        return ctypes.string_at(data.value, nb.value) if nb.value else b""
+
+    def tensor_q8_0(self, name):
+        """tensor_q8_0 (reader.rs:351-376) for a Q8_0 tensor: (shape, scales f16
+        [blocks], quants int8 [blocks, 32])."""
+        dtype, shape, _ = self.tensor_info(name)
+        if dtype != GGML_Q8_0:
+            raise VestraError(VA_ERR_DTYPE, f"tensor '{name}' is not Q8_0 (dtype {dtype})")
+        blk = np.frombuffer(self.tensor_bytes(name), np.uint8).reshape(-1, 34)
+        return shape, blk[:, :2].copy().view("<f2").reshape(-1), blk[:, 2:].copy().view(np.int8)
+
+    def tensor_f32(self, name, transpose2d: bool = False):
+        """tensor_f32 (reader.rs:279-349) converted on the GPU: (shape, F32 values
+        flat).  transpose2d: a rank-2 tensor comes back transposed (weights_from_gguf)."""
+        dtype, shape, _ = self.tensor_info(name)
+        n = int(np.prod(shape, dtype=np.int64))
+        out = np.empty(n, np.float32)
+        rc = self.lib.va_gguf_tensor_f32(self.h, name.encode(), int(transpose2d), out.ctypes.data, n)
+        if rc:
+            self._raise(rc)
+        return shape, out
+
+    def tensor_device(self, name, out_dev, transpose2d: bool = False, stream=0):
+        """tensor_f32 into a device buffer (numel floats)."""
+        rc = self.lib.va_gguf_tensor_device(self.h, name.encode(), int(transpose2d), _ptr(out_dev), _ptr(stream))
+        if rc:
+            self._raise(rc)
+
+    def model_config(self) -> dict:
+        """ModelConfig::from_gguf (config.rs:219-264), every field."""
+        c = VaModelConfig()
+        rc = self.lib.va_gguf_model_config(self.h, ctypes.byref(c))
+        if rc:
+            self._raise(rc)
+        d = {f: getattr(c, f) for f, _ in VaModelConfig._fields_}
+        for f in ("arch", "ffn_type", "img_resize_mode"):
+            d[f] = d[f].decode()
+        d["out_layers"] = list(c.out_layers[:c.n_out_layers])
+        del d["n_out_layers"]
+        d["img_mean"], d["img_std"] = list(c.img_mean), list(c.img_std)
+        d["cat_token"], d["head_pos_embed"] = bool(c.cat_token), bool(c.head_pos_embed)
+        return d
+
+
+def weights_from_gguf(g: GgufFile) -> dict:
+    """weights_from_gguf (engine.rs:110-126): name -> F32 values, rank-2 tensors
+    transposed to [in, out]; converted on the GPU."""
+    return {name: g.tensor_f32(name, transpose2d=True)[1] for name in g.tensor_names()}
 
 
 def mlp_params_from_weights(weights: dict, i: int) -> dict:
