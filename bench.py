@@ -571,7 +571,27 @@ def run_ours(args):
     copy_ms = copy_ms[3:]
     h2d_ms = max_over_ranks(statistics.median(c[0] for c in copy_ms))
     d2h_ms = max_over_ranks(statistics.median(c[1] for c in copy_ms))
-    del d_in, h_tmp
+    # Both directions at once (the floor of a pipelined batch): one step's input in
+    # and another buffer's output back on two streams, timed from a common start.
+    d_out = torch.empty_like(d_in)
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    duplex = []
+    for _ in range(3 + args.steps):
+        ca, cb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ca.record(stream)
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        with torch.cuda.stream(s_in):
+            d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            h_tmp.copy_(d_out, non_blocking=True)
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+        cb.record(stream)
+        cb.synchronize()
+        duplex.append(ca.elapsed_time(cb))
+    duplex_ms = max_over_ranks(statistics.median(duplex[3:]))
+    del d_in, h_tmp, d_out
     e2e_value = flops / (e2e_s / args.steps) / 1e12
     # parity of the host path against the device path on this input.  The host path
     # attends its queries in wave-sized chunks, the device path in one launch whose
@@ -581,6 +601,31 @@ def run_ours(args):
     e2e_diff = max_over_ranks(e2e_diff if np.isfinite(e2e_diff) else 1e30)
     if e2e_diff > 2e-2:
         raise SystemExit(f"e2e output differs from the device-path output (max abs {e2e_diff})")
+    # The same steps as independent requests through va_attention_host_batch: step
+    # s+1's copy in runs beside step s's attention and copy out (both PCIe directions
+    # at once).  One GPU; two pinned input and output buffers, alternating.
+    pipelined = None
+    if world == 1:
+        h_ins = [h_in, torch.from_numpy(x_local.copy()).pin_memory()]
+        h_outs = [torch.empty_like(h_in).pin_memory() for _ in range(2)]
+        ins = [h_ins[s % 2] for s in range(args.steps)]
+        outs = [h_outs[s % 2] for s in range(args.steps)]
+        ctx.attention_host_batch(LAYER, ins[:2], outs[:2], wl.gh, wl.gw, wl.views, wl.global_)  # warm-up
+        flush_buf.zero_()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        ctx.attention_host_batch(LAYER, ins, outs, wl.gh, wl.gw, wl.views, wl.global_)
+        pipe_s = time.perf_counter() - t
+        pipe_diff = max(float(np.abs(o.numpy() - h_out.numpy()).max()) for o in h_outs)
+        if not pipe_diff == 0.0:
+            raise SystemExit(f"pipelined host batch differs from va_attention_host (max abs {pipe_diff})")
+        pipelined = {"value": round(flops / (pipe_s / args.steps) / 1e12, 3), "unit": "TFLOP/s",
+                     "ms_per_step": round(pipe_s / args.steps * 1e3, 4),
+                     "h2d_bytes_per_step": int(wl.rows * wl.embed * 4),
+                     "d2h_bytes_per_step": int(wl.rows * wl.embed * 4),
+                     "path": "va_attention_host_batch (C ABI, K independent steps in one call, pinned host "
+                             "in/out; outputs bitwise equal to va_attention_host)"}
+        del h_ins, h_outs, ins, outs
 
     # ---- model file: a 12-block DA3 GGUF of this width (Q8_0 linear weights, F32
     # vectors, the patch embedding) read and converted into a fresh context's device
@@ -636,10 +681,14 @@ def run_ours(args):
                     "max_abs_vs_device_path": e2e_diff,
                     "pcie_floor_ms": {"h2d": round(h2d_ms, 4), "d2h": round(d2h_ms, 4),
                                       "sum": round(h2d_ms + d2h_ms, 4),
+                                      "duplex": round(duplex_ms, 4),
                                       "h2d_gbs": round(h_in.numel() * 4 / (h2d_ms * 1e-3) / 1e9, 1),
                                       "d2h_gbs": round(h_in.numel() * 4 / (d2h_ms * 1e-3) / 1e9, 1),
                                       "what": "the step's input H2D then its output D2H alone, per rank "
-                                              "(median); a global block's outputs need its last input row"}},
+                                              "(median); a global block's outputs need its last input row; "
+                                              "duplex: both copies at once on two streams (the floor of the "
+                                              "pipelined batch)"},
+                    "pipelined": pipelined},
             "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
             "gguf": gguf_section,
             "gpu_launches": 4 * args.steps,

@@ -110,6 +110,16 @@ int va_run_attention(va_ctx* ctx, int layer, const float* input, int64_t rows, i
 int va_attention_host(va_ctx* ctx, int layer, const float* ln1, int64_t rows, int gh, int gw,
                       int view_count, int global, float* out);
 
+/* va_attention_host over nsteps independent inputs of one shape (several requests'
+ * windows, one layer), pipelined (no reference counterpart; the reference runs one
+ * call at a time): step s+1's copy in runs beside step s's attention and copy out,
+ * so both PCIe directions are busy at once, which a single call of a global block
+ * cannot do (no output row is ready before its last input row has arrived).
+ * ln1[s] / out[s]: host buffers [rows, E] (pinned for full speed); the results are
+ * those of nsteps va_attention_host calls.  Single GPU; returns when all are done. */
+int va_attention_host_batch(va_ctx* ctx, int layer, const float* const* ln1, float* const* out, int nsteps,
+                            int64_t rows, int gh, int gw, int view_count, int global);
+
 /* Same, device-resident: ln1_dev and out_dev are device F32 [rows, E]. */
 int va_attention_device(va_ctx* ctx, int layer, const float* ln1_dev, float* out_dev,
                         int64_t rows, int gh, int gw, int view_count, int global, void* stream);

@@ -140,6 +140,12 @@ struct va_ctx {
   cudaStream_t h2d = nullptr, d2h = nullptr;
   cudaEvent_t ev_in[kMaxHostChunks] = {};
   cudaEvent_t ev_out[kMaxHostChunks] = {};
+  // Pipelined host batches alternate two staging pairs (in_f32/out_f32 and these):
+  // copy-out chunk j of pair p done, and the last QKV chunk has read pair p's input.
+  float* in_f32_alt = nullptr;
+  float* out_f32_alt = nullptr;
+  cudaEvent_t ev_d2h[2][kMaxHostChunks] = {};
+  cudaEvent_t ev_in_free[2] = {};
   int sms = 148;
   // phase profile (va_set_phase_profile): events between the launches of the last
   // device-path call: ln | qkv+qk_norm_rope | all-gather | core | proj
@@ -871,7 +877,11 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   for (int i = 0; i < kMaxHostChunks; ++i) {
     if ((e = cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
     if ((e = cudaEventCreateWithFlags(&c->ev_out[i], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
+    for (int p = 0; p < 2; ++p)
+      if ((e = cudaEventCreateWithFlags(&c->ev_d2h[p][i], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
   }
+  for (int p = 0; p < 2; ++p)
+    if ((e = cudaEventCreateWithFlags(&c->ev_in_free[p], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
   if ((e = cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
     return bail(e);
   for (int i = 0; i <= kPhases; ++i)
@@ -915,6 +925,8 @@ void va_destroy(va_ctx* c) {
   dfree(c->o);
   dfree(c->in_f32);
   dfree(c->out_f32);
+  dfree(c->in_f32_alt);
+  dfree(c->out_f32_alt);
   dfree(c->pos);
   for (auto& e : c->pos_cache) dfree(e.dev);
   dfree(c->rope_cs);
@@ -932,7 +944,11 @@ void va_destroy(va_ctx* c) {
   for (int i = 0; i < kMaxHostChunks; ++i) {
     if (c->ev_in[i]) cudaEventDestroy(c->ev_in[i]);
     if (c->ev_out[i]) cudaEventDestroy(c->ev_out[i]);
+    for (int p = 0; p < 2; ++p)
+      if (c->ev_d2h[p][i]) cudaEventDestroy(c->ev_d2h[p][i]);
   }
+  for (int p = 0; p < 2; ++p)
+    if (c->ev_in_free[p]) cudaEventDestroy(c->ev_in_free[p]);
   for (int i = 0; i <= kPhases; ++i)
     if (c->ph_ev[i]) cudaEventDestroy(c->ph_ev[i]);
   for (int p = 0; p < va::kMaxPeers; ++p) {
@@ -1207,6 +1223,76 @@ int host_call(va_ctx* c, int layer, BranchSpec b, int view_count, const float* l
   return read_device_error(c);
 }
 
+// host_call over independent steps of one shape (single GPU), pipelined.  Steps
+// alternate two staging pairs (input F32, output F32), so step s's copy in only
+// waits for step s-2's last QKV chunk and step s's projection of chunk j only for
+// step s-2's copy out of that chunk: the copy in of one step, the compute of the
+// next and the copy out of the one before run at once (both PCIe directions busy).
+int host_batch(va_ctx* c, int layer, const BranchSpec& b0, int view_count, const float* const* ln1,
+               float* const* out, int nsteps) {
+  int rc = VA_OK;
+  const int E = c->cfg.embed_dim;
+  if (nsteps > 1 && !c->in_f32_alt) {
+    VA_CUDA(c, dmalloc(&c->in_f32_alt, static_cast<size_t>(c->cap) * E));
+    VA_CUDA(c, dmalloc(&c->out_f32_alt, static_cast<size_t>(c->cap) * E));
+  }
+  Bounds in, outb;
+  plan_host_chunks(c, b0, view_count, &in, &outb);
+  const size_t row_bytes = static_cast<size_t>(E) * sizeof(float);
+  auto finish = [&](int code) {
+    cudaStreamSynchronize(c->h2d);
+    cudaStreamSynchronize(c->stream);
+    cudaStreamSynchronize(c->d2h);
+    return code;
+  };
+#define VA_HOST(call)                                                          \
+  do {                                                                         \
+    cudaError_t e_ = (call);                                                   \
+    if (e_ != cudaSuccess) return finish(cuda_fail(c, e_, #call));             \
+  } while (0)
+  const int n_in = static_cast<int>(in.size()) - 1, n_out = static_cast<int>(outb.size()) - 1;
+  for (int s = 0; s < nsteps; ++s) {
+    const int p = s & 1;
+    BranchSpec b = b0;
+    b.in = p ? c->in_f32_alt : c->in_f32;
+    b.out = p ? c->out_f32_alt : c->out_f32;
+    float* in_buf = const_cast<float*>(b.in);
+    if (s >= 2) VA_HOST(cudaStreamWaitEvent(c->h2d, c->ev_in_free[p], 0));
+    for (int i = 0; i < n_in; ++i) {
+      VA_HOST(cudaMemcpyAsync(in_buf + in[i] * E, ln1[s] + in[i] * E, (in[i + 1] - in[i]) * row_bytes,
+                              cudaMemcpyHostToDevice, c->h2d));
+      VA_HOST(cudaEventRecord(c->ev_in[i], c->h2d));
+    }
+    for (int i = 0; i < n_in; ++i) {
+      VA_HOST(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
+      if ((rc = stage_qkv(c, layer, b, in[i], in[i + 1], c->stream))) return finish(rc);
+      if (b.seg_len > 0) {  // local: the chunk's views are complete
+        if (s >= 2) VA_HOST(cudaStreamWaitEvent(c->stream, c->ev_d2h[p][i], 0));
+        if ((rc = stage_attn(c, layer, b, in[i], in[i + 1], c->stream))) return finish(rc);
+        VA_HOST(cudaEventRecord(c->ev_out[i], c->stream));
+      }
+    }
+    VA_HOST(cudaEventRecord(c->ev_in_free[p], c->stream));
+    if (b.seg_len == 0) {
+      for (int j = 0; j < n_out; ++j) {
+        if (s >= 2) VA_HOST(cudaStreamWaitEvent(c->stream, c->ev_d2h[p][j], 0));
+        if ((rc = stage_attn(c, layer, b, outb[j], outb[j + 1], c->stream))) return finish(rc);
+        VA_HOST(cudaEventRecord(c->ev_out[j], c->stream));
+      }
+    }
+    for (int j = 0; j < n_out; ++j) {
+      VA_HOST(cudaStreamWaitEvent(c->d2h, c->ev_out[j], 0));
+      VA_HOST(cudaMemcpyAsync(out[s] + outb[j] * E, b.out + outb[j] * E, (outb[j + 1] - outb[j]) * row_bytes,
+                              cudaMemcpyDeviceToHost, c->d2h));
+      VA_HOST(cudaEventRecord(c->ev_d2h[p][j], c->d2h));
+    }
+  }
+#undef VA_HOST
+  VA_CUDA(c, cudaStreamSynchronize(c->d2h));
+  finish(VA_OK);
+  return read_device_error(c);
+}
+
 
 }  // namespace
 
@@ -1222,6 +1308,21 @@ int va_attention_host(va_ctx* c, int layer, const float* ln1, int64_t rows, int 
                        view_count, global, false, &b);
   if (rc) return rc;
   return host_call(c, layer, b, view_count, ln1, out);
+}
+
+int va_attention_host_batch(va_ctx* c, int layer, const float* const* ln1, float* const* out, int nsteps,
+                            int64_t rows, int gh, int gw, int view_count, int global) {
+  if (!c || !ln1 || !out || nsteps < 0) return VA_ERR_INVALID;
+  for (int s = 0; s < nsteps; ++s)
+    if (!ln1[s] || !out[s]) return fail(c, VA_ERR_INVALID, "null step buffer");
+  if (nsteps == 0) return VA_OK;
+  if (rows <= 0 || rows > c->cap) return fail(c, VA_ERR_INVALID, "rows out of range");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  BranchSpec b;
+  int rc = make_branch(c, layer, c->in_f32, false, c->out_f32, nullptr, rows, rows, 0, gh, gw,
+                       view_count, global, false, &b);
+  if (rc) return rc;
+  return host_batch(c, layer, b, view_count, ln1, out, nsteps);
 }
 
 int va_attention_host_sharded(va_ctx* c, int layer, const float* ln1_local, float* out_local,

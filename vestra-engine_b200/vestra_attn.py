@@ -44,7 +44,7 @@ EXPORTED = [
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
     "va_load_vit_norm", "va_backbone_device", "va_backbone_device_sharded",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
-    "va_attention_host_sharded",
+    "va_attention_host_sharded", "va_attention_host_batch",
     "va_op_attention_noalloc",
     "va_load_patch_embed", "va_prepare_tokens_device", "va_prepare_tokens_host", "va_pos_embed_device",
     "va_selftest_peer_wait",
@@ -119,6 +119,7 @@ def load_library(path: str = LIB_PATH):
         "va_layer_flags": ([_vp, c_int, _i32p, _i32p], c_int),
         "va_run_attention": ([_vp, c_int, _vp, i64, c_int, c_int, _vp, _vp], c_int),
         "va_attention_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
+        "va_attention_host_batch": ([_vp, c_int, _vp, _vp, c_int, i64, c_int, c_int, c_int, c_int], c_int),
         "va_attention_device": ([_vp, c_int, _vp, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_block_attention_device": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_op_attention_device": ([_vp, _vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float,
@@ -377,6 +378,17 @@ class Context:
         self.check(self.lib.va_attention_host(self.h, layer, _ptr(ln1), rows, gh, gw, view_count,
                                               int(bool(global_)), _ptr(out)))
         return out
+
+    def attention_host_batch(self, layer, inputs, outputs, gh, gw, view_count, global_):
+        """va_attention_host over independent same-shape host inputs, pipelined."""
+        n = len(inputs)
+        assert len(outputs) == n and n > 0
+        rows = inputs[0].shape[0]
+        ins = (ctypes.c_void_p * n)(*[_ptr(x) for x in inputs])
+        outs = (ctypes.c_void_p * n)(*[_ptr(y) for y in outputs])
+        self.check(self.lib.va_attention_host_batch(self.h, layer, ins, outs, n, rows, gh, gw, view_count,
+                                                    int(bool(global_))))
+        return outputs
 
     def attention_device(self, layer, ln1_dev, out_dev, gh, gw, view_count, global_, stream=0):
         self.check(self.lib.va_attention_device(self.h, layer, _ptr(ln1_dev), _ptr(out_dev), ln1_dev.shape[0],
