@@ -297,7 +297,11 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
  * the two query tiles taking turns in the exponential section, form 6 = form 3
  * with the split tail off (one CTA per unit), form 7 = form 3 with P handed over
  * in two 64-key halves, variant 64 = 64-key half-steps with S and P
- * double-buffered in TMEM.  Query i is row
+ * double-buffered in TMEM.  variant + 256: exponents relative to 0 instead of the
+ * running row max (form 3 only; others ignore it), for callers that guarantee
+ * |q.k| / 8 * log2(e) <= 64 for every query/key pair (bf16 V only); the layer entry
+ * points choose this themselves for QK-normalised layers whose norm weights bound
+ * the scores that far (VA_SOFTMAX_FIXED_OFFSET=0 turns it off).  Query i is row
  * q_offset + i of the key window.  seg_len = 0: every query attends to all kv_rows
  * keys; seg_len > 0: independent segments of seg_len tokens (q_offset and q_count
  * multiples of seg_len).  out bf16 [q_count, heads*64]. */

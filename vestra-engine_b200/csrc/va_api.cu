@@ -39,6 +39,9 @@ struct LayerWeights {
   float* qn_b = nullptr;
   float* kn_g = nullptr;
   float* kn_b = nullptr;
+  // Bound on |q.k| * scale * log2(e) after this layer's QK-norm (qk_bound_log2);
+  // infinite without QK-norm tensors.
+  float qk_bound = INFINITY;
 };
 
 constexpr int kMaxHostChunks = 32;
@@ -99,6 +102,9 @@ struct va_ctx {
   float* vit_norm_w = nullptr;    // [E] final-norm affine of the captures
   float* vit_norm_b = nullptr;
   bool vit_norm_in_arena = false;
+  // QK-normalised layers whose score bound allows it run the softmax with a fixed
+  // exponent offset (no row max); VA_SOFTMAX_FIXED_OFFSET=0 forces the row max.
+  bool fixed_softmax = true;
   // Weights read from a model file (va_load_model_gguf) live in a few large chunks
   // carved in order, so a load makes a handful of allocations instead of one per tensor.
   std::vector<void*> weight_chunks;
@@ -265,9 +271,32 @@ void free_layer(LayerWeights& l) {
   release(l.qn_b, a);
   release(l.kn_g, a);
   release(l.kn_b, a);
+  l.qk_bound = INFINITY;
   l.in_arena = false;
   l.loaded = false;
 }
+
+// Bound on |q.k| * scale * log2(e) for a layer with QK-norm.  Each q (or k) head row
+// is gamma * xhat + beta with xhat a LayerNorm output, |xhat| <= sqrt(d), so |q| <=
+// max|gamma| sqrt(d) + |beta|; the 2D RoPE rotates pairs of components (norm kept).
+// 2 % covers the bf16 rounding of q and k.  Non-finite weights give infinity.
+float qk_bound_log2(const float* qg, const float* qb, const float* kg, const float* kb, int d) {
+  auto row_bound = [d](const float* g, const float* b) {
+    double mg = 0.0, sb = 0.0;
+    for (int i = 0; i < d; ++i) {
+      mg = std::max(mg, std::fabs(static_cast<double>(g[i])));
+      sb += static_cast<double>(b[i]) * b[i];
+    }
+    return mg * std::sqrt(static_cast<double>(d)) + std::sqrt(sb);
+  };
+  const double bound = row_bound(qg, qb) * row_bound(kg, kb) / std::sqrt(static_cast<double>(d)) *
+                       1.4426950408889634 * 1.02;
+  return std::isfinite(bound) ? static_cast<float>(bound) : INFINITY;
+}
+
+// Largest bound for which the attention kernel may use exponents relative to 0
+// (FlashArgs::fixed_offset): every 2^x then lies in [2^-64, 2^64].
+constexpr float kFixedOffsetMaxBound = 64.0f;
 
 void free_mlp(MlpWeights& m) {
   const bool a = m.in_arena;
@@ -661,6 +690,8 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
   fa.o_tok = c->o + q0 * E;
   fa.embed = E;
   fa.v_f16 = 0;
+  fa.fixed_offset = c->fixed_softmax && layer_use_qknorm(c, layer) &&
+                    c->layers[layer].qk_bound <= kFixedOffsetMaxBound;
   const __nv_bfloat16* kk = b.kwin;
   const __nv_bfloat16* vv = b.vwin;
   if (b.seg_len > 0) {
@@ -871,6 +902,10 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
   if ((e = dmalloc(&c->pos, static_cast<size_t>(c->cap))) != cudaSuccess) return bail(e);
   if ((e = dmalloc(&c->err, 1)) != cudaSuccess) return bail(e);
   if ((e = cudaMemset(c->err, 0, sizeof(int))) != cudaSuccess) return bail(e);
+  {
+    const char* fx = std::getenv("VA_SOFTMAX_FIXED_OFFSET");
+    c->fixed_softmax = !(fx && fx[0] == '0');
+  }
   if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
   if ((e = cudaStreamCreateWithFlags(&c->h2d, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
   if ((e = cudaStreamCreateWithFlags(&c->d2h, cudaStreamNonBlocking)) != cudaSuccess) return bail(e);
@@ -996,6 +1031,7 @@ int va_load_layer(va_ctx* c, int layer, const float* norm1_w, const float* norm1
   if ((rc = upload_vec(c, &l.qn_b, qnorm_b, 64))) return rc;
   if ((rc = upload_vec(c, &l.kn_g, knorm_w, 64))) return rc;
   if ((rc = upload_vec(c, &l.kn_b, knorm_b, 64))) return rc;
+  l.qk_bound = qnorm_w ? qk_bound_log2(qnorm_w, qnorm_b, knorm_w, knorm_b, 64) : INFINITY;
   l.loaded = true;
   return VA_OK;
 }
@@ -1636,6 +1672,13 @@ int va_load_model_gguf(va_ctx* c, const va_gguf* g, int64_t* uploaded_bytes) {
     if ((rc = L.vec("vit.norm.bias", c->cfg.embed_dim, true, &c->vit_norm_b))) return rc;
   }
   VA_CUDA(c, L.st.finish());
+  for (auto& l : c->layers) {
+    if (!l.in_arena || !l.qn_g) continue;
+    float h[4][64];
+    const float* src[4] = {l.qn_g, l.qn_b, l.kn_g, l.kn_b};
+    for (int i = 0; i < 4; ++i) VA_CUDA(c, cudaMemcpy(h[i], src[i], sizeof(h[i]), cudaMemcpyDeviceToHost));
+    l.qk_bound = qk_bound_log2(h[0], h[1], h[2], h[3], 64);
+  }
   if (uploaded_bytes) *uploaded_bytes = static_cast<int64_t>(L.st.uploaded);
   return VA_OK;
 }
@@ -1964,6 +2007,11 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   fa.o_tok = static_cast<__nv_bfloat16*>(out);
   fa.embed = heads * 64;
   fa.v_f16 = v_f16 ? 1 : 0;
+  if (variant >= 256) {  // caller guarantees |q.k| * scale * log2(e) <= 64
+    if (v_f16) return fail(c, VA_ERR_INVALID, "the fixed exponent offset needs bf16 V");
+    fa.fixed_offset = 1;
+    variant -= 256;
+  }
   if (variant >= 0) {
     if ((variant & 7) > 2 || (variant >> 3) > 8 || ((variant >> 3) == 8 && (variant & 7) != 0))
       return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..7), or 64");

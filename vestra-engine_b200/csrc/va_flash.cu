@@ -818,25 +818,37 @@ __global__ void __launch_bounds__(kW20Threads, 1)
             for (int e = 0; e < 4; ++e)
               if (8 * k + c0 + (e & 1) >= valid) s[4 * k + e] = -INFINITY;
         }
-        float a0 = max3f(s[0], s[1], s[4]), a1 = max3f(s[2], s[3], s[6]);
-        float b0 = max3f(s[5], s[8], s[9]), b1 = max3f(s[7], s[10], s[11]);
+        // Reference exponent of this step: the running row max (online softmax), or
+        // with fa.fixed_offset 0 for every row.  The caller sets fixed_offset only
+        // where |s| * scale * log2(e) <= 64 is guaranteed (QK-normalised rows of
+        // bounded norm), so every 2^x lies in [2^-64, 2^64]: nothing flushes or
+        // overflows in F32 or bf16 and no rescale is ever needed.
+        bool grow0 = false, grow1 = false;
+        float mn0 = 0.f, mn1 = 0.f, al0 = 1.0f, al1 = 1.0f;
+        if (!fa.fixed_offset) {
+          float a0 = max3f(s[0], s[1], s[4]), a1 = max3f(s[2], s[3], s[6]);
+          float b0 = max3f(s[5], s[8], s[9]), b1 = max3f(s[7], s[10], s[11]);
 #pragma unroll
-        for (int k = 3; k < 16; k += 2) {
-          a0 = max3f(a0, s[4 * k], s[4 * k + 1]);
-          a1 = max3f(a1, s[4 * k + 2], s[4 * k + 3]);
-          if (k + 1 < 16) {
-            b0 = max3f(b0, s[4 * k + 4], s[4 * k + 5]);
-            b1 = max3f(b1, s[4 * k + 6], s[4 * k + 7]);
+          for (int k = 3; k < 16; k += 2) {
+            a0 = max3f(a0, s[4 * k], s[4 * k + 1]);
+            a1 = max3f(a1, s[4 * k + 2], s[4 * k + 3]);
+            if (k + 1 < 16) {
+              b0 = max3f(b0, s[4 * k + 4], s[4 * k + 5]);
+              b1 = max3f(b1, s[4 * k + 6], s[4 * k + 7]);
+            }
           }
+          float mx0 = fmaxf(a0, b0), mx1 = fmaxf(a1, b1);
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * sl2;
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * sl2;
+          grow0 = mx0 > m0 + kRescaleLog2;
+          grow1 = mx1 > m1 + kRescaleLog2;
+          mn0 = grow0 ? mx0 : m0;
+          mn1 = grow1 ? mx1 : m1;
+          al0 = grow0 ? ex2(m0 - mn0) : 1.0f;
+          al1 = grow1 ? ex2(m1 - mn1) : 1.0f;
         }
-        float mx0 = fmaxf(a0, b0), mx1 = fmaxf(a1, b1);
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2)) * sl2;
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2)) * sl2;
-        const bool grow0 = mx0 > m0 + kRescaleLog2, grow1 = mx1 > m1 + kRescaleLog2;
-        const float mn0 = grow0 ? mx0 : m0, mn1 = grow1 ? mx1 : m1;
-        const float al0 = grow0 ? ex2(m0 - mn0) : 1.0f, al1 = grow1 ? ex2(m1 - mn1) : 1.0f;
         const uint64_t ng0 = f32x2_pack(-mn0, -mn0), ng1 = f32x2_pack(-mn1, -mn1);
         if (kOrder && g.nq == 2 && (t == 1 || j > 0)) {
           ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,

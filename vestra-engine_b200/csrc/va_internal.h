@@ -104,6 +104,9 @@ struct FlashArgs {
   int embed;
   int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
   int poly_per8 = kDefaultPolyPer8;  // bf16 path: variant = poly + 8 * form (see launch_flash)
+  // 1: exponents relative to 0 instead of the running row max (w20 kernel, bf16 P;
+  // other forms ignore it).  Only for inputs with |q.k| * scale * log2(e) <= 64.
+  int fixed_offset = 0;
   // Split-key tail of global attention (four-threads-per-row kernel only).  With
   // U = heads x query-pairs units and `sms` multiprocessors, the last U mod sms
   // units (the partial last wave) are each run as `splits` CTAs over disjoint key
