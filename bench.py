@@ -537,6 +537,9 @@ def run_ours(args):
                 name = {3: f"w20_poly{p}", 5: f"w20ord_poly{p}", 6: f"w20nosplit_poly{p}",
                         7: f"w20splitp_poly{p}"}.get(form, f"form{form}_poly{p}")
                 variants[name] = to_tf(time_flash(vw, p + 8 * form))
+        for p in range(3):
+            variants[f"w20fixed_poly{p}"] = to_tf(time_flash(vw, 256 + 24 + p))
+            variants[f"w20fixed_nosplit_poly{p}"] = to_tf(time_flash(vw, 256 + 48 + p))
         variants["w20half_poly0"] = to_tf(time_flash(vw, 64))
         variants["f16_p"] = to_tf(time_flash(vw.to(torch.float16)))
     peak_tflops, _, peak_kind = load_peaks()
