@@ -42,9 +42,10 @@ import synthetic as syn  # noqa: E402
 LAYER = 5           # a global block of the DA3-BASE schedule (alt_start 4: globals 5,7,9,11)
 L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one flash launch on cfg3 (47.94 MB
-# + 2.85 MB), from the ncu capture summarised in profiles/flash_fwd_d64_cfg3.md;
-# used for the roofline's `traffic` when the bench runs that workload.
-FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.78e6}
+# + 2.98 MB), from the ncu capture summarised in
+# profiles/flash_fwd_d64_fixed_offset_cfg3.md; used for the roofline's `traffic`
+# when the bench runs that workload.
+FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.92e6}
 
 
 def parse_args():
