@@ -256,7 +256,7 @@ def run_reference(args):
         "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t_full * 1e3, 3), "sample_ms_per_step": round(total / args.steps * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
         "config": workload_config(wl, 1),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": sample, "cpu": cpu_info()},
