@@ -264,7 +264,7 @@ def run_reference(args):
         "note": "CPU F32 restatement of the reference attention (vestra-kernels is un-vendored and no Rust "
                 "toolchain exists, so the reference binary cannot be built)",
     }
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=JSON_OUT, flush=True)
     return 0
 
 
@@ -711,7 +711,7 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=JSON_OUT, flush=True)
     ctx.close()
     if world > 1:
         dist.barrier()
@@ -719,8 +719,18 @@ def run_ours(args):
     return 0
 
 
+JSON_OUT = sys.stdout
+
+
 def main():
+    global JSON_OUT
     args = parse_args()
+    # The result line is the only thing on the process's stdout: file descriptor 1
+    # is pointed at stderr for everything else (NCCL's version banner, any print of
+    # the libraries), and the line goes to a duplicate of the original stdout.
+    sys.stdout.flush()
+    JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
