@@ -114,6 +114,34 @@ def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, se
     assert_close(got, ref, what=f"flash variant {variant} h{heads} n{seg}x{segs}")
 
 
+@pytest.mark.parametrize("variant", [511, 256 + 72, 256 + 73, 256 + 74, 256 + 75, 256 + 76])
+@pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 129, 1), (2, 300, 1), (12, 866, 1), (4, 865, 3),
+                                            (12, 1732, 1), (12, 10392, 1)])
+def test_flash_key_split_matches_oracle_core(ctx, oracle_mod, heads, seg, segs, variant):
+    # The key-split softmax (variant 72 + i: 64 + 8 i keys of every 128 on MUFU, the
+    # rest on the FMA pipe; 511 = the library default with the fixed exponent offset)
+    # with the fixed exponent offset, which bounded scores allow: LayerNormed q and k
+    # rows, as the QK-norm leaves them, so |q.k| / 8 * log2(e) <= 11.6.  Local
+    # segments (865 x 3) end inside a key tile whose other rows are the next
+    # segment's; the global window of 10,392 tokens runs the split tail.
+    rows = seg * segs
+    rng = np.random.default_rng(heads * 11 + seg + variant)
+
+    def normed(x):
+        x = (x - x.mean(-1, keepdims=True)) / np.sqrt(x.var(-1, keepdims=True) + 1e-5)
+        return bf16_round(x.astype(np.float32))
+
+    q, k = (normed(rng.standard_normal((heads, rows, 64))) for _ in range(2))
+    v = bf16_round(rng.standard_normal((heads, rows, 64)).astype(np.float32))
+    out = torch.zeros(rows, heads * 64, dtype=torch.bfloat16, device="cuda")
+    ctx.flash_bf16(_tok(q), _tok(k), _tok(v), heads, out, seg_len=seg if segs > 1 else 0, variant=variant)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    got = out.float().cpu().numpy().reshape(rows, heads, 64).transpose(1, 0, 2)
+    ref = oracle_mod.attention_core(q, k, v, seg_len=seg)
+    assert_close(got, ref, what=f"key-split variant {variant} h{heads} n{seg}x{segs}")
+
+
 @pytest.mark.parametrize("nranks", [2, 8])
 def test_flash_query_slices_of_a_window(ctx, oracle_mod, nranks):
     # What one rank of a sharded global block computes: its query slice against the

@@ -2011,10 +2011,14 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
     if (v_f16) return fail(c, VA_ERR_INVALID, "the fixed exponent offset needs bf16 V");
     fa.fixed_offset = 1;
     variant -= 256;
+    if (variant == 255) variant = -1;  // 511: fixed offset with the library's default layout
   }
   if (variant >= 0) {
-    if ((variant & 7) > 2 || (variant >> 3) > 8 || ((variant >> 3) == 8 && (variant & 7) != 0))
-      return fail(c, VA_ERR_INVALID, "variant must be poly (0..2) + 8 * form (0..7), or 64");
+    const int poly = variant & 7, form = variant >> 3;
+    const bool key_split = form == 9 && poly <= 4 && fa.fixed_offset;
+    if (!key_split && (poly > 2 || form > 8 || (form == 8 && poly != 0)))
+      return fail(c, VA_ERR_INVALID,
+                  "variant must be poly (0..2) + 8 * form (0..7), 64, or with the fixed offset 72..76");
     fa.poly_per8 = variant;
   }
   set_split_workspace(c, &fa);

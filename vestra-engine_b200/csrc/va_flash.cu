@@ -36,10 +36,12 @@
 #include <math.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "va_internal.h"
 #include "va_ptx.cuh"
 #include "va_tmem16.cuh"
+#include "va_tmem32.cuh"
 
 namespace va {
 
@@ -80,7 +82,9 @@ struct FlashSmem {
   // p_full, pv_done, o_final, ex_done, p_full_hi, pv_done_hi, s_full_b1, s_free_b1
   static constexpr uint32_t kNumBars = 1 + 2 * kStages + 20;
   static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
-  static constexpr uint32_t kBytes = kMisc + 64;
+  // key-split layout: partial row sums [tile][role][128] F32
+  static constexpr uint32_t kRed = kMisc + 64;
+  static constexpr uint32_t kBytes = kRed + 2 * 2 * 128 * 4;
   static constexpr uint32_t kLaunchBytes = kBytes + 1024;
 };
 
@@ -1058,6 +1062,230 @@ __global__ void __launch_bounds__(kW20Threads, 1)
   cta_teardown(c, tmem);
 }
 
+// ============================================================== "ks" layout (key split)
+// For launches with the fixed exponent offset (no row maximum, so no value has to
+// be shared between the threads of one row within a step).  20 warps as in w20;
+// the softmax warps are one thread per query row, and the two warps of a TMEM lane
+// quadrant (same SM sub-partition) split the 128 keys of every S tile:
+//   MUFU warp  keys [0, KA):   p = ex2.approx(s * c)
+//   FMA warp   keys [KA, 128): p = 2^(s * c) by exp2 on the FMA pipe (n = round(x)
+//              taken from x + 1.5 * 2^23, f = x - n in [-0.5, 0.5], the fitted
+//              cubic of exp2_fma_x2 for 2^f, n added to the exponent field)
+// so the exponentials of one step run on both pipes at once, in different warps
+// (MUFU alone gives 16 exponentials per clock per SM; the two pipes together
+// more).  Every thread keeps the partial row sum of its keys; the two halves meet
+// in shared memory after the last step.
+
+// p = 2^x for a pair x = s * c on the FMA pipe; valid for |x| <= 2^22 (the
+// fixed-offset launches keep |x| <= 64).  Returns the pair as packed F32.
+__device__ __forceinline__ uint64_t exp2_fma_pair(uint64_t s2, uint64_t c2) {
+  const uint64_t magic = f32x2_pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+  const uint64_t t = f32x2_fma(s2, c2, magic);   // low mantissa bits: n = round(x)
+  const uint64_t nn = f32x2_sub(magic, t);        // -n
+  const uint64_t f = f32x2_fma(s2, c2, nn);       // x - n
+  uint64_t p = f32x2_fma(f32x2_pack(kExp2C3, kExp2C3), f, f32x2_pack(kExp2C2, kExp2C2));
+  p = f32x2_fma(p, f, f32x2_pack(kExp2C1, kExp2C1));
+  p = f32x2_fma(p, f, f32x2_pack(kExp2C0, kExp2C0));
+  float p0, p1, t0, t1;
+  f32x2_unpack(p, p0, p1);
+  f32x2_unpack(t, t0, t1);
+  return f32x2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+                    __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
+}
+
+// One softmax thread's steps over keys [K0, K0 + NK) of its row of query tile t.
+// Returns false when a wait timed out or the CTA aborted.
+template <int K0, int NK, bool kFma>
+__device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uint32_t tS, uint32_t tP,
+                                         uint64_t sc2, float& l, int* err) {
+  volatile int* abort_flag = c.abort_flag();
+  for (int j = 0; j < g.num_kv; ++j) {
+    bool ok = mbar_wait(c.s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return false;
+    tc_fence_after();
+    float s[NK];
+    tmem_ld_cols<NK>(tS + K0, s);
+    tc_fence_before();
+    mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
+    uint32_t pk[NK / 2];
+    uint64_t acc[2];
+    // Keys at or past `valid` (the range's last tile) get probability 0.  Their
+    // scores are finite: zero-filled rows past the tensor, or another segment's
+    // keys, which the fixed-offset bound covers as well.
+    auto body = [&](auto masked_c) {
+      constexpr bool kMasked = decltype(masked_c)::value;
+      const int valid = g.last_valid - K0;
+#pragma unroll
+      for (int i = 0; i < NK / 2; ++i) {
+        const uint64_t s2 = f32x2_pack(s[2 * i], s[2 * i + 1]);
+        float p0, p1;
+        if constexpr (kFma) {
+          f32x2_unpack(exp2_fma_pair(s2, sc2), p0, p1);
+        } else {
+          float x0, x1;
+          f32x2_unpack(f32x2_mul(s2, sc2), x0, x1);
+          p0 = ex2(x0);
+          p1 = ex2(x1);
+        }
+        if constexpr (kMasked) {
+          p0 = 2 * i < valid ? p0 : 0.0f;
+          p1 = 2 * i + 1 < valid ? p1 : 0.0f;
+        }
+        const uint64_t pp = f32x2_pack(p0, p1);
+        acc[i & 1] = i < 2 ? pp : f32x2_add(acc[i & 1], pp);
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+    };
+    if (j == g.tail_iter && g.last_valid < K0 + NK)
+      body(std::true_type{});
+    else
+      body(std::false_type{});
+    if (j > 0) {
+      // PV_t(j-1) has finished reading P_t.
+      ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) return false;
+      tc_fence_after();
+    }
+    tmem_st_cols<NK / 2>(tP + K0 / 2, pk);
+    tmem_wait_st();
+    float a0, a1, b0, b1;
+    f32x2_unpack(acc[0], a0, a1);
+    f32x2_unpack(acc[1], b0, b1);
+    l += (a0 + a1) + (b0 + b1);
+    tc_fence_before();
+    mbar_arrive(c.p_full(t));
+  }
+  return true;
+}
+
+template <int KA, bool kSplit>
+__global__ void __launch_bounds__(kW20Threads, 1)
+    flash_fwd_d64_ks_kernel(const __grid_constant__ CUtensorMap map_q,
+                            const __grid_constant__ CUtensorMap map_k,
+                            const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  static_assert(KA % 8 == 0 && KA >= 8 && KA <= kTileK - 8, "key split");
+  const Ctl c = make_ctl();
+  const Geom g = make_geom<kSplit>(fa);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t tmem = cta_setup(c, g, 256, &map_q, &map_k, &map_v);
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kW20LowRegs));
+    if (warp == 0) {
+      if (lane == 0) run_producer(c, g, fa, &map_q, &map_k, &map_v, err);
+    } else if (warp < 3) {
+      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false>(c, g, tmem, warp - 1, err);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));
+    const int sw = warp - 4;             // 0..15
+    const int t = sw >> 3;               // query tile
+    const int role = (sw >> 2) & 1;      // 0: MUFU keys [0, KA); 1: FMA keys [KA, 128)
+    const int quad = warp & 3;           // TMEM lane quadrant
+    const int r = quad * 32 + lane;      // row of the query tile
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + col_s(t);
+    const uint32_t tP = tmem + lane_off + col_p(t);
+    const uint32_t tO = tmem + lane_off + col_o(t);
+    const uint64_t sc2 = f32x2_pack(fa.scale_log2, fa.scale_log2);
+    // Partial row sums of the two key ranges: [tile][role][row].
+    float* red = reinterpret_cast<float*>(c.smem + FlashSmem::kRed);
+    if (t < g.nq) {
+      float l = 0.f;
+      bool ok = role == 0 ? ks_steps<0, KA, false>(c, g, t, tS, tP, sc2, l, err)
+                          : ks_steps<KA, kTileK - KA, true>(c, g, t, tS, tP, sc2, l, err);
+      bool fin = ok && mbar_wait(c.o_final(t), 0, c.abort_flag(), err, kDevTimeoutConsumer);
+      fin = __all_sync(0xffffffffu, fin);
+      // The row sum: this thread's keys plus the other warp's (every thread of the
+      // tile's 8 warps reaches the barrier; each wait above is bounded).
+      red[(t * 2 + role) * kTileQ + r] = l;
+      named_bar_sync(1 + t, 256);
+      l += red[(t * 2 + (role ^ 1)) * kTileQ + r];
+      float o[32];  // O columns [32 * role, 32 * role + 32) of this row, unnormalised
+      if (fin) {
+        tc_fence_after();
+        tmem_ld32(tO + 32 * role, o);
+      }
+      const float mrow = 0.f;  // reference exponent of this row (0: fixed offset)
+      const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{0, 0, 1, 0};
+      if (kSplit && sp.nsplit > 1) {
+        // Split tail: publish this key range's partial rows, count the arrival, and
+        // let the CTA that arrives last merge every split (as in the w20 layout).
+        const int slot = (sp.tail_unit * sp.nsplit + sp.split) * 2 + t;
+        if (fin) {
+          float4* po = reinterpret_cast<float4*>(fa.part_o + (static_cast<size_t>(slot) * kTileQ + r) * kHeadDim +
+                                                 32 * role);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) po[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          if (role == 0)
+            reinterpret_cast<float2*>(fa.part_ml + static_cast<size_t>(slot) * kTileQ * 2)[r] = make_float2(mrow, l);
+        }
+        __threadfence();
+        named_bar_sync(1 + t, 256);
+        if (sw == 8 * t && lane == 0) {
+          const int old = atomicAdd(fa.counters + sp.tail_unit * 2 + t, 1);
+          const bool last = old == sp.nsplit - 1;
+          if (last) atomicExch(fa.counters + sp.tail_unit * 2 + t, 0);  // ready for the next launch
+          *c.merge_flag(t) = last ? 1 : 0;
+        }
+        named_bar_sync(1 + t, 256);
+        if (*c.merge_flag(t) == 0) {
+          fin = false;  // another split's CTA merges this tile
+        } else if (fin) {
+          __threadfence();
+          float mx = -INFINITY;
+          for (int s = 0; s < sp.nsplit; ++s) {
+            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+            mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r).x);
+          }
+          l = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          for (int s = 0; s < sp.nsplit; ++s) {
+            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+            const float2 a = __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r);
+            const float w = ex2(a.x - mx);
+            l += w * a.y;
+            const float4* po = reinterpret_cast<const float4*>(
+                fa.part_o + (static_cast<size_t>(sl) * kTileQ + r) * kHeadDim + 32 * role);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 u = __ldcg(po + q);
+              o[4 * q] += w * u.x;
+              o[4 * q + 1] += w * u.y;
+              o[4 * q + 2] += w * u.z;
+              o[4 * q + 3] += w * u.w;
+            }
+          }
+        }
+      }
+      const int token = g.q0 + t * kTileQ + r;  // row of the local Q / O buffers
+      if (fin && token < g.q_end) {
+        const float inv = 1.0f / l;
+        if (fa.out_mode == 0) {
+          uint4* d = reinterpret_cast<uint4*>(fa.o_tok + static_cast<size_t>(token) * fa.embed + g.col + 32 * role);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            d[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
+                              pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                              pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                              pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+        } else {
+          float4* d = reinterpret_cast<float4*>(
+              fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim + 32 * role);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            d[q] = make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv, o[4 * q + 3] * inv);
+        }
+      }
+    }
+  }
+  cta_teardown(c, tmem);
+}
+
 }  // namespace
 
 cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
@@ -1111,13 +1339,25 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
        flash_fwd_d64_w20_kernel<2, false, false, true>},
       {flash_fwd_d64_w20_kernel<0, false, true, true>, flash_fwd_d64_w20_kernel<1, false, true, true>,
        flash_fwd_d64_w20_kernel<2, false, true, true>}};
+  // form 9: key split (fixed exponent offset only), KA = 64 + 8 * poly MUFU keys.
+  static const Kern ks[5][2] = {
+      {flash_fwd_d64_ks_kernel<64, false>, flash_fwd_d64_ks_kernel<64, true>},
+      {flash_fwd_d64_ks_kernel<72, false>, flash_fwd_d64_ks_kernel<72, true>},
+      {flash_fwd_d64_ks_kernel<80, false>, flash_fwd_d64_ks_kernel<80, true>},
+      {flash_fwd_d64_ks_kernel<88, false>, flash_fwd_d64_ks_kernel<88, true>},
+      {flash_fwd_d64_ks_kernel<96, false>, flash_fwd_d64_ks_kernel<96, true>}};
   Kern kern;
   int threads = kRowsThreads;
   bool w20_kernel = false, no_split = false;
+  if (fa.poly_per8 < 0) fa.poly_per8 = fa.fixed_offset && !fa.v_f16 ? kDefaultKeySplit : kDefaultPolyPer8;
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (fa.poly_per8 < 0 || poly > 2 || form > 8 || (form == 8 && poly != 0)) return cudaErrorInvalidValue;
-    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7 || form == 8;
+    if (form == 9) {
+      if (poly > 4 || !fa.fixed_offset) return cudaErrorInvalidValue;
+    } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
+      return cudaErrorInvalidValue;
+    }
+    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7 || form == 8 || form == 9;
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
@@ -1162,7 +1402,8 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = form == 8      ? w20_half[fa.splits > 1]
+      kern = form == 9      ? ks[poly][fa.splits > 1]
+             : form == 8    ? w20_half[fa.splits > 1]
              : form == 7    ? w20_sp[fa.splits > 1][poly]
              : fa.splits > 1 ? w20[form == 5][poly]
              : form == 5     ? w20[1][poly]

@@ -86,6 +86,9 @@ struct PatchEpilogueArgs {
 // Default softmax variant (poly + 8 * form): form 3 (four threads per row, 20
 // warps), every exponential on MUFU.
 constexpr int kDefaultPolyPer8 = 24;
+// Default for launches with the fixed exponent offset: form 9 (key split between
+// MUFU and FMA-pipe warps), KA = 64 + 8 * (variant & 7) keys on MUFU.
+constexpr int kDefaultKeySplit = 9 * 8 + 1;
 // Q is [q_count][E] token-major (this rank's queries, the first of which is row
 // q_offset of the key window); K and V are [kv_rows][E] token-major.
 // seg_len == 0: global attention, every query sees all kv_rows keys.
@@ -103,7 +106,9 @@ struct FlashArgs {
   float* o_hnd;
   int embed;
   int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
-  int poly_per8 = kDefaultPolyPer8;  // bf16 path: variant = poly + 8 * form (see launch_flash)
+  // bf16 path: variant = poly + 8 * form (see launch_flash); < 0: the library default
+  // (kDefaultKeySplit with fixed_offset, else kDefaultPolyPer8)
+  int poly_per8 = -1;
   // 1: exponents relative to 0 instead of the running row max (w20 kernel, bf16 P;
   // other forms ignore it).  Only for inputs with |q.k| * scale * log2(e) <= 64.
   int fixed_offset = 0;
