@@ -114,12 +114,13 @@ def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, se
     assert_close(got, ref, what=f"flash variant {variant} h{heads} n{seg}x{segs}")
 
 
-@pytest.mark.parametrize("variant", [511, 256 + 72, 256 + 73, 256 + 74, 256 + 75, 256 + 76])
+@pytest.mark.parametrize("variant", [511] + [256 + 8 * form + i for form in (9, 10, 11, 12) for i in range(5)])
 @pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 129, 1), (2, 300, 1), (12, 866, 1), (4, 865, 3),
                                             (12, 1732, 1), (12, 10392, 1)])
 def test_flash_key_split_matches_oracle_core(ctx, oracle_mod, heads, seg, segs, variant):
-    # The key-split softmax (variant 72 + i: 64 + 8 i keys of every 128 on MUFU, the
-    # rest on the FMA pipe; 511 = the library default with the fixed exponent offset)
+    # The key-split softmax (variant 72 + i / 80 + i: 64 + 8 i keys of every 128 on
+    # MUFU, the rest on the FMA pipe by a cubic / quadratic exp2; 511 = the library
+    # default with the fixed exponent offset)
     # with the fixed exponent offset, which bounded scores allow: LayerNormed q and k
     # rows, as the QK-norm leaves them, so |q.k| / 8 * log2(e) <= 11.6.  Local
     # segments (865 x 3) end inside a key tile whose other rows are the next

@@ -1076,16 +1076,32 @@ __global__ void __launch_bounds__(kW20Threads, 1)
 // more).  Every thread keeps the partial row sum of its keys; the two halves meet
 // in shared memory after the last step.
 
+// Quadratic for 2^f on [-0.5, 0.5], fitted here like the cubic of exp2_fma_x2
+// (Lawson-reweighted least squares in relative error on 4001 Chebyshev nodes):
+// relative error < 1.73e-3 in F32, below the 1.95e-3 half-ulp of the bf16 the
+// probabilities are rounded to for the PV product.
+constexpr float kExp2Q0 = 0x1.001d0ap+0f;
+constexpr float kExp2Q1 = 0x1.682a56p-1f;
+constexpr float kExp2Q2 = 0x1.e84d6ap-3f;
+
 // p = 2^x for a pair x = s * c on the FMA pipe; valid for |x| <= 2^22 (the
-// fixed-offset launches keep |x| <= 64).  Returns the pair as packed F32.
+// fixed-offset launches keep |x| <= 64).  kQuad: the quadratic above instead of
+// the cubic.  Returns the pair as packed F32.
+template <bool kQuad>
 __device__ __forceinline__ uint64_t exp2_fma_pair(uint64_t s2, uint64_t c2) {
   const uint64_t magic = f32x2_pack(12582912.0f, 12582912.0f);  // 1.5 * 2^23
   const uint64_t t = f32x2_fma(s2, c2, magic);   // low mantissa bits: n = round(x)
   const uint64_t nn = f32x2_sub(magic, t);        // -n
   const uint64_t f = f32x2_fma(s2, c2, nn);       // x - n
-  uint64_t p = f32x2_fma(f32x2_pack(kExp2C3, kExp2C3), f, f32x2_pack(kExp2C2, kExp2C2));
-  p = f32x2_fma(p, f, f32x2_pack(kExp2C1, kExp2C1));
-  p = f32x2_fma(p, f, f32x2_pack(kExp2C0, kExp2C0));
+  uint64_t p;
+  if constexpr (kQuad) {
+    p = f32x2_fma(f32x2_pack(kExp2Q2, kExp2Q2), f, f32x2_pack(kExp2Q1, kExp2Q1));
+    p = f32x2_fma(p, f, f32x2_pack(kExp2Q0, kExp2Q0));
+  } else {
+    p = f32x2_fma(f32x2_pack(kExp2C3, kExp2C3), f, f32x2_pack(kExp2C2, kExp2C2));
+    p = f32x2_fma(p, f, f32x2_pack(kExp2C1, kExp2C1));
+    p = f32x2_fma(p, f, f32x2_pack(kExp2C0, kExp2C0));
+  }
   float p0, p1, t0, t1;
   f32x2_unpack(p, p0, p1);
   f32x2_unpack(t, t0, t1);
@@ -1095,7 +1111,11 @@ __device__ __forceinline__ uint64_t exp2_fma_pair(uint64_t s2, uint64_t c2) {
 
 // One softmax thread's steps over keys [K0, K0 + NK) of its row of query tile t.
 // Returns false when a wait timed out or the CTA aborted.
-template <int K0, int NK, bool kFma>
+// kTurns: the two query tiles take turns in the exponential section (tile 0 of
+// step j, tile 1 of step j, tile 0 of step j + 1, ...), so each tile's softmax has
+// MUFU and the issue slots of the sub-partition to itself while the other tile
+// waits for its UMMAs, P store and next S.
+template <int K0, int NK, bool kFma, bool kQuad, bool kTurns>
 __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uint32_t tS, uint32_t tP,
                                          uint64_t sc2, float& l, int* err) {
   volatile int* abort_flag = c.abort_flag();
@@ -1108,6 +1128,12 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
     tmem_ld_cols<NK>(tS + K0, s);
     tc_fence_before();
     mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
+    if (kTurns && g.nq == 2 && (t == 1 || j > 0)) {
+      ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
+                     kDevTimeoutConsumer);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) return false;
+    }
     uint32_t pk[NK / 2];
     uint64_t acc[2];
     // Keys at or past `valid` (the range's last tile) get probability 0.  Their
@@ -1121,7 +1147,7 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
         const uint64_t s2 = f32x2_pack(s[2 * i], s[2 * i + 1]);
         float p0, p1;
         if constexpr (kFma) {
-          f32x2_unpack(exp2_fma_pair(s2, sc2), p0, p1);
+          f32x2_unpack(exp2_fma_pair<kQuad>(s2, sc2), p0, p1);
         } else {
           float x0, x1;
           f32x2_unpack(f32x2_mul(s2, sc2), x0, x1);
@@ -1141,6 +1167,7 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
       body(std::true_type{});
     else
       body(std::false_type{});
+    if (kTurns && g.nq == 2) mbar_arrive(c.ex_done(t));
     if (j > 0) {
       // PV_t(j-1) has finished reading P_t.
       ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
@@ -1160,7 +1187,7 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
   return true;
 }
 
-template <int KA, bool kSplit>
+template <int KA, bool kSplit, bool kQuad, bool kTurns>
 __global__ void __launch_bounds__(kW20Threads, 1)
     flash_fwd_d64_ks_kernel(const __grid_constant__ CUtensorMap map_q,
                             const __grid_constant__ CUtensorMap map_k,
@@ -1195,8 +1222,8 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     float* red = reinterpret_cast<float*>(c.smem + FlashSmem::kRed);
     if (t < g.nq) {
       float l = 0.f;
-      bool ok = role == 0 ? ks_steps<0, KA, false>(c, g, t, tS, tP, sc2, l, err)
-                          : ks_steps<KA, kTileK - KA, true>(c, g, t, tS, tP, sc2, l, err);
+      bool ok = role == 0 ? ks_steps<0, KA, false, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err)
+                          : ks_steps<KA, kTileK - KA, true, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err);
       bool fin = ok && mbar_wait(c.o_final(t), 0, c.abort_flag(), err, kDevTimeoutConsumer);
       fin = __all_sync(0xffffffffu, fin);
       // The row sum: this thread's keys plus the other warp's (every thread of the
@@ -1339,25 +1366,27 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
        flash_fwd_d64_w20_kernel<2, false, false, true>},
       {flash_fwd_d64_w20_kernel<0, false, true, true>, flash_fwd_d64_w20_kernel<1, false, true, true>,
        flash_fwd_d64_w20_kernel<2, false, true, true>}};
-  // form 9: key split (fixed exponent offset only), KA = 64 + 8 * poly MUFU keys.
-  static const Kern ks[5][2] = {
-      {flash_fwd_d64_ks_kernel<64, false>, flash_fwd_d64_ks_kernel<64, true>},
-      {flash_fwd_d64_ks_kernel<72, false>, flash_fwd_d64_ks_kernel<72, true>},
-      {flash_fwd_d64_ks_kernel<80, false>, flash_fwd_d64_ks_kernel<80, true>},
-      {flash_fwd_d64_ks_kernel<88, false>, flash_fwd_d64_ks_kernel<88, true>},
-      {flash_fwd_d64_ks_kernel<96, false>, flash_fwd_d64_ks_kernel<96, true>}};
+  // form 9..12: key split (fixed exponent offset only), KA = 64 + 8 * poly MUFU
+  // keys; the FMA-pipe exp2 by the cubic (9, 11) or the quadratic (10, 12); in
+  // forms 11 and 12 the two query tiles take turns in the exponential section.
+#define VA_KS(KA, Q, T) {flash_fwd_d64_ks_kernel<KA, false, Q, T>, flash_fwd_d64_ks_kernel<KA, true, Q, T>}
+#define VA_KS_FORM(Q, T) {VA_KS(64, Q, T), VA_KS(72, Q, T), VA_KS(80, Q, T), VA_KS(88, Q, T), VA_KS(96, Q, T)}
+  static const Kern ks[4][5][2] = {VA_KS_FORM(false, false), VA_KS_FORM(true, false), VA_KS_FORM(false, true),
+                                   VA_KS_FORM(true, true)};
+#undef VA_KS_FORM
+#undef VA_KS
   Kern kern;
   int threads = kRowsThreads;
   bool w20_kernel = false, no_split = false;
   if (fa.poly_per8 < 0) fa.poly_per8 = fa.fixed_offset && !fa.v_f16 ? kDefaultKeySplit : kDefaultPolyPer8;
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (form == 9) {
+    if (form >= 9 && form <= 12) {
       if (poly > 4 || !fa.fixed_offset) return cudaErrorInvalidValue;
     } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
       return cudaErrorInvalidValue;
     }
-    w20_kernel = form == 3 || form == 5 || form == 6 || form == 7 || form == 8 || form == 9;
+    w20_kernel = form == 3 || (form >= 5 && form <= 12);
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
@@ -1402,7 +1431,7 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = form == 9      ? ks[poly][fa.splits > 1]
+      kern = form >= 9      ? ks[form - 9][poly][fa.splits > 1]
              : form == 8    ? w20_half[fa.splits > 1]
              : form == 7    ? w20_sp[fa.splits > 1][poly]
              : fa.splits > 1 ? w20[form == 5][poly]

@@ -86,9 +86,10 @@ struct PatchEpilogueArgs {
 // Default softmax variant (poly + 8 * form): form 3 (four threads per row, 20
 // warps), every exponential on MUFU.
 constexpr int kDefaultPolyPer8 = 24;
-// Default for launches with the fixed exponent offset: form 9 (key split between
-// MUFU and FMA-pipe warps), KA = 64 + 8 * (variant & 7) keys on MUFU.
-constexpr int kDefaultKeySplit = 9 * 8 + 1;
+// Default for launches with the fixed exponent offset: form 10 (key split between
+// MUFU and FMA-pipe warps, quadratic exp2 on the FMA pipe), KA = 64 + 8 * 1 = 72
+// keys of every 128 on MUFU (the fastest split measured at S=12).
+constexpr int kDefaultKeySplit = 10 * 8 + 1;
 // Q is [q_count][E] token-major (this rank's queries, the first of which is row
 // q_offset of the key window); K and V are [kv_rows][E] token-major.
 // seg_len == 0: global attention, every query sees all kv_rows keys.
