@@ -41,11 +41,15 @@ import synthetic as syn  # noqa: E402
 
 LAYER = 5           # a global block of the DA3-BASE schedule (alt_start 4: globals 5,7,9,11)
 L2_FLUSH_BYTES = 256 << 20
-# dram__bytes_read.sum + dram__bytes_write.sum of one flash launch on cfg3 (47.94 MB
-# + 2.98 MB), from the ncu capture summarised in
-# profiles/flash_fwd_d64_fixed_offset_cfg3.md; used for the roofline's `traffic`
-# when the bench runs that workload.
-FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.92e6}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the default
+# fixed-offset attention kernel (flash_fwd_d64_ks_kernel<72, split, quadratic>) on
+# the cfg3 window at one GPU, from one ncu capture of that kernel (47.97 MB read:
+# Q + K + V once; 2.65 MB written, O mostly still in L2 when the launch ends).  Used
+# for the roofline's `traffic` at N = 1; a rank's launch at N > 1 reads the whole
+# key window but only its own queries, so the figure does not carry over.
+FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.62e6}
+PARITY_ROWS = 256   # seeded output rows checked against the oracle at every N
+MAX_ABS, MIN_COS = 2e-2, 0.9999
 
 
 def parse_args():
@@ -55,12 +59,20 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="cfg3_s12_global", choices=sorted(syn.CONFIGS))
-    ap.add_argument("--cpu-seconds", type=float, default=12.0,
-                    help="bound on the CPU-baseline sample (seconds of CPU work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--variants", action="store_true",
                     help="also time the attention kernel's exponential-split and f16-P variants")
+    ap.add_argument("--no-large", action="store_true", help="skip the DA3-LARGE S=32 window section")
     return ap.parse_args()
+
+
+def cpu_threads():
+    """Host threads this process may run on (the oracle is given this count
+    explicitly, so a launcher's OMP_NUM_THREADS=1 does not apply)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def dist_env():
@@ -147,69 +159,27 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def cpu_attention_sample(wl, seconds_budget, threads=0):
-    """Times the CPU F32 restatement (oracle/) of the attention sub-block on a
-    bounded sample of the workload; returns (TFLOP/s, cores, sample description)."""
+def cpu_attention_full(wl, reps, threads, warmup=1):
+    """Times the CPU F32 restatement (oracle/) of the attention sub-block over the
+    whole window (every query row, no extrapolation) on `threads` host threads;
+    returns the per-run seconds."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import numpy as np
     import oracle
+    import vestra_attn as va
 
     oracle.build()
     x = syn.hidden_states(wl.rows, wl.embed, seed=0)
     p = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
-    pos = None
-    try:
-        import vestra_attn as va
-        pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
-    except Exception:
-        pass
-    seg = wl.seg_len
-    cores = threads or os.cpu_count() or 1
-    # Probe with a small row subset to size the sample.
-    probe_rows = np.sort(np.random.default_rng(1).choice(wl.rows, min(wl.rows, 256), replace=False))
-    t = time.perf_counter()
-    oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg if not wl.global_ else 0,
-                           q_rows=probe_rows, threads=threads)
-    t_probe = time.perf_counter() - t
-    # Per query row the attention costs 4*seg*64*heads FLOPs; K/V projection is fixed.
-    per_row = max(t_probe / len(probe_rows), 1e-9)
-    nq = int(min(wl.rows, max(256, seconds_budget / 3 / per_row)))
-    if nq >= wl.rows:
-        q_rows, sample = None, f"full window ({wl.rows} query rows), median of 3"
-        nq = wl.rows
-    else:
-        q_rows = np.sort(np.random.default_rng(2).choice(wl.rows, nq, replace=False)).astype(np.int64)
-        sample = f"{nq} of {wl.rows} query rows (seeded), all K/V rows projected, median of 3"
+    pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
+    seg = 0 if wl.global_ else wl.seg_len
+    for _ in range(warmup):
+        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, threads=threads)
     times = []
-    for _ in range(3):
+    for _ in range(reps):
         t = time.perf_counter()
-        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg if not wl.global_ else 0,
-                               q_rows=q_rows, threads=threads)
+        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, threads=threads)
         times.append(time.perf_counter() - t)
-    t_fixed = cpu_fixed_part(oracle, x, p, wl, pos, threads)
-    t_full = cpu_full_window_time(statistics.median(times), t_fixed, nq, wl.rows)
-    sample += f"; full-window time estimated as fixed {t_fixed:.3f} s + (sample - fixed) x {wl.rows}/{nq}"
-    return wl.attention_flops() / t_full / 1e12, cores, sample
-
-
-def cpu_fixed_part(oracle, x, p, wl, pos, threads=0):
-    """Seconds of the part of a CPU sub-block that does not grow with the query rows
-    (LN-cast and K/V projection of every row of the window), median of 3."""
-    import numpy as np
-    few = np.arange(0, wl.rows, max(1, wl.rows // 8), dtype=np.int64)[:8]
-    ts = []
-    for _ in range(3):
-        t = time.perf_counter()
-        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=wl.seg_len if not wl.global_ else 0,
-                               q_rows=few, threads=threads)
-        ts.append(time.perf_counter() - t)
-    return statistics.median(ts)
-
-
-def cpu_full_window_time(t_sample, t_fixed, nq, rows):
-    """CPU time of the full window from a sample of nq query rows: the fixed part once
-    plus the per-query part scaled to all rows (rows are independent)."""
-    return t_fixed + max(t_sample - t_fixed, 0.0) * rows / nq
+    return times
 
 
 def run_reference(args):
@@ -217,52 +187,25 @@ def run_reference(args):
     if rank != 0:
         return 0
     wl = syn.CONFIGS[args.workload]
-    import numpy as np
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-
-    oracle.build()
-    x = syn.hidden_states(wl.rows, wl.embed, seed=0)
-    p = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
-    import vestra_attn as va
-    pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
-    seg = wl.seg_len if not wl.global_ else 0
-    cores = os.cpu_count() or 1
-    # Size each step to at most ~3 s of CPU work (the whole run stays within minutes).
-    probe = np.sort(np.random.default_rng(1).choice(wl.rows, min(wl.rows, 256), replace=False))
-    t = time.perf_counter()
-    oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=probe)
-    per_row = (time.perf_counter() - t) / len(probe)
-    nq = int(min(wl.rows, max(256, 3.0 / max(per_row, 1e-9))))
-    q_rows = None if nq >= wl.rows else np.sort(
-        np.random.default_rng(2).choice(wl.rows, nq, replace=False)).astype(np.int64)
-    nq = wl.rows if q_rows is None else nq
-    for _ in range(args.warmup):
-        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=q_rows)
-    times = []
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        oracle.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=seg, q_rows=q_rows)
-        times.append(time.perf_counter() - t)
+    threads = cpu_threads()
+    # Every step is the whole window: each query row, the full K/V projection, the
+    # output projection, on all host threads (about half a second at cfg3).
+    times = cpu_attention_full(wl, args.steps, threads, warmup=args.warmup)
     total = sum(times)
-    t_fixed = cpu_fixed_part(oracle, x, p, wl, pos)
-    t_full = cpu_full_window_time(total / args.steps, t_fixed, nq, wl.rows)
-    value = wl.attention_flops() / t_full / 1e12
-    sample = ("full window" if q_rows is None else f"{nq} of {wl.rows} query rows (seeded)") + \
-        f", all K/V rows projected, per step; full-window time estimated as fixed {t_fixed:.3f} s + " \
-        f"(step - fixed) x {wl.rows}/{nq}"
+    value = wl.attention_flops() / (total / args.steps) / 1e12
+    sample = f"the full window ({wl.rows} query rows) every step, {threads} threads"
     line = {
         "impl": "reference", "metric": "global-attention TFLOP/s", "value": round(value, 4),
         "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t_full * 1e3, 3), "sample_ms_per_step": round(total / args.steps * 1e3, 3),
+        "ms_per_step": round(total / args.steps * 1e3, 3),
         "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights)",
-        "config": workload_config(wl, 1),
-        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+        "config": workload_config(wl, args.gpus),
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample, "cpu": cpu_info()},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "CPU F32 restatement of the reference attention (vestra-kernels is un-vendored and no Rust "
-                "toolchain exists, so the reference binary cannot be built)",
+                "toolchain exists, so the reference binary cannot be built); rank 0 alone runs it",
     }
     print(json.dumps(line), file=JSON_OUT, flush=True)
     return 0
@@ -276,8 +219,129 @@ def workload_config(wl, n_gpus):
         "flops_per_step": wl.attention_flops(),
         "l2": f"flushed between timed steps ({L2_FLUSH_BYTES >> 20} MiB write)",
         "parallelism": "single GPU" if n_gpus == 1 else
-        f"query-sharded window over {n_gpus} GPUs, K/V all-gather (NCCL)",
+        f"query-sharded window over {n_gpus} GPUs; K'/V rows exchanged directly over NVLink (copy-engine "
+        "push with per-peer flags, or QKV-epilogue peer stores), NCCL all-gather as the fallback",
     }
+
+
+# --------------------------------------------------------------------------- parity
+def parity_rows(rows, n, seed):
+    """Seeded sorted sample of n window rows (every row when the window is smaller)."""
+    import numpy as np
+    if n >= rows:
+        return np.arange(rows, dtype=np.int64)
+    return np.sort(np.random.default_rng(seed).choice(rows, n, replace=False)).astype(np.int64)
+
+
+def parity_check(wl, p, x_all, out_local, row0, sel, world, rank, seg_len=0):
+    """Compares a seeded sample of output rows, gathered from every rank, with the
+    oracle (CPU F32 restatement) on rank 0.  Collective; returns the same dict on
+    every rank: {rows, max_abs, cos, ok}."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    local = out_local.shape[0]
+    mine = sel[(sel >= row0) & (sel < row0 + local)]
+    got = out_local[torch.from_numpy(mine - row0).to(out_local.device)].float().cpu().numpy()
+    parts = [(mine, got)]
+    if world > 1:
+        parts = [None] * world
+        dist.all_gather_object(parts, (mine, got))
+    res = None
+    if rank == 0:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        import vestra_attn as va
+
+        oracle.build()
+        idx = np.concatenate([a for a, _ in parts])
+        val = np.concatenate([b for _, b in parts])
+        order = np.argsort(idx)
+        idx, val = idx[order], val[order]
+        pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
+        ref = oracle.attention_block(x_all, p, wl.heads, pos_yx=pos, seg_len=seg_len, q_rows=idx,
+                                     threads=cpu_threads())
+        a, b = val.astype(np.float64), ref.astype(np.float64)
+        err = float(np.abs(a - b).max()) if np.isfinite(a).all() else float("inf")
+        cos = float((a.ravel() @ b.ravel()) / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+        res = {"rows": int(len(idx)), "max_abs": err, "cos": round(cos, 8),
+               "ok": bool(len(idx) == len(sel) and err <= MAX_ABS and cos >= MIN_COS)}
+    if world > 1:
+        box = [res]
+        dist.broadcast_object_list(box, src=0)
+        res = box[0]
+    return res
+
+
+# --------------------------------------------------------------------------- cfg5
+def run_large(args, world, rank, local_rank, barrier, max_over_ranks, flush_buf, stream):
+    """The DA3-LARGE S=32 window (E=1024, 16 heads, 110,656 tokens): one global
+    attention sub-block, query-sharded over the run's GPUs with the same exchange as
+    the metric's window, timed with CUDA events (max over ranks), and an oracle
+    check of a seeded row sample."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import vestra_attn as va
+
+    wl = syn.CONFIGS["cfg5_large_s32_global"]
+    row0, local = va.shard_rows(wl.rows, world, rank)
+    cfg = va.default_config(embed_dim=wl.embed, num_heads=wl.heads, num_register=wl.n_special - 1,
+                            max_rows=wl.rows, depth=24, rope_start=4, qknorm_start=4)
+    ctx = va.Context(cfg, local_rank)
+    p = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
+    ctx.load_layer(LAYER, p)
+    if world > 1:
+        obj = [va.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.comm_init(obj[0], world, rank)
+    x_all = syn.hidden_states(wl.rows, wl.embed, seed=0)
+    ln1 = torch.from_numpy(np.ascontiguousarray(x_all[row0:row0 + local])).cuda()
+    out = torch.empty_like(ln1)
+    sp = stream.cuda_stream
+
+    def step():
+        if world == 1:
+            ctx.attention_device(LAYER, ln1, out, wl.gh, wl.gw, wl.views, True, stream=sp)
+        else:
+            ctx.attention_device_sharded(LAYER, ln1, out, wl.gh, wl.gw, wl.views, True, stream=sp)
+
+    for _ in range(2):
+        step()
+    barrier()
+    ctx.check_device()
+    evs = []
+    for _ in range(3):
+        flush_buf.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        evs.append((a, b))
+    barrier()
+    ctx.check_device()
+    ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in evs))
+    ctx.set_phase_profile(True)
+    flush_buf.zero_()
+    step()
+    core = ctx.phase_times()["core"]
+    ctx.set_phase_profile(False)
+    barrier()
+    flops = wl.attention_flops()
+    peak, _, kind = load_peaks()
+    my_flops = 4.0 * local * wl.rows * 64 * wl.heads
+    par = parity_check(wl, p, x_all, out, row0, parity_rows(wl.rows, 64, 9), world, rank)
+    ctx.close()
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": wl.name, "window_tokens": wl.rows, "embed": wl.embed, "heads": wl.heads,
+            "attention_flops": flops, "ms": round(ms, 3), "tflops": round(tf, 1),
+            "frac_of_n_peaks": round(tf / (world * peak), 4),
+            "core_ms_rank0": round(core, 3), "kernel_tflops_rank0": round(my_flops / (core * 1e-3) / 1e12, 1),
+            "parity": par,
+            "what": "one global attention sub-block of the S=32 DA3-LARGE window (LN1 out -> QKV -> attention "
+                    f"-> proj), query-sharded over {world} GPU(s); frac against {world} x the measured bf16 "
+                    f"peak ({kind})"}
 
 
 # --------------------------------------------------------------------------- ours
@@ -362,11 +426,14 @@ def run_ours(args):
     # ---- per-phase times of the same step (CUDA events between its launches),
     # the reference's phase names; outside the timed region above.
     ctx.set_phase_profile(True)
-    phase_runs = []
+    phase_runs, xchg_runs = [], []
+    mode = ctx.exchange_mode() if world > 1 else "single GPU"
     for _ in range(max(3, min(args.steps, 10))):
         flush_buf.zero_()
         step()
         phase_runs.append(ctx.phase_times())
+        if mode == "direct-ce":
+            xchg_runs.append(ctx.exchange_times())
     ctx.set_phase_profile(False)
     barrier()
     phases = {k: round(statistics.median(r[k] for r in phase_runs), 4) for k in phase_runs[0]}
@@ -376,6 +443,30 @@ def run_ours(args):
         "proj": round(2.0 * local_rows * wl.embed * wl.embed / (phases["proj"] * 1e-3) / 1e12, 1),
     }
     ln_gbs = round(local_rows * wl.embed * 6 / (phases["ln"] * 1e-3) / 1e9, 1)  # F32 read + bf16 write
+    exchange = None
+    if world > 1:
+        exchange = {"mode": mode}
+        if xchg_runs:
+            npeer = len(xchg_runs[0][0])
+            per_peer = [statistics.median(r[0][i] for r in xchg_runs) for i in range(npeer)]
+            nbytes = xchg_runs[0][1]
+            exchange.update({
+                "bytes_per_peer": nbytes,
+                "per_peer_ms": [round(v, 4) for v in per_peer],
+                "per_peer_gbs": [round(nbytes / (v * 1e-3) / 1e9, 1) for v in per_peer],
+                "push_ms": round(max(per_peer), 4),
+                "out_gbs": round(nbytes * npeer / (max(per_peer) * 1e-3) / 1e9, 1),
+                "what": "this rank's K'/V rows pushed to every peer by copy engines: CUDA events around each "
+                        "peer's copies and flag writes on its copy stream, median of the profiled steps "
+                        "(rank 0's view); out_gbs = all bytes sent / the slowest peer's push"})
+
+    # ---- parity of this N's output against the oracle: a seeded sample of output
+    # rows gathered from every rank, outside the timed region.  Exits non-zero (after
+    # the line is printed) when the gates fail.
+    p_metric = syn.layer_weights(wl.embed, seed=0, layer=LAYER)
+    parity = parity_check(wl, p_metric, x_all, out, row0, parity_rows(wl.rows, PARITY_ROWS, 7), world, rank)
+    parity["gate"] = f"max-abs <= {MAX_ABS}, cos >= {MIN_COS}"
+    parity["vs"] = "oracle (CPU F32 restatement), rows gathered from every rank"
 
     # ---- one whole block (device-resident tail: attention + LN2/MLP, residuals),
     # reported beside the metric; tokens restored from a copy before every run.
@@ -463,6 +554,62 @@ def run_ours(args):
             del graph
     ctx.load_layer(LAYER, syn.layer_weights(wl.embed, seed=0, layer=LAYER))  # back to the metric's weights
 
+    # ---- local blocks (cfg4: the same 12 views, each attending to itself): this
+    # rank's whole views, no communication; the attention kernel's time from the
+    # phase profile.
+    local_section = None
+    n_tok = wl.rows // wl.views
+    if wl.views >= world:
+        v0, vrows = va.shard_views(wl.views, n_tok, world, rank)
+        lv = vrows // n_tok
+        xl = torch.from_numpy(np.ascontiguousarray(x_all[v0:v0 + vrows])).cuda()
+        ol = torch.empty_like(xl)
+
+        def lstep():
+            ctx.attention_device(LAYER, xl, ol, wl.gh, wl.gw, lv, False, stream=sp)
+
+        for _ in range(3):
+            lstep()
+        barrier()
+        lms, lcore = [], []
+        ctx.set_phase_profile(True)
+        for _ in range(max(3, args.steps // 2)):
+            flush_buf.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            lstep()
+            b.record(stream)
+            lms.append((a, b))
+            lcore.append(ctx.phase_times()["core"])
+        ctx.set_phase_profile(False)
+        barrier()
+        ctx.check_device()
+        l_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in lms))
+        l_core = max_over_ranks(statistics.median(lcore))
+        l_flops = 4.0 * wl.views * n_tok * n_tok * 64 * wl.heads
+        my_flops = 4.0 * lv * n_tok * n_tok * 64 * wl.heads
+        peak_t, _, _ = load_peaks()
+        lpar = parity_check(wl, p_metric, x_all, ol, v0, parity_rows(wl.rows, PARITY_ROWS, 8), world, rank,
+                            seg_len=n_tok)
+        local_section = {
+            "workload": "cfg4 local blocks (12 x 866-token views, block-diagonal attention)",
+            "ms": round(l_ms, 4), "attention_flops": l_flops,
+            "tflops": round(l_flops / (l_ms * 1e-3) / 1e12, 1),
+            "core_ms_rank0": round(statistics.median(lcore), 4),
+            "kernel_tflops_rank0": round(my_flops / (statistics.median(lcore) * 1e-3) / 1e12, 1),
+            "kernel_frac_rank0": round(my_flops / (statistics.median(lcore) * 1e-3) / 1e12 / peak_t, 4),
+            "views_per_rank": [va.shard_views(wl.views, n_tok, world, r)[1] // n_tok for r in range(world)],
+            "parity": lpar,
+            "what": "one local attention sub-block over this rank's whole views (max over ranks); kernel = "
+                    "the attention launch alone (phase profile), rank 0's views"}
+        del xl, ol
+
+    # ---- the DA3-LARGE S=32 window (cfg5: E=1024, 16 heads, 110,656 tokens),
+    # query-sharded over the run's GPUs exactly like the metric's window.
+    large = None
+    if not args.no_large:
+        large = run_large(args, world, rank, local_rank, barrier, max_over_ranks, flush_buf, stream)
+
     # ---- token input side: this rank's views of 504x336 images -> tokens (patch
     # projection GEMM + position/CLS/register assembly), no communication.
     pw = syn.patch_embed_weights(wl.embed, 14, 37, wl.n_special - 1, seed=0)
@@ -508,7 +655,7 @@ def run_ours(args):
     q = head_norm(torch.randn(local, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
     kw = head_norm(torch.randn(wl.rows, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
     vw = (0.5 * torch.randn(wl.rows, wl.embed, device="cuda", generator=g)).to(torch.bfloat16)
-    FIXED = 256 + 24  # fixed exponent offset + the library's default form (see va_flash_attention_bf16)
+    FIXED = 511  # fixed exponent offset with the library's default layout (see va_flash_attention_bf16)
     o = torch.empty(local, wl.embed, device="cuda", dtype=torch.bfloat16)
 
     def time_flash(v_tensor, poly=-1):
@@ -530,6 +677,7 @@ def run_ours(args):
     flash_flops = 4.0 * local * wl.rows * 64 * wl.heads
     flash_ms = time_flash(vw, FIXED)
     rowmax_ms = time_flash(vw)
+    w20_fixed_ms = time_flash(vw, 256 + 24)  # the four-threads-per-row layout with the fixed offset
     variants = {}
     if args.variants:
         to_tf = lambda ms: round(flash_flops / (ms * 1e-3) / 1e12, 2)  # noqa: E731
@@ -542,6 +690,9 @@ def run_ours(args):
             variants[f"w20fixed_poly{p}"] = to_tf(time_flash(vw, 256 + 24 + p))
             variants[f"w20fixed_nosplit_poly{p}"] = to_tf(time_flash(vw, 256 + 48 + p))
         variants["w20half_poly0"] = to_tf(time_flash(vw, 64))
+        for form, name in ((9, "ks_cubic"), (10, "ks_quad"), (11, "ks_cubic_turns"), (12, "ks_quad_turns")):
+            for i in range(5):
+                variants[f"{name}_ka{64 + 8 * i}"] = to_tf(time_flash(vw, 256 + 8 * form + i))
         variants["f16_p"] = to_tf(time_flash(vw.to(torch.float16)))
     peak_tflops, _, peak_kind = load_peaks()
     achieved = flash_flops / (flash_ms * 1e-3) / 1e12
@@ -669,8 +820,11 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_attention_sample(wl, args.cpu_seconds)
-        cpu = {"value": round(v, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample,
+        threads = cpu_threads()
+        times = cpu_attention_full(wl, 3, threads)
+        cpu = {"value": round(wl.attention_flops() / statistics.median(times) / 1e12, 4), "unit": "TFLOP/s",
+               "cores": threads, "kind": "port", "ms_per_step": round(statistics.median(times) * 1e3, 1),
+               "sample": f"the full window ({wl.rows} query rows), median of 3 after one warm-up",
                "cpu": cpu_info()}
 
     if rank == 0:
@@ -682,12 +836,14 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, QK-norm gamma 1 beta 0)",
             "config": workload_config(wl, world),
-            "roofline": {"bound": "tensor", "kernel": "flash_fwd_d64_w20_kernel", "achieved": round(achieved, 2),
+            "roofline": {"bound": "tensor", "kernel": "flash_fwd_d64_ks_kernel", "achieved": round(achieved, 2),
                          "peak": peak_tflops, "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
                          "peak_kind": f"bf16 burst ({peak_kind})", "flops_per_launch": flash_flops,
                          "ms_per_launch": round(flash_ms, 4),
-                         "softmax": "fixed exponent offset (scores bounded by the QK-norm)",
+                         "softmax": "fixed exponent offset (scores bounded by the QK-norm); keys split between "
+                                    "MUFU and FMA-pipe warps (72 of every 128 on MUFU)",
                          "rowmax_tflops": round(flash_flops / (rowmax_ms * 1e-3) / 1e12, 2),
+                         "w20_fixed_tflops": round(flash_flops / (w20_fixed_ms * 1e-3) / 1e12, 2),
                          **({"variants_tflops": variants} if variants else {}),
                          "traffic": FLASH_DRAM_BYTES_PER_LAUNCH.get(args.workload) if world == 1 else None},
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_s / args.steps * 1e3, 4),
@@ -707,7 +863,8 @@ def run_ours(args):
                     "pipelined": pipelined},
             "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
             "gguf": gguf_section,
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": (5 if mode == "direct" else 4) * args.steps,
+            "parity": parity, "exchange": exchange, "local": local_section, "large": large,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
         }
@@ -716,6 +873,11 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    failed = [n for n, sec in (("metric", parity), ("local", (local_section or {}).get("parity")),
+                               ("large", (large or {}).get("parity"))) if sec is not None and not sec["ok"]]
+    if failed:
+        print(f"parity gates failed: {failed}", file=sys.stderr)
+        return 1
     return 0
 
 

@@ -261,11 +261,9 @@ int va_backbone_device_sharded(va_ctx* ctx, float* tokens_local, int64_t local_r
 int va_comm_unique_id(void* id_out);
 /* Collective.  Creates the NCCL communicator, then maps every peer's key/value
  * window into this process (CUDA IPC, up to 8 ranks).  When every rank mapped
- * every peer, K'/V are exchanged directly: the QKV GEMM's epilogue stores each
- * finished K'/V tile into every peer's window over NVLink and a one-warp barrier
- * kernel (release/acquire flags at system scope, bounded wait) closes the step.
- * Otherwise, or with VA_KV_EXCHANGE=nccl in every rank's environment, an in-place
- * NCCL all-gather assembles the window. */
+ * every peer, K'/V are exchanged directly (see va_comm_exchange_mode); otherwise,
+ * or with VA_KV_EXCHANGE=nccl in every rank's environment, an in-place NCCL
+ * all-gather assembles the window. */
 int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
 /* va_attention_device_sharded with host buffers (pinned for overlap): this rank's
  * ln1_local / out_local F32 [local_rows, E].  The rows are copied in chunks on a
@@ -273,12 +271,16 @@ int va_comm_init(va_ctx* ctx, const void* id, int nranks, int rank);
  * copied back chunk by chunk while later attention chunks compute.  Collective. */
 int va_attention_host_sharded(va_ctx* ctx, int layer, const float* ln1_local, float* out_local,
                               int64_t local_rows, int gh, int gw, int view_count, int global);
-/* 0: no communicator, 1: NCCL all-gather, 2: direct peer stores from the QKV
- * epilogue + barrier kernel, 3: direct, pushed by copy engines (one stream per peer,
- * then a stream memory write of the call's epoch into the peer's flag array); the
- * attention kernel starts on the rank's own key tiles and waits (bounded) for the
- * peers' flags before the first tile that is not its own.  VA_KV_EXCHANGE=nccl or
- * =sm at va_comm_init force modes 1 or 2. */
+/* 0: no communicator, 1: NCCL all-gather, 2: direct, the QKV epilogue stores each
+ * finished K'/V tile into every peer's window over NVLink, then a one-warp kernel
+ * raises this rank's flag in every peer (system-scope release, no wait), 3: direct,
+ * pushed by copy engines in VA_PUSH_CHUNKS chunks per peer (default 2), each chunk
+ * followed by a stream memory write of this rank's flag in that peer (one copy
+ * stream per peer, or with VA_PUSH_ORDER=stagger one stream serving rank - 1 first).
+ * A flag holds the call's epoch and how far this rank's rows have arrived.  In modes
+ * 2 and 3 the attention kernel starts on the rank's own key tiles and, before each
+ * later tile, waits (bounded) only until the rows of that tile are in place.
+ * VA_KV_EXCHANGE=nccl or =sm at va_comm_init force modes 1 or 2. */
 int va_comm_exchange_mode(const va_ctx* ctx);
 /* ln1_local/out_local: device F32 [local_rows, E], this rank's rows
  * [rank*local_rows, (rank+1)*local_rows) of a window of nranks*local_rows tokens
@@ -342,6 +344,13 @@ int va_check_device(va_ctx* ctx);
  * synchronisation to the call; va_phase_times waits for the last event. */
 int va_set_phase_profile(va_ctx* ctx, int enable);
 int va_phase_times(va_ctx* ctx, float* ms_out /* [5] */);
+/* With the phase profile enabled: the copy-engine K'/V push of the last profiled
+ * sharded call, per peer (no reference counterpart; the reference has no
+ * multi-GPU path): ms_out[p] = time from the first copy to this peer to its last
+ * flag (CUDA events on the copy stream), *npeer_out peers, *bytes_per_peer bytes
+ * (this rank's K' and V rows) sent to each.  VA_ERR_STATE when the last profiled
+ * call pushed nothing. */
+int va_exchange_times(va_ctx* ctx, float* ms_out /* [7] */, int* npeer_out, int64_t* bytes_per_peer);
 
 /* Failure-detection self-test (no reference counterpart; the reference has no
  * device-side waits).  Launches one kernel whose only wait is on a barrier that
@@ -353,7 +362,7 @@ int va_phase_times(va_ctx* ctx, float* ms_out /* [5] */);
 int va_selftest_bounded_wait(va_ctx* ctx, int64_t limit_us);
 /* Self-test of the attention kernel's wait for peer rows (the copy-engine K'/V
  * exchange) on one GPU: a 1-head, 256-key launch as rank 0 of 2 owning the first
- * 128 keys, with rank 1's flag set to peer_flag against epoch 1.  peer_flag >= 1:
+ * 128 keys; peer_flag != 0 raises rank 1's flag (epoch 1, all rows in place).  peer_flag != 0:
  * VA_OK and *out_max_abs = max |difference| to the same launch without a peer
  * (0: same key order).  peer_flag 0: the kernel gives up after its 2 s wait limit
  * and the call returns VA_ERR_DEVICE; the context stays usable. */

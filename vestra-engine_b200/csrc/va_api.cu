@@ -179,6 +179,21 @@ struct va_ctx {
   cudaStream_t ce_st[va::kMaxPeers] = {};
   cudaEvent_t ce_ev[va::kMaxPeers] = {};
   cudaEvent_t ev_qkv = nullptr;
+  // 64-bit exchange flags (FlashArgs::peer_flags), written by the peers; 128 bytes
+  // into the flag area of the arena.
+  unsigned long long* xflags64 = nullptr;
+  // Copy-engine push plan: rows are pushed in push_chunks chunks per peer (each
+  // followed by its flag), on one stream per peer, or with push_stagger on one
+  // stream peer after peer, the peer that reads this rank's rows first (rank - 1)
+  // first.  VA_PUSH_CHUNKS / VA_PUSH_ORDER=stagger|parallel.
+  int push_chunks = 2;
+  bool push_stagger = false;
+  // With the phase profile on: per-peer push times of the last sharded call
+  // (events around each peer's copies).
+  cudaEvent_t ce_t0[va::kMaxPeers] = {};
+  cudaEvent_t ce_t1[va::kMaxPeers] = {};
+  int xchg_peers = 0;
+  int64_t xchg_bytes = 0;
   int epoch = 0;
   void* peer_arena[va::kMaxRanks] = {};
   // token input side (va_load_patch_embed)
@@ -484,7 +499,8 @@ struct BranchSpec {
   __nv_bfloat16* peer_v[va::kMaxPeers];
   bool ce = false;        // copy-engine exchange (see va_ctx::ce)
   int epoch = 0;
-  int* peer_flag[va::kMaxPeers] = {};  // this rank's flag in each peer's flag array
+  unsigned long long* peer_flag[va::kMaxPeers] = {};  // this rank's flag in each peer's flag array
+  int peer_rank[va::kMaxPeers] = {};
 };
 
 // In-place all-gather of this rank's K'/V slices into the window buffers.
@@ -571,8 +587,9 @@ int setup_peers(va_ctx* c) {
     ce_ok = 1;
     for (int r = 0; ce_ok && r < nranks; ++r) {
       if (r == rank) continue;
-      int* slot = reinterpret_cast<int*>(static_cast<char*>(c->peer_arena[r]) + kArenaWindows * c->win_bytes) + rank;
-      ce_ok = va::stream_write_u32(c->stream, slot, 0u) ? 1 : 0;
+      auto* slot = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->peer_arena[r]) +
+                                                         kArenaWindows * c->win_bytes + 128) + rank;
+      ce_ok = va::stream_write_u64(c->stream, slot, 0ull) ? 1 : 0;
     }
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) {
       cudaGetLastError();
@@ -703,8 +720,8 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
   } else {
     fa.q_offset = static_cast<int>(b.row_offset + q0);
     fa.kv_rows = static_cast<int>(b.window_rows);
-    if (b.ce) {
-      fa.peer_flags = c->xflags;
+    if (b.npeer > 0) {
+      fa.peer_flags = c->xflags64;
       fa.epoch = b.epoch;
       fa.nranks = va::comm_size(c->comm);
       fa.rank = va::comm_rank(c->comm);
@@ -730,7 +747,7 @@ int stage_attn(va_ctx* c, int layer, const BranchSpec& b, int64_t q0, int64_t q1
 // Direct K'/V exchange of one sharded call: picks the call's window pair (1 or 2,
 // alternating) and every peer's copy of it, and fills the barrier arguments.
 // Returns false when the call uses no direct exchange.
-bool prepare_exchange(va_ctx* c, BranchSpec* b, va::PeerBarrierArgs* pb) {
+bool prepare_exchange(va_ctx* c, BranchSpec* b) {
   if (!b->gather || !c->p2p) return false;
   const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
   const int set = 1 + ((++c->epoch) & 1);
@@ -739,59 +756,75 @@ bool prepare_exchange(va_ctx* c, BranchSpec* b, va::PeerBarrierArgs* pb) {
   b->kwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set) * win);
   b->vwin = reinterpret_cast<__nv_bfloat16*>(own + (2 * set + 1) * win);
   b->npeer = 0;
-  *pb = va::PeerBarrierArgs{};
-  pb->local_flags = c->xflags;
-  pb->nranks = nranks;
-  pb->rank = rank;
-  pb->epoch = c->epoch;
   for (int r = 0; r < nranks; ++r) {
     if (r == rank) continue;
     char* pa = static_cast<char*>(c->peer_arena[r]);
     b->peer_k[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set) * win);
     b->peer_v[b->npeer] = reinterpret_cast<__nv_bfloat16*>(pa + (2 * set + 1) * win);
-    b->peer_flag[b->npeer] = reinterpret_cast<int*>(pa + kArenaWindows * win) + rank;
+    b->peer_flag[b->npeer] = reinterpret_cast<unsigned long long*>(pa + kArenaWindows * win + 128) + rank;
+    b->peer_rank[b->npeer] = r;
     ++b->npeer;
-    pb->peer_flags[r] = reinterpret_cast<int*>(pa + kArenaWindows * win);
   }
   b->ce = c->ce;
   b->epoch = c->epoch;
   return true;
 }
 
-// The copy-engine push of this rank's K'/V rows (after its QKV on `st`): one copy
-// stream per peer, K then V, then this rank's flag in that peer's flag array.
+// The copy-engine push of this rank's K'/V rows (after its QKV on `st`): per peer,
+// the rows in push_chunks chunks (K then V), each chunk followed by the peer's flag
+// (epoch, rows delivered so far, complete after the last chunk).  One copy stream
+// per peer, or with push_stagger one stream that serves the peers in the order they
+// read this rank's rows (rank - 1 first).
 int push_rows(va_ctx* c, const BranchSpec& b, cudaStream_t st) {
   const int E = c->cfg.embed_dim;
-  const size_t off = static_cast<size_t>(b.row_offset) * E;
-  const size_t bytes = static_cast<size_t>(b.rows) * E * sizeof(__nv_bfloat16);
+  const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
   VA_CUDA(c, cudaEventRecord(c->ev_qkv, st));
-  for (int p = 0; p < b.npeer; ++p) {
-    cudaStream_t cs = c->ce_st[p];
-    VA_CUDA(c, cudaStreamWaitEvent(cs, c->ev_qkv, 0));
-    VA_CUDA(c, cudaMemcpyAsync(b.peer_k[p] + off, b.kwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
-    VA_CUDA(c, cudaMemcpyAsync(b.peer_v[p] + off, b.vwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
-    if (!va::stream_write_u32(cs, b.peer_flag[p], static_cast<uint32_t>(b.epoch)))
-      return fail(c, VA_ERR_CUDA, "stream flag write to a peer failed");
-    VA_CUDA(c, cudaEventRecord(c->ce_ev[p], cs));
+  const int chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(c->push_chunks, b.rows / 64)));
+  const bool prof = c->phase_profile;
+  for (int k = 1; k < nranks; ++k) {
+    const int dst = (rank - k + nranks) % nranks;
+    const int p = dst < rank ? dst : dst - 1;  // peer index (peers in rank order)
+    cudaStream_t cs = c->ce_st[b.ce && c->push_stagger ? 0 : p];
+    if (!c->push_stagger || k == 1) VA_CUDA(c, cudaStreamWaitEvent(cs, c->ev_qkv, 0));
+    if (prof) VA_CUDA(c, cudaEventRecord(c->ce_t0[p], cs));
+    for (int ch = 0; ch < chunks; ++ch) {
+      const int64_t r0 = b.row_offset + b.rows * ch / chunks, r1 = b.row_offset + b.rows * (ch + 1) / chunks;
+      const size_t off = static_cast<size_t>(r0) * E;
+      const size_t bytes = static_cast<size_t>(r1 - r0) * E * sizeof(__nv_bfloat16);
+      VA_CUDA(c, cudaMemcpyAsync(b.peer_k[p] + off, b.kwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
+      VA_CUDA(c, cudaMemcpyAsync(b.peer_v[p] + off, b.vwin + off, bytes, cudaMemcpyDeviceToDevice, cs));
+      if (!va::stream_write_u64(cs, b.peer_flag[p], va::peer_flag_value(b.epoch, ch + 1 == chunks, r1)))
+        return fail(c, VA_ERR_CUDA, "stream flag write to a peer failed");
+    }
+    if (prof) VA_CUDA(c, cudaEventRecord(c->ce_t1[p], cs));
   }
+  for (int p = 0; p < b.npeer; ++p)
+    if (!c->push_stagger || p == 0) VA_CUDA(c, cudaEventRecord(c->ce_ev[p], c->ce_st[p]));
+  c->xchg_peers = prof ? b.npeer : 0;
+  c->xchg_bytes = b.rows * E * 2 * static_cast<int64_t>(sizeof(__nv_bfloat16));
   return VA_OK;
 }
 
 // `st` waits for every copy stream of the call (the copies read this rank's rows,
 // which the call after next overwrites).
 int join_push(va_ctx* c, const BranchSpec& b, cudaStream_t st) {
-  for (int p = 0; b.ce && p < b.npeer; ++p) VA_CUDA(c, cudaStreamWaitEvent(st, c->ce_ev[p], 0));
+  for (int p = 0; b.ce && p < b.npeer; ++p)
+    if (!c->push_stagger || p == 0) VA_CUDA(c, cudaStreamWaitEvent(st, c->ce_ev[p], 0));
   return VA_OK;
 }
 
 // The exchange step between the projection and the attention of a sharded call:
-// the direct exchange's barrier, or the NCCL all-gather.
-int exchange_step(va_ctx* c, const BranchSpec& b, bool direct, const va::PeerBarrierArgs& pb,
-                  cudaStream_t st) {
+// the copy-engine push, the flags after the epilogue's peer stores, or the NCCL
+// all-gather.
+int exchange_step(va_ctx* c, const BranchSpec& b, bool direct, cudaStream_t st) {
   if (direct && b.ce) {
     return push_rows(c, b, st);
   } else if (direct) {
-    VA_CUDA(c, va::launch_peer_barrier(pb, c->err, st));
+    va::PeerFlagArgs pf{};
+    pf.npeer = b.npeer;
+    for (int p = 0; p < b.npeer; ++p) pf.peer_flag[p] = b.peer_flag[p];
+    pf.value = va::peer_flag_value(b.epoch, true, b.row_offset + b.rows);
+    VA_CUDA(c, va::launch_peer_flags(pf, st));
   } else if (b.gather) {
     const int E = c->cfg.embed_dim;
     return gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st);
@@ -804,17 +837,17 @@ int run_branch(va_ctx* c, int layer, const BranchSpec& b_in, cudaStream_t st) {
   int rc = validate_branch(c, layer, b_in);
   if (rc) return rc;
   BranchSpec b = b_in;
-  va::PeerBarrierArgs pb{};
-  const bool direct = prepare_exchange(c, &b, &pb);
+  const bool direct = prepare_exchange(c, &b);
   // With the phase profile on, an event goes between every two launches; the ln
   // and qkv phases are split inside stage_qkv's two launches by mark(1).
   const bool prof = c->phase_profile;
   auto mark = [&](int i) { return prof ? cudaEventRecord(c->ph_ev[i], st) : cudaSuccess; };
   c->phase_valid = false;
+  c->xchg_peers = 0;
   VA_CUDA(c, mark(0));
   if ((rc = stage_qkv(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[1] : nullptr))) return rc;
   VA_CUDA(c, mark(2));
-  if ((rc = exchange_step(c, b, direct, pb, st))) return rc;
+  if ((rc = exchange_step(c, b, direct, st))) return rc;
   VA_CUDA(c, mark(3));
   if ((rc = stage_attn(c, layer, b, 0, b.rows, st, prof ? c->ph_ev[4] : nullptr))) return rc;
   if ((rc = join_push(c, b, st))) return rc;
@@ -894,6 +927,7 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
     c->k = reinterpret_cast<__nv_bfloat16*>(a);
     c->v = reinterpret_cast<__nv_bfloat16*>(a + win);
     c->xflags = reinterpret_cast<int*>(a + kArenaWindows * win);
+    c->xflags64 = reinterpret_cast<unsigned long long*>(a + kArenaWindows * win + 128);
     if ((e = cudaMemset(c->xflags, 0, 256)) != cudaSuccess) return bail(e);
   }
   if ((e = dmalloc(&c->o, n)) != cudaSuccess) return bail(e);
@@ -926,6 +960,16 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
     if ((e = cudaEventCreateWithFlags(&c->ce_ev[p], cudaEventDisableTiming)) != cudaSuccess) return bail(e);
   }
   if ((e = cudaEventCreateWithFlags(&c->ev_qkv, cudaEventDisableTiming)) != cudaSuccess) return bail(e);
+  for (int p = 0; p < va::kMaxPeers; ++p) {
+    if ((e = cudaEventCreate(&c->ce_t0[p])) != cudaSuccess) return bail(e);
+    if ((e = cudaEventCreate(&c->ce_t1[p])) != cudaSuccess) return bail(e);
+  }
+  {
+    const char* pc = std::getenv("VA_PUSH_CHUNKS");
+    if (pc && std::atoi(pc) >= 1 && std::atoi(pc) <= 16) c->push_chunks = std::atoi(pc);
+    const char* po = std::getenv("VA_PUSH_ORDER");
+    if (po) c->push_stagger = std::string(po) == "stagger";
+  }
   {
     const size_t slots = static_cast<size_t>(va::flash_part_slots(c->sms));
     if ((e = dmalloc(&c->part_o, slots * 128 * 64)) != cudaSuccess) return bail(e);
@@ -994,6 +1038,10 @@ void va_destroy(va_ctx* c) {
     if (c->ce_ev[p]) cudaEventDestroy(c->ce_ev[p]);
   }
   if (c->ev_qkv) cudaEventDestroy(c->ev_qkv);
+  for (int p = 0; p < va::kMaxPeers; ++p) {
+    if (c->ce_t0[p]) cudaEventDestroy(c->ce_t0[p]);
+    if (c->ce_t1[p]) cudaEventDestroy(c->ce_t1[p]);
+  }
   delete c;
 }
 
@@ -1207,8 +1255,7 @@ void plan_host_chunks(const va_ctx* c, const BranchSpec& b, int view_count, Boun
 // attention chunk.
 int host_call(va_ctx* c, int layer, BranchSpec b, int view_count, const float* ln1, float* out) {
   int rc = VA_OK;
-  va::PeerBarrierArgs pb{};
-  const bool direct = prepare_exchange(c, &b, &pb);
+  const bool direct = prepare_exchange(c, &b);
   Bounds in, outb;
   plan_host_chunks(c, b, view_count, &in, &outb);
   const int E = c->cfg.embed_dim;
@@ -1241,7 +1288,7 @@ int host_call(va_ctx* c, int layer, BranchSpec b, int view_count, const float* l
     }
   }
   if (b.seg_len == 0) {
-    if ((rc = exchange_step(c, b, direct, pb, c->stream))) return finish(rc);
+    if ((rc = exchange_step(c, b, direct, c->stream))) return finish(rc);
     for (int j = 0; j < n_out; ++j) {
       if ((rc = stage_attn(c, layer, b, outb[j], outb[j + 1], c->stream))) return finish(rc);
       VA_HOST(cudaEventRecord(c->ev_out[j], c->stream));
@@ -2190,6 +2237,20 @@ int va_phase_times(va_ctx* c, float* ms_out) {
   return VA_OK;
 }
 
+int va_exchange_times(va_ctx* c, float* ms_out, int* npeer_out, int64_t* bytes_per_peer) {
+  if (!c || !ms_out || !npeer_out || !bytes_per_peer) return VA_ERR_INVALID;
+  if (!c->phase_valid || c->xchg_peers == 0)
+    return fail(c, VA_ERR_STATE, "no profiled copy-engine exchange since the profile was enabled");
+  VA_CUDA(c, cudaSetDevice(c->device));
+  for (int p = 0; p < c->xchg_peers; ++p) {
+    VA_CUDA(c, cudaEventSynchronize(c->ce_t1[p]));
+    VA_CUDA(c, cudaEventElapsedTime(&ms_out[p], c->ce_t0[p], c->ce_t1[p]));
+  }
+  *npeer_out = c->xchg_peers;
+  *bytes_per_peer = c->xchg_bytes;
+  return VA_OK;
+}
+
 int va_selftest_bounded_wait(va_ctx* c, int64_t limit_us) {
   if (!c) return VA_ERR_INVALID;
   if (limit_us <= 0 || limit_us > 1000000) return fail(c, VA_ERR_INVALID, "limit_us must be in (0, 1e6]");
@@ -2216,7 +2277,7 @@ int va_selftest_peer_wait(va_ctx* c, int peer_flag, float* out_max_abs) {
   std::vector<uint16_t> h(static_cast<size_t>(rows) * cols);
   for (size_t i = 0; i < h.size(); ++i) h[i] = f32_to_bf16_rne(std::sin(0.37f * static_cast<float>(i)));
   __nv_bfloat16 *qkv = nullptr, *o1 = nullptr, *o2 = nullptr;
-  int* flags = nullptr;
+  unsigned long long* flags = nullptr;
   auto release = [&]() {
     cudaStreamSynchronize(c->stream);
     dfree(qkv);
@@ -2229,8 +2290,9 @@ int va_selftest_peer_wait(va_ctx* c, int peer_flag, float* out_max_abs) {
   if (e == cudaSuccess) e = dmalloc(&o2, h.size());
   if (e == cudaSuccess) e = dmalloc(&flags, va::kMaxRanks);
   if (e == cudaSuccess) e = cudaMemcpy(qkv, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemset(flags, 0, va::kMaxRanks * sizeof(int));
-  if (e == cudaSuccess && peer_flag) e = cudaMemcpy(flags + 1, &peer_flag, sizeof(int), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(flags, 0, va::kMaxRanks * sizeof(unsigned long long));
+  const unsigned long long raised = va::peer_flag_value(1, true, rows);
+  if (e == cudaSuccess && peer_flag) e = cudaMemcpy(flags + 1, &raised, sizeof(raised), cudaMemcpyHostToDevice);
   va::FlashArgs fa{};
   fa.q_count = rows;
   fa.kv_rows = rows;

@@ -262,20 +262,62 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int s
   return *c.tmem_slot();
 }
 
-// Waits (bounded) until every peer's rows of the key window have arrived.
-__device__ __forceinline__ bool wait_peer_rows(const FlashArgs& fa, volatile int* abort_flag, int* err) {
-  const unsigned long long t0 = globaltimer_ns();
-  for (int r = 0; r < fa.nranks; ++r) {
-    if (r == fa.rank) continue;
-    while (ld_acquire_sys(fa.peer_flags + r) < fa.epoch) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        report_error(err, kDevTimeoutPeer);
-        return false;
+// Progress of the peers' rows in this rank's key window (sharded global blocks).
+// The ranks' slices are contiguous and in rank order, and the producer visits key
+// tiles from its own slice onwards, so the rows it needs next belong to rank + 1,
+// then rank + 2, ..., wrapping to rank 0.  Peer r announces its rows in
+// peer_flags[r] = epoch << 32 | complete << 31 | end: its rows up to window row
+// `end` are in place (complete: all of them), so no rank needs the other ranks'
+// slice boundaries in advance.  `covered` counts the rows known present after
+// own_end in that cyclic order.
+struct PeerCover {
+  int next;
+  int covered;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Rows of key tile [row, re) that are not this rank's, as a count of cyclic rows
+// after own_end that must be present (0: the tile is this rank's alone).
+__device__ __forceinline__ int tile_need(const FlashArgs& fa, int row, int re) {
+  int need = 0;
+  if (re > max(row, fa.own_end)) need = re - fa.own_end;                    // rows at or after own_end
+  const int below = min(re, fa.own_begin);
+  if (below > row) need = max(need, below - fa.own_end + fa.kv_rows);       // rows before own_begin
+  return need;
+}
+
+// Waits (bounded) until the peers' rows cover `need` rows after own_end.
+__device__ __forceinline__ bool wait_cover(const FlashArgs& fa, PeerCover& pc, int need,
+                                           volatile int* abort_flag, int* err) {
+  const int total = fa.kv_rows - (fa.own_end - fa.own_begin);  // every row that is not ours
+  need = min(need, total);
+  unsigned long long t0 = 0;
+  while (pc.covered < need) {
+    const unsigned long long f = ld_acquire_sys_u64(fa.peer_flags + pc.next);
+    if (static_cast<unsigned>(f >> 32) == static_cast<unsigned>(fa.epoch)) {
+      int cov = static_cast<int>(f & 0x7fffffffu) - fa.own_end;
+      if (cov <= 0) cov += fa.kv_rows;
+      pc.covered = max(pc.covered, cov);
+      if (f & (1ull << 31)) {  // all of this peer's rows: go on to the next rank
+        pc.next = pc.next + 1 == fa.nranks ? 0 : pc.next + 1;
+        if (pc.next == fa.rank) pc.covered = total;
+        continue;
       }
-      __nanosleep(200);
+      if (pc.covered >= need) break;
     }
+    if (t0 == 0) t0 = globaltimer_ns();
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      report_error(err, kDevTimeoutPeer);
+      return false;
+    }
+    __nanosleep(128);
   }
   return true;
 }
@@ -288,14 +330,14 @@ __device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const 
   mbar_arrive_expect_tx(c.q_full(), g.nq * kTileBytes);
   tma_load_2d(c.sQ(0), mq, c.q_full(), g.col, g.q0);
   if (g.nq == 2) tma_load_2d(c.sQ(1), mq, c.q_full(), g.col, g.q0 + kTileQ);
-  bool peers_in = fa.peer_flags == nullptr;
+  PeerCover pc{fa.rank + 1 == fa.nranks ? 0 : fa.rank + 1, 0};
   for (int j = 0; j < g.num_kv; ++j) {
     const int s = j % kStages;
     const uint32_t ph = (j / kStages) & 1;
     const int row = g.k0 + ((j + g.rot) % g.num_kv) * kTileK;
-    if (!peers_in && !(row >= fa.own_begin && row + kTileK <= fa.own_end)) {
-      if (!wait_peer_rows(fa, c.abort_flag(), err)) break;
-      peers_in = true;
+    if (fa.peer_flags) {
+      const int need = tile_need(fa, row, min(row + kTileK, fa.kv_rows));
+      if (need > pc.covered && !wait_cover(fa, pc, need, c.abort_flag(), err)) break;
     }
     if (!mbar_wait(c.kv_empty(s), ph ^ 1, c.abort_flag(), err, kDevTimeoutProducer)) break;
     mbar_arrive_expect_tx(c.kv_full(s), 2 * kTileBytes);

@@ -49,6 +49,16 @@ struct Fc1EpilogueArgs {
 cudaError_t launch_fc1_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int m, int n, int k,
                             const Fc1EpilogueArgs& epi, int* err, cudaStream_t st);
 
+// Flag writes of the epilogue-store K'/V exchange: after the QKV kernel's peer
+// stores, value is written (system-scope release) to each peer's flag, with no
+// wait: the attention kernels wait on their own flags.
+struct PeerFlagArgs {
+  unsigned long long* peer_flag[kMaxPeers];  // this rank's flag in each peer's flag array
+  int npeer;
+  unsigned long long value;
+};
+cudaError_t launch_peer_flags(const PeerFlagArgs& a, cudaStream_t st);
+
 // Barrier of the direct K'/V exchange: this rank tells every peer that its slice
 // has arrived there (flag = epoch in the peer's flag array at index `rank`) and
 // waits until every peer has told it the same.
@@ -126,18 +136,24 @@ struct FlashArgs {
   // Filled in by launch_flash (kernel-side view of the plan).
   int n_full = 0;
   int splits = 1;
-  // Copy-engine K'/V exchange of a sharded global block: key rows outside this
-  // rank's own rows [own_begin, own_end) arrive from the peers; peer r's rows are in
-  // place once peer_flags[r] >= epoch (written by r's copy stream).  The producer
-  // starts at the first key tile of its own rows and waits (bounded) for every peer
-  // before the first tile that is not entirely its own.  nullptr: nothing to wait for.
-  const int* peer_flags = nullptr;
+  // K'/V exchange of a sharded global block: key rows outside this rank's own rows
+  // [own_begin, own_end) arrive from the peers.  peer_flags[r] = epoch << 32 |
+  // complete << 31 | end once peer r's rows up to window row `end` are in place
+  // (complete: all of them); the ranks' slices are contiguous in rank order.  The
+  // producer starts at the first key tile of its own rows and waits (bounded) only
+  // for the rows of the next tile it loads.  nullptr: nothing to wait for.
+  const unsigned long long* peer_flags = nullptr;
   int epoch = 0;
   int nranks = 0;
   int rank = 0;
   int own_begin = 0;
   int own_end = 0;
 };
+// Value of an exchange flag (see FlashArgs::peer_flags).
+inline unsigned long long peer_flag_value(int epoch, bool complete, int64_t end) {
+  return (static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32) |
+         (complete ? (1ull << 31) : 0ull) | static_cast<unsigned long long>(end & 0x7fffffff);
+}
 // Slots a context provides for the split tail: rem < sms units, at most 4 key
 // ranges each, two query tiles per CTA.
 inline int flash_part_slots(int sms) { return 2 * 4 * sms; }
@@ -146,6 +162,8 @@ inline int flash_part_slots(int sms) { return 2 * 4 * sms; }
 // `value` lands at `addr` (this GPU's or a mapped peer's memory) once the stream's
 // earlier work is done, behind a memory fence.  False when unavailable or refused.
 bool stream_write_u32(cudaStream_t st, int* addr, uint32_t value);
+// The same for a 64-bit value (cuStreamWriteValue64).
+bool stream_write_u64(cudaStream_t st, unsigned long long* addr, unsigned long long value);
 
 // Tensor-map encoding through the driver entry point (no -lcuda needed).
 bool encode_tma_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

@@ -44,6 +44,8 @@ bool get_encode() {
 namespace {
 PFN_cuStreamWriteValue32_v11070 g_write32 = nullptr;
 std::once_flag g_write32_once;
+PFN_cuStreamWriteValue64_v11070 g_write64 = nullptr;
+std::once_flag g_write64_once;
 }  // namespace
 
 bool stream_write_u32(cudaStream_t st, int* addr, uint32_t value) {
@@ -57,6 +59,20 @@ bool stream_write_u32(cudaStream_t st, int* addr, uint32_t value) {
   if (!g_write32 || !addr) return false;
   // Default flags: the write is preceded by a memory fence over the stream's earlier work.
   return g_write32(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(addr), value,
+                   CU_STREAM_WRITE_VALUE_DEFAULT) == CUDA_SUCCESS;
+}
+
+bool stream_write_u64(cudaStream_t st, unsigned long long* addr, unsigned long long value) {
+  std::call_once(g_write64_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue64", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_write64 = reinterpret_cast<PFN_cuStreamWriteValue64_v11070>(fn);
+  });
+  if (!g_write64 || !addr) return false;
+  // Default flags: the write is preceded by a memory fence over the stream's earlier work.
+  return g_write64(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(addr), value,
                    CU_STREAM_WRITE_VALUE_DEFAULT) == CUDA_SUCCESS;
 }
 
@@ -627,6 +643,21 @@ __global__ void peer_barrier_kernel(PeerBarrierArgs a, int* err) {
       }
     }
   }
+}
+
+__global__ void peer_flags_kernel(PeerFlagArgs a) {
+  const int p = threadIdx.x;
+  if (p < a.npeer) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a.peer_flag[p]), "l"(a.value) : "memory");
+  }
+}
+
+cudaError_t launch_peer_flags(const PeerFlagArgs& a, cudaStream_t st) {
+  if (a.npeer < 0 || a.npeer > kMaxPeers) return cudaErrorInvalidValue;
+  if (a.npeer == 0) return cudaSuccess;
+  peer_flags_kernel<<<1, 32, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, int* err, cudaStream_t st) {
