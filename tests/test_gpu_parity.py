@@ -185,6 +185,29 @@ def test_attention_block_matches_oracle(ctx, oracle_mod, name):
     assert_close(got, ref, what=name)
 
 
+@pytest.mark.parametrize("name", ["cfg1_single_view", "cfg2_s2_global"])
+def test_attention_block_interleaved_rope_pairing(oracle_mod, name):
+    # rope_pairing = 1 (pairs (2i, 2i+1) inside each half instead of (i, i+16)): the
+    # QKV epilogue's RoPE and the host tables follow the switch, against the oracle
+    # run with the same pairing; the fixed-offset and the row-max softmax both.
+    wl = syn.CONFIGS[name]
+    cfg = va.default_config(max_rows=wl.rows, depth=12, rope_start=4, qknorm_start=4, num_register=1,
+                            rope_pairing=1)
+    c = va.Context(cfg, 0)
+    try:
+        p = syn.layer_weights(wl.embed, seed=9, layer=4, bias=True, perturb_norm=True)
+        c.load_layer(4, p)
+        x = syn.hidden_states(wl.rows, wl.embed, seed=9)
+        got = c.attention_host(4, x, wl.gh, wl.gw, wl.views, wl.global_)
+        pos = va.positions_yx(wl.rows, wl.views, wl.n_special, wl.gh, wl.gw, wl.global_)
+        ref = oracle_mod.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=wl.seg_len, pairing=1)
+        assert_close(got, ref, what=f"{name} pairing 1")
+        ref0 = oracle_mod.attention_block(x, p, wl.heads, pos_yx=pos, seg_len=wl.seg_len, pairing=0)
+        assert np.abs(ref0 - ref).max() > 1e-3  # the two pairings differ on these inputs
+    finally:
+        c.close()
+
+
 def test_attention_block_reference_token_count_865(ctx, oracle_mod):
     # The reference DA3-BASE layout has 1 special token (865 per view).
     cfg = va.default_config(max_rows=2 * 865, num_register=0)
