@@ -589,7 +589,8 @@ def run_ours(args):
         l_flops = 4.0 * wl.views * n_tok * n_tok * 64 * wl.heads
         my_flops = 4.0 * lv * n_tok * n_tok * 64 * wl.heads
         peak_t, _, _ = load_peaks()
-        lpar = parity_check(wl, p_metric, x_all, ol, v0, parity_rows(wl.rows, PARITY_ROWS, 8), world, rank,
+        wl_local = syn.CONFIGS["cfg4_s12_local"]  # the same views with per-view positions
+        lpar = parity_check(wl_local, p_metric, x_all, ol, v0, parity_rows(wl.rows, PARITY_ROWS, 8), world, rank,
                             seg_len=n_tok)
         local_section = {
             "workload": "cfg4 local blocks (12 x 866-token views, block-diagonal attention)",
