@@ -3,9 +3,10 @@
 One child process per GPU; rank 0 creates the NCCL unique id and hands it to the
 others through a multiprocessing queue, every rank then projects K'/V for its own
 equal token slice, all-gathers them in place and attends its queries to the whole
-window.  K'/V travel either by direct peer stores from the QKV epilogue (the
-default when every rank can map every peer's window) or by an NCCL all-gather
-(VA_KV_EXCHANGE=nccl); both must give the same result.  The concatenated rank
+window.  K'/V travel by copy-engine pushes with per-peer flags (the default when
+every rank can map every peer's window and write its flags), by direct peer stores
+from the QKV epilogue (VA_KV_EXCHANGE=sm), or by an NCCL all-gather
+(VA_KV_EXCHANGE=nccl); all must give the same result.  The concatenated rank
 outputs must match the single-GPU sub-block (same kernels; only the split of the
 single launch's last wave rounds differently) and meet the oracle gates on a row
 sample.
@@ -39,6 +40,10 @@ def _rank_main(rank, nranks, exchange, ids, results):
     try:
         if exchange in ("nccl", "sm"):
             os.environ["VA_KV_EXCHANGE"] = exchange
+        elif exchange == "stagger":  # copy-engine push, one stream, rank - 1 first
+            os.environ["VA_PUSH_ORDER"] = "stagger"
+        elif exchange.startswith("chunks"):  # copy-engine push in that many chunks per peer
+            os.environ["VA_PUSH_CHUNKS"] = exchange[len("chunks"):]
         torch.cuda.set_device(rank)
         wl = syn.CONFIGS[WORKLOAD]
         row0, local = va.shard_rows(wl.rows, nranks, rank)
@@ -75,12 +80,15 @@ def _rank_main(rank, nranks, exchange, ids, results):
 
 
 # "default": the copy-engine push where every rank can write a peer's flag by a
-# stream memory operation, else the epilogue's peer stores; "sm": forced epilogue
-# stores + barrier kernel; "nccl": forced all-gather.
-EXPECTED_MODE = {"default": ("direct-ce", "direct"), "sm": ("direct",), "nccl": ("nccl",)}
+# stream memory operation, else the epilogue's peer stores; "stagger" / "chunks1" /
+# "chunks5": the same push on one stream peer after peer / in 1 or 5 chunks per
+# peer; "sm": forced epilogue stores + flag kernel; "nccl": forced all-gather.
+EXPECTED_MODE = {"default": ("direct-ce", "direct"), "stagger": ("direct-ce", "direct"),
+                 "chunks1": ("direct-ce", "direct"), "chunks5": ("direct-ce", "direct"),
+                 "sm": ("direct",), "nccl": ("nccl",)}
 
 
-@pytest.mark.parametrize("exchange", ["default", "sm", "nccl"])
+@pytest.mark.parametrize("exchange", ["default", "stagger", "chunks1", "chunks5", "sm", "nccl"])
 @pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks, exchange):
     if torch.cuda.device_count() < nranks:
