@@ -274,7 +274,8 @@ int va_attention_host_sharded(va_ctx* ctx, int layer, const float* ln1_local, fl
 /* 0: no communicator, 1: NCCL all-gather, 2: direct, the QKV epilogue stores each
  * finished K'/V tile into every peer's window over NVLink, then a one-warp kernel
  * raises this rank's flag in every peer (system-scope release, no wait), 3: direct,
- * pushed by copy engines in VA_PUSH_CHUNKS chunks per peer (default 2), each chunk
+ * pushed by copy engines in VA_PUSH_CHUNKS chunks per peer (default: one per 16 MB
+ * sent to the peer, at most 4), each chunk
  * followed by a stream memory write of this rank's flag in that peer (one copy
  * stream per peer, or with VA_PUSH_ORDER=stagger one stream serving rank - 1 first).
  * A flag holds the call's epoch and how far this rank's rows have arrived.  In modes

@@ -182,11 +182,11 @@ struct va_ctx {
   // 64-bit exchange flags (FlashArgs::peer_flags), written by the peers; 128 bytes
   // into the flag area of the arena.
   unsigned long long* xflags64 = nullptr;
-  // Copy-engine push plan: rows are pushed in push_chunks chunks per peer (each
-  // followed by its flag), on one stream per peer, or with push_stagger on one
-  // stream peer after peer, the peer that reads this rank's rows first (rank - 1)
-  // first.  VA_PUSH_CHUNKS / VA_PUSH_ORDER=stagger|parallel.
-  int push_chunks = 2;
+  // Copy-engine push plan: rows are pushed in chunks per peer (each followed by its
+  // flag; push_chunks, or 0: one per 16 MB per peer, at most 4), on one stream per
+  // peer, or with push_stagger on one stream peer after peer, the peer that reads
+  // this rank's rows first (rank - 1) first.  VA_PUSH_CHUNKS / VA_PUSH_ORDER.
+  int push_chunks = 0;
   bool push_stagger = false;
   // With the phase profile on: per-peer push times of the last sharded call
   // (events around each peer's copies).
@@ -779,7 +779,11 @@ int push_rows(va_ctx* c, const BranchSpec& b, cudaStream_t st) {
   const int E = c->cfg.embed_dim;
   const int nranks = va::comm_size(c->comm), rank = va::comm_rank(c->comm);
   VA_CUDA(c, cudaEventRecord(c->ev_qkv, st));
-  const int chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(c->push_chunks, b.rows / 64)));
+  // Chunks: the VA_PUSH_CHUNKS setting, else one per 16 MB sent to a peer (each copy
+  // costs ~10 us of its own, so small slices go in one piece), at most 4.
+  const int64_t peer_bytes = b.rows * E * 2 * static_cast<int64_t>(sizeof(__nv_bfloat16));
+  const int64_t want = c->push_chunks > 0 ? c->push_chunks : std::min<int64_t>(4, (peer_bytes + (16 << 20) - 1) >> 24);
+  const int chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, b.rows / 64)));
   const bool prof = c->phase_profile;
   for (int k = 1; k < nranks; ++k) {
     const int dst = (rank - k + nranks) % nranks;

@@ -299,7 +299,16 @@ __device__ __forceinline__ bool wait_cover(const FlashArgs& fa, PeerCover& pc, i
   unsigned long long t0 = 0;
   while (pc.covered < need) {
     const unsigned long long f = ld_acquire_sys_u64(fa.peer_flags + pc.next);
-    if (static_cast<unsigned>(f >> 32) == static_cast<unsigned>(fa.epoch)) {
+    const int fe = static_cast<int>(f >> 32);
+    // A peer can be one call ahead: it pushes the next call's rows into the other
+    // window pair once its own attention of this call is done, and raises its flag
+    // for that call.  A newer epoch therefore means every row of this call arrived.
+    if (fe > fa.epoch) {
+      pc.next = pc.next + 1 == fa.nranks ? 0 : pc.next + 1;
+      if (pc.next == fa.rank) pc.covered = total;
+      continue;
+    }
+    if (fe == fa.epoch) {
       int cov = static_cast<int>(f & 0x7fffffffu) - fa.own_end;
       if (cov <= 0) cov += fa.kv_rows;
       pc.covered = max(pc.covered, cov);

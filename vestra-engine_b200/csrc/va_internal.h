@@ -59,16 +59,6 @@ struct PeerFlagArgs {
 };
 cudaError_t launch_peer_flags(const PeerFlagArgs& a, cudaStream_t st);
 
-// Barrier of the direct K'/V exchange: this rank tells every peer that its slice
-// has arrived there (flag = epoch in the peer's flag array at index `rank`) and
-// waits until every peer has told it the same.
-struct PeerBarrierArgs {
-  int* local_flags;            // [kMaxRanks], written by the peers
-  int* peer_flags[kMaxRanks];  // each peer's flag array (nullptr at index rank)
-  int nranks, rank, epoch;
-};
-cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, int* err, cudaStream_t st);
-
 // ---- output projection (K3): O[rows,E] bf16 x Wp^T + b (* ls1) (+ residual) -> F32 ----
 struct ProjEpilogueArgs {
   const float* bias;      // [E]

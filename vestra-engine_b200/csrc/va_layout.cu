@@ -620,31 +620,10 @@ __global__ void bounded_wait_selftest_kernel(unsigned long long limit_ns, int* e
   __syncthreads();
 }
 
-// Direct K'/V exchange barrier, one warp: lane r publishes this rank's epoch to
-// peer r, then waits (bounded) for peer r's epoch here.  The QKV kernel before it
-// fenced its peer stores at system scope; the release/acquire pair orders them
-// before the peer's attention kernel reads them.
-constexpr unsigned long long kPeerWaitNs = 2000000000ull;
-
-__global__ void peer_barrier_kernel(PeerBarrierArgs a, int* err) {
-  const int r = threadIdx.x;
-  const bool peer = r < a.nranks && r != a.rank;
-  if (peer) {
-    __threadfence_system();
-    st_release_sys(a.peer_flags[r] + a.rank, a.epoch);
-  }
-  __syncwarp();
-  if (peer) {
-    const unsigned long long t0 = globaltimer_ns();
-    while (ld_acquire_sys(a.local_flags + r) < a.epoch) {
-      if (globaltimer_ns() - t0 > kPeerWaitNs) {
-        report_error(err, kDevTimeoutPeer);
-        break;
-      }
-    }
-  }
-}
-
+// Flags of the epilogue-store K'/V exchange, one warp: lane p publishes this rank's
+// flag value to peer p (system-scope release, no wait).  The QKV kernel before it
+// on the stream stored the rows; the fence and the release order those stores
+// before the flag, and the peer's attention kernel reads the flag with acquire.
 __global__ void peer_flags_kernel(PeerFlagArgs a) {
   const int p = threadIdx.x;
   if (p < a.npeer) {
@@ -657,12 +636,6 @@ cudaError_t launch_peer_flags(const PeerFlagArgs& a, cudaStream_t st) {
   if (a.npeer < 0 || a.npeer > kMaxPeers) return cudaErrorInvalidValue;
   if (a.npeer == 0) return cudaSuccess;
   peer_flags_kernel<<<1, 32, 0, st>>>(a);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_peer_barrier(const PeerBarrierArgs& a, int* err, cudaStream_t st) {
-  if (a.nranks < 1 || a.nranks > kMaxRanks || a.rank < 0 || a.rank >= a.nranks) return cudaErrorInvalidValue;
-  peer_barrier_kernel<<<1, 32, 0, st>>>(a, err);
   return cudaGetLastError();
 }
 
