@@ -432,8 +432,8 @@ def run_ours(args):
         flush_buf.zero_()
         step()
         phase_runs.append(ctx.phase_times())
-        if mode == "direct-ce":
-            xchg_runs.append(ctx.exchange_times())
+        if world > 1:
+            xchg_runs.append((ctx.last_exchange(), ctx.exchange_times()))
     ctx.set_phase_profile(False)
     barrier()
     phases = {k: round(statistics.median(r[k] for r in phase_runs), 4) for k in phase_runs[0]}
@@ -445,11 +445,15 @@ def run_ours(args):
     ln_gbs = round(local_rows * wl.embed * 6 / (phases["ln"] * 1e-3) / 1e9, 1)  # F32 read + bf16 write
     exchange = None
     if world > 1:
-        exchange = {"mode": mode}
-        if xchg_runs:
-            npeer = len(xchg_runs[0][0])
-            per_peer = [statistics.median(r[0][i] for r in xchg_runs) for i in range(npeer)]
-            nbytes = xchg_runs[0][1]
+        used = xchg_runs[-1][0]
+        exchange = {"mode": mode, "path": {"direct": "QKV-epilogue peer stores + per-peer flags",
+                                           "direct-ce": "copy-engine push + per-peer flags",
+                                           "nccl": "NCCL all-gather"}.get(used, used)}
+        pushes = [r[1] for r in xchg_runs if r[1][0]]
+        if pushes:
+            npeer = len(pushes[0][0])
+            per_peer = [statistics.median(r[0][i] for r in pushes) for i in range(npeer)]
+            nbytes = pushes[0][1]
             exchange.update({
                 "bytes_per_peer": nbytes,
                 "per_peer_ms": [round(v, 4) for v in per_peer],
@@ -864,7 +868,7 @@ def run_ours(args):
                     "pipelined": pipelined},
             "phases_ms": phases, "gemm_tflops": gemm_tflops, "ln_cast_gbs": ln_gbs, "block": block, "window": window, "tokens": tokens,
             "gguf": gguf_section,
-            "gpu_launches": (5 if mode == "direct" else 4) * args.steps,
+            "gpu_launches": (5 if world > 1 and xchg_runs[-1][0] == "direct" else 4) * args.steps,
             "parity": parity, "exchange": exchange, "local": local_section, "large": large,
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,

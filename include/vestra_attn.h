@@ -277,12 +277,17 @@ int va_attention_host_sharded(va_ctx* ctx, int layer, const float* ln1_local, fl
  * pushed by copy engines in VA_PUSH_CHUNKS chunks per peer (default: one per 16 MB
  * sent to the peer, at most 4), each chunk
  * followed by a stream memory write of this rank's flag in that peer (one copy
- * stream per peer, or with VA_PUSH_ORDER=stagger one stream serving rank - 1 first).
+ * stream serving the peers in the order they read this rank's rows, rank - 1 first,
+ * or with VA_PUSH_ORDER=parallel one copy stream per peer).
  * A flag holds the call's epoch and how far this rank's rows have arrived.  In modes
  * 2 and 3 the attention kernel starts on the rank's own key tiles and, before each
- * later tile, waits (bounded) only until the rows of that tile are in place.
- * VA_KV_EXCHANGE=nccl or =sm at va_comm_init force modes 1 or 2. */
+ * later tile, waits (bounded) only until the rows of that tile are in place.  Where
+ * mode 3 is available a call still uses mode 2 when it sends less than 12 MB to each
+ * peer (the epilogue stores are faster there).  VA_KV_EXCHANGE=nccl, =sm or =ce at
+ * va_comm_init force modes 1, 2 or (where available) 3. */
 int va_comm_exchange_mode(const va_ctx* ctx);
+/* The path the last sharded call took (codes as above; 0 before any). */
+int va_last_exchange(const va_ctx* ctx);
 /* ln1_local/out_local: device F32 [local_rows, E], this rank's rows
  * [rank*local_rows, (rank+1)*local_rows) of a window of nranks*local_rows tokens
  * made of view_count views.  Collective: every rank calls it for the same layer. */
@@ -349,8 +354,8 @@ int va_phase_times(va_ctx* ctx, float* ms_out /* [5] */);
  * sharded call, per peer (no reference counterpart; the reference has no
  * multi-GPU path): ms_out[p] = time from the first copy to this peer to its last
  * flag (CUDA events on the copy stream), *npeer_out peers, *bytes_per_peer bytes
- * (this rank's K' and V rows) sent to each.  VA_ERR_STATE when the last profiled
- * call pushed nothing. */
+ * (this rank's K' and V rows) sent to each; *npeer_out = 0 when the last profiled
+ * call pushed nothing by copy engines.  VA_ERR_STATE before any profiled call. */
 int va_exchange_times(va_ctx* ctx, float* ms_out /* [7] */, int* npeer_out, int64_t* bytes_per_peer);
 
 /* Failure-detection self-test (no reference counterpart; the reference has no

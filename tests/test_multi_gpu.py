@@ -40,9 +40,13 @@ def _rank_main(rank, nranks, exchange, ids, results):
     try:
         if exchange in ("nccl", "sm"):
             os.environ["VA_KV_EXCHANGE"] = exchange
-        elif exchange == "stagger":  # copy-engine push, one stream, rank - 1 first
-            os.environ["VA_PUSH_ORDER"] = "stagger"
+        elif exchange == "ce":  # copy-engine push for every slice size
+            os.environ["VA_KV_EXCHANGE"] = "ce"
+        elif exchange == "parallel":  # copy-engine push, one stream per peer
+            os.environ["VA_KV_EXCHANGE"] = "ce"
+            os.environ["VA_PUSH_ORDER"] = "parallel"
         elif exchange.startswith("chunks"):  # copy-engine push in that many chunks per peer
+            os.environ["VA_KV_EXCHANGE"] = "ce"
             os.environ["VA_PUSH_CHUNKS"] = exchange[len("chunks"):]
         torch.cuda.set_device(rank)
         wl = syn.CONFIGS[WORKLOAD]
@@ -79,16 +83,17 @@ def _rank_main(rank, nranks, exchange, ids, results):
         results.put((rank, f"error: {e!r}", None))
 
 
-# "default": the copy-engine push where every rank can write a peer's flag by a
-# stream memory operation, else the epilogue's peer stores; "stagger" / "chunks1" /
-# "chunks5": the same push on one stream peer after peer / in 1 or 5 chunks per
+# "default": the copy-engine push (one stream, peers in reading order) where every
+# rank can write a peer's flag by a stream memory operation and a peer gets 12 MB or
+# more, else the epilogue's peer stores; "ce": the push for every size; "parallel" /
+# "chunks1" / "chunks5": the push on one stream per peer / in 1 or 5 chunks per
 # peer; "sm": forced epilogue stores + flag kernel; "nccl": forced all-gather.
-EXPECTED_MODE = {"default": ("direct-ce", "direct"), "stagger": ("direct-ce", "direct"),
-                 "chunks1": ("direct-ce", "direct"), "chunks5": ("direct-ce", "direct"),
-                 "sm": ("direct",), "nccl": ("nccl",)}
+EXPECTED_MODE = {"default": ("direct-ce", "direct"), "ce": ("direct-ce", "direct"),
+                 "parallel": ("direct-ce", "direct"), "chunks1": ("direct-ce", "direct"),
+                 "chunks5": ("direct-ce", "direct"), "sm": ("direct",), "nccl": ("nccl",)}
 
 
-@pytest.mark.parametrize("exchange", ["default", "stagger", "chunks1", "chunks5", "sm", "nccl"])
+@pytest.mark.parametrize("exchange", ["default", "ce", "parallel", "chunks1", "chunks5", "sm", "nccl"])
 @pytest.mark.parametrize("nranks", [2, 4, 8])
 def test_sharded_global_attention_matches_single_gpu(oracle_mod, nranks, exchange):
     if torch.cuda.device_count() < nranks:

@@ -187,7 +187,13 @@ struct va_ctx {
   // peer, or with push_stagger on one stream peer after peer, the peer that reads
   // this rank's rows first (rank - 1) first.  VA_PUSH_CHUNKS / VA_PUSH_ORDER.
   int push_chunks = 0;
-  bool push_stagger = false;
+  bool push_stagger = true;
+  // Copy engines carry a call's K'/V only from ce_min_peer_bytes per peer up: below
+  // that the QKV epilogue's peer stores win (measured on 8 B200s: 4 MB per peer,
+  // 0.160 vs 0.218 ms per S=12 sub-block; 16 MB at 2 GPUs: 0.327 vs 0.288 ms).
+  // VA_KV_EXCHANGE=ce forces copy engines for every size.
+  int64_t ce_min_peer_bytes = int64_t(12) << 20;
+  int last_xchg = 0;  // path of the last sharded call (va_last_exchange)
   // With the phase profile on: per-peer push times of the last sharded call
   // (events around each peer's copies).
   cudaEvent_t ce_t0[va::kMaxPeers] = {};
@@ -765,8 +771,10 @@ bool prepare_exchange(va_ctx* c, BranchSpec* b) {
     b->peer_rank[b->npeer] = r;
     ++b->npeer;
   }
-  b->ce = c->ce;
+  const int64_t peer_bytes = b->rows * c->cfg.embed_dim * 2 * static_cast<int64_t>(sizeof(__nv_bfloat16));
+  b->ce = c->ce && peer_bytes >= c->ce_min_peer_bytes;
   b->epoch = c->epoch;
+  c->last_xchg = b->ce ? 3 : 2;
   return true;
 }
 
@@ -830,6 +838,7 @@ int exchange_step(va_ctx* c, const BranchSpec& b, bool direct, cudaStream_t st) 
     pf.value = va::peer_flag_value(b.epoch, true, b.row_offset + b.rows);
     VA_CUDA(c, va::launch_peer_flags(pf, st));
   } else if (b.gather) {
+    c->last_xchg = 1;
     const int E = c->cfg.embed_dim;
     return gather_kv(c, c->k + b.row_offset * E, c->v + b.row_offset * E, b.rows, st);
   }
@@ -972,7 +981,9 @@ int va_create(const va_config* cfg, int device, va_ctx** out) {
     const char* pc = std::getenv("VA_PUSH_CHUNKS");
     if (pc && std::atoi(pc) >= 1 && std::atoi(pc) <= 16) c->push_chunks = std::atoi(pc);
     const char* po = std::getenv("VA_PUSH_ORDER");
-    if (po) c->push_stagger = std::string(po) == "stagger";
+    if (po) c->push_stagger = std::string(po) != "parallel";
+    const char* xe = std::getenv("VA_KV_EXCHANGE");
+    if (xe && std::string(xe) == "ce") c->ce_min_peer_bytes = 0;
   }
   {
     const size_t slots = static_cast<size_t>(va::flash_part_slots(c->sms));
@@ -2241,10 +2252,14 @@ int va_phase_times(va_ctx* c, float* ms_out) {
   return VA_OK;
 }
 
+int va_last_exchange(const va_ctx* c) { return c ? c->last_xchg : 0; }
+
 int va_exchange_times(va_ctx* c, float* ms_out, int* npeer_out, int64_t* bytes_per_peer) {
   if (!c || !ms_out || !npeer_out || !bytes_per_peer) return VA_ERR_INVALID;
-  if (!c->phase_valid || c->xchg_peers == 0)
-    return fail(c, VA_ERR_STATE, "no profiled copy-engine exchange since the profile was enabled");
+  if (!c->phase_valid) return fail(c, VA_ERR_STATE, "no profiled device-path call since the profile was enabled");
+  *npeer_out = 0;
+  *bytes_per_peer = 0;
+  if (c->xchg_peers == 0) return VA_OK;  // the last call pushed nothing by copy engines
   VA_CUDA(c, cudaSetDevice(c->device));
   for (int p = 0; p < c->xchg_peers; ++p) {
     VA_CUDA(c, cudaEventSynchronize(c->ce_t1[p]));

@@ -40,7 +40,7 @@ EXPORTED = [
     "va_block_attention_device", "va_op_attention_device", "va_flash_attention_bf16",
     "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
-    "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times", "va_exchange_times",
+    "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times", "va_exchange_times", "va_last_exchange",
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
     "va_load_vit_norm", "va_backbone_device", "va_backbone_device_sharded",
     "va_comm_unique_id", "va_comm_init", "va_comm_exchange_mode", "va_attention_device_sharded",
@@ -153,6 +153,7 @@ def load_library(path: str = LIB_PATH):
         "va_run_tail_host": ([_vp, c_int, _vp, i64, c_int, c_int, c_int, c_int, _vp], c_int),
         "va_phase_times": ([_vp, _vp], c_int),
         "va_exchange_times": ([_vp, _vp, _vp, _vp], c_int),
+        "va_last_exchange": ([_vp], c_int),
         "va_load_patch_embed": ([_vp, _vp, _vp, _vp, _vp, i64, _vp, c_int, c_int, c_float], c_int),
         "va_prepare_tokens_device": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp, _vp], c_int),
         "va_prepare_tokens_host": ([_vp, _vp, c_int, c_int, c_int, _vp, _vp], c_int),
@@ -471,6 +472,10 @@ class Context:
         ms = np.zeros(len(self.PHASES), np.float32)
         self.check(self.lib.va_phase_times(self.h, _ptr(ms)))
         return dict(zip(self.PHASES, (float(v) for v in ms)))
+
+    def last_exchange(self) -> str:
+        """The K'/V path the last sharded call took (names as exchange_mode)."""
+        return ("none", "nccl", "direct", "direct-ce")[self.lib.va_last_exchange(self.h)]
 
     def exchange_times(self):
         """Per-peer copy-engine push of the last profiled sharded call: (ms per peer,
