@@ -144,7 +144,8 @@ int va_op_attention_device(va_ctx* ctx, const float* q, const float* k, const fl
  * allocates nothing; its bf16 operand scratch is a fixed array of 12 MiB inside the
  * library, held on every GPU that loads it until exit.  All pointers are device
  * pointers: q, k, v, out [heads, n, 64] F32; norm vectors [64] or NULL; pos_yx_dev
- * [n, 2] F32 (rounded) or NULL; rope_pairing as in va_config.  Limit: heads * n * 64
+ * [n, 2] F32 (rounded half away from zero; each in [0, 65535], else VA_ERR_INVALID) or
+ * NULL; rope_pairing as in va_config.  Limit: heads * n * 64
  * <= 2,097,152, else VA_ERR_CAPACITY.  The first call on a device looks up the
  * scratch address with that device current and should come before any stream
  * capture.  Calls share the scratch: calls that overlap on the GPU race.  The call

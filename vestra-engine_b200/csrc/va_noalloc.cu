@@ -22,6 +22,11 @@
 //     cleared at the start of every call.
 //   * The call is synchronous: it waits for its stream and returns
 //     VA_ERR_DEVICE if a kernel gave up on a bounded wait.
+//   * RoPE positions are rounded half away from zero (f32::round, as the
+//     reference's cpu_backend.rs:291-292 and the context entry points) and must lie
+//     in [0, 65535] like theirs; a position outside that range makes the call
+//     return VA_ERR_INVALID (checked on the device, so nothing is copied to the host).
+#include <cmath>
 #include <mutex>
 
 #include "../../include/vestra_attn.h"
@@ -31,6 +36,12 @@
 namespace {
 
 constexpr size_t kNoAllocMaxElems = size_t(1) << 21;  // per operand (bf16 elements)
+constexpr int kBadPosition = va::kDevBadShape;        // error word: a position out of range
+
+// freq^(-2i/32), i < 16, computed on the host in double.
+struct InvFreq {
+  double v[16];
+};
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) __nv_bfloat16 g_noalloc_scratch[3 * kNoAllocMaxElems];
@@ -71,13 +82,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // [H][n][64] F32 -> optional per-row LayerNorm -> optional 2D RoPE -> token-major
-// bf16 [n][H*64].  Positions come from a device F32 [n][2] table (rounded, as in
-// cpu_backend.rs:291-292) and the rotation angles pos * freq^(-2i/32) are formed
-// here with sincosf, so the call needs no host-built table.
+// bf16 [n][H*64].  Positions come from a device F32 [n][2] table (rounded half away
+// from zero, as in cpu_backend.rs:291-292) and the rotation angles
+// pos * freq^(-2i/32) are formed here in double, like the context's host table, so
+// the call needs no host-built table.  A position outside [0, 65535] sets *err.
 __global__ void __launch_bounds__(256) noalloc_prep_kernel(
     const float* __restrict__ x, int rows_total, int n, const float* __restrict__ g,
-    const float* __restrict__ b, float eps, const float* __restrict__ pos_yx, float log2_freq,
-    int pairing, __nv_bfloat16* __restrict__ y) {
+    const float* __restrict__ b, float eps, const float* __restrict__ pos_yx, InvFreq inv_freq,
+    int pairing, __nv_bfloat16* __restrict__ y, int* err) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows_total) return;
@@ -93,7 +105,11 @@ __global__ void __launch_bounds__(256) noalloc_prep_kernel(
   const int heads = rows_total / n;
   const int h = row / n, t = row - h * n;
   if (pos_yx != nullptr) {
-    const float py = rintf(__ldg(pos_yx + 2 * t)), px = rintf(__ldg(pos_yx + 2 * t + 1));
+    const float py = roundf(__ldg(pos_yx + 2 * t)), px = roundf(__ldg(pos_yx + 2 * t + 1));
+    if (!(py >= 0.f && py <= 65535.f && px >= 0.f && px <= 65535.f)) {  // NaN fails too
+      if (lane == 0) atomicCAS(err, 0, kBadPosition);
+      return;
+    }
     const float sw0 = __shfl_xor_sync(0xffffffffu, a0, 8);  // rotate-half partner, channel c^16
     const float sw1 = __shfl_xor_sync(0xffffffffu, a1, 8);
     float out[2];
@@ -114,9 +130,9 @@ __global__ void __launch_bounds__(256) noalloc_prep_kernel(
         f = i >> 1;
         sgn = (e == 0) ? -1.f : 1.f;
       }
-      float s, co;
-      sincosf(p * exp2f(-(2.0f * f / 32.0f) * log2_freq), &s, &co);
-      out[e] = me * co + sgn * partner * s;
+      double s, co;
+      sincos(static_cast<double>(p) * inv_freq.v[f], &s, &co);
+      out[e] = me * static_cast<float>(co) + sgn * partner * static_cast<float>(s);
     }
     a0 = out[0];
     a1 = out[1];
@@ -148,14 +164,15 @@ extern "C" int va_op_attention_noalloc(const float* q, const float* k, const flo
   __nv_bfloat16* ks = sym.scratch + kNoAllocMaxElems;
   __nv_bfloat16* vs = sym.scratch + 2 * kNoAllocMaxElems;
   if (cudaMemsetAsync(sym.err, 0, sizeof(int), st) != cudaSuccess) return VA_ERR_CUDA;
-  const float log2_freq = pos_yx_dev ? log2f(freq) : 0.f;
+  InvFreq inv{};
+  for (int i = 0; i < 16; ++i) inv.v[i] = std::pow(static_cast<double>(freq), -2.0 * i / 32.0);
   const dim3 grid((rows + 7) / 8);
   noalloc_prep_kernel<<<grid, 256, 0, st>>>(q, rows, static_cast<int>(n), qn_g, qn_b, qk_norm_eps,
-                                            pos_yx_dev, log2_freq, rope_pairing, qs);
+                                            pos_yx_dev, inv, rope_pairing, qs, sym.err);
   noalloc_prep_kernel<<<grid, 256, 0, st>>>(k, rows, static_cast<int>(n), kn_g, kn_b, qk_norm_eps,
-                                            pos_yx_dev, log2_freq, rope_pairing, ks);
+                                            pos_yx_dev, inv, rope_pairing, ks, sym.err);
   noalloc_prep_kernel<<<grid, 256, 0, st>>>(v, rows, static_cast<int>(n), nullptr, nullptr, 0.f,
-                                            nullptr, 0.f, 0, vs);
+                                            nullptr, inv, 0, vs, sym.err);
   if (cudaGetLastError() != cudaSuccess) return VA_ERR_CUDA;
   va::FlashArgs fa{};
   fa.q_count = static_cast<int>(n);
@@ -172,5 +189,5 @@ extern "C" int va_op_attention_noalloc(const float* q, const float* k, const flo
   if (cudaMemcpyAsync(&h_err, sym.err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess)
     return VA_ERR_CUDA;
-  return h_err == 0 ? VA_OK : VA_ERR_DEVICE;
+  return h_err == 0 ? VA_OK : h_err == kBadPosition ? VA_ERR_INVALID : VA_ERR_DEVICE;
 }
