@@ -43,11 +43,11 @@ LAYER = 5           # a global block of the DA3-BASE schedule (alt_start 4: glob
 L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the default
 # fixed-offset attention kernel (flash_fwd_d64_ks_kernel<72, split, quadratic>) on
-# the cfg3 window at one GPU, from one ncu capture of that kernel (47.97 MB read:
-# Q + K + V once; 2.65 MB written, O mostly still in L2 when the launch ends).  Used
+# the cfg3 window at one GPU, from one ncu capture of that kernel (47.95 MB read:
+# Q + K + V once; 2.07 MB written, O mostly still in L2 when the launch ends).  Used
 # for the roofline's `traffic` at N = 1; a rank's launch at N > 1 reads the whole
 # key window but only its own queries, so the figure does not carry over.
-FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.62e6}
+FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.02e6}
 PARITY_ROWS = 256   # seeded output rows checked against the oracle at every N
 MAX_ABS, MIN_COS = 2e-2, 0.9999
 
@@ -63,6 +63,8 @@ def parse_args():
     ap.add_argument("--variants", action="store_true",
                     help="also time the attention kernel's exponential-split and f16-P variants")
     ap.add_argument("--no-large", action="store_true", help="skip the DA3-LARGE S=32 window section")
+    ap.add_argument("--ncu-case", choices=NCU_CASES, default=None,
+                    help="run one small case of a kernel family a few times and exit (for a profiler)")
     return ap.parse_args()
 
 
@@ -73,6 +75,82 @@ def cpu_threads():
         return len(os.sched_getaffinity(0))
     except AttributeError:
         return os.cpu_count() or 1
+
+
+NCU_CASES = ("subblock", "block", "fc2", "tokens", "capture", "gguf", "flash", "flash_slice8")
+
+
+def run_ncu_case(name):
+    """One small case of a kernel family on cuda:0 at the cfg3 shapes, run a few times
+    (the profiler skips the first launches): subblock / block (LN1, QKV, attention,
+    proj / + LN2, fc1, fc2), fc2 (the K3 GEMM at fc2's K = 3072), tokens (patchify +
+    patch projection), capture (two capture launches), gguf (device decoding of a
+    2-block Q8_0 file), flash (the default fixed-offset attention launch over the
+    window) and flash_slice8 (one rank's 1,299 queries of 8 against the window)."""
+    import numpy as np
+    import torch
+    import vestra_attn as va
+
+    wl = syn.CONFIGS["cfg3_s12_global"]
+    E = wl.embed
+    ctx = va.Context(va.default_config(max_rows=wl.rows, depth=12, rope_start=4, qknorm_start=4,
+                                       num_register=1), 0)
+    x = torch.from_numpy(syn.hidden_states(wl.rows, E, seed=0)).cuda()
+    if name in ("subblock", "block", "capture"):
+        for layer in (4, LAYER):
+            p = syn.layer_weights(E, seed=0, layer=layer, norm1=True, mlp=True)
+            ctx.load_layer(layer, p)
+            ctx.load_mlp(layer, p)
+        if name == "capture":
+            ctx.load_vit_norm(np.ones(E, np.float32), np.zeros(E, np.float32))
+            ctx.backbone_device(x.clone(), wl.gh, wl.gw, wl.views, 4, 6, 4, out_layers=(4, 5), cat_token=True)
+        else:
+            out = torch.empty_like(x)
+            for _ in range(3):
+                if name == "subblock":
+                    ctx.attention_device(LAYER, x, out, wl.gh, wl.gw, wl.views, True)
+                else:
+                    ctx.block_device(LAYER, x.clone(), wl.gh, wl.gw, wl.views, True)
+    elif name == "fc2":
+        h = torch.randn(wl.rows, 4 * E, device="cuda").to(torch.bfloat16)
+        w = (0.02 * torch.randn(E, 4 * E, device="cuda")).to(torch.bfloat16)
+        out = torch.empty(wl.rows, E, device="cuda")
+        for _ in range(3):
+            ctx.linear_bf16(h, w, out, bias=torch.zeros(E, device="cuda"), residual=x)
+    elif name == "tokens":
+        pw = syn.patch_embed_weights(E, 14, 37, 1, seed=0)
+        ctx.load_patch_embed(pw["weight"], pw["bias"], pw["cls"], pw["pos_embed"], pw["registers"], 14)
+        imgs = torch.from_numpy(syn.images(wl.views, wl.gh * 14, wl.gw * 14, seed=0)).cuda()
+        tk = torch.empty(wl.rows, E, device="cuda")
+        for _ in range(3):
+            ctx.prepare_tokens_device(imgs, wl.views, wl.gh * 14, wl.gw * 14, tk)
+    elif name == "gguf":
+        data = syn.gguf_model(embed=E, depth=2, heads=wl.heads, grid=37, dtype="q8_0", seed=0)
+        with tempfile.TemporaryDirectory() as d:
+            path = os.path.join(d, "m.gguf")
+            with open(path, "wb") as f:
+                f.write(data)
+            with va.GgufFile(path) as g:
+                c2 = va.Context(va.default_config(embed_dim=E, num_heads=wl.heads, depth=2, max_rows=1024), 0)
+                c2.load_gguf(g)
+                c2.close()
+    else:
+        g = torch.Generator(device="cuda").manual_seed(0)
+
+        def hn(t):
+            return torch.nn.functional.layer_norm(t.view(t.shape[0], wl.heads, 64), (64,)).view(t.shape[0], -1)
+
+        local = wl.rows if name == "flash" else wl.rows // 8
+        q = hn(torch.randn(local, E, device="cuda", generator=g)).to(torch.bfloat16)
+        k = hn(torch.randn(wl.rows, E, device="cuda", generator=g)).to(torch.bfloat16)
+        v = torch.randn(wl.rows, E, device="cuda", generator=g).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        for _ in range(3):
+            ctx.flash_bf16(q, k, v, wl.heads, o, q_offset=wl.rows - local, variant=511)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    ctx.close()
+    return 0
 
 
 def dist_env():
@@ -898,6 +976,8 @@ def main():
     sys.stdout.flush()
     JSON_OUT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
+    if args.ncu_case:
+        return run_ncu_case(args.ncu_case)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
