@@ -44,10 +44,11 @@ L2_FLUSH_BYTES = 256 << 20
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the default
 # fixed-offset attention kernel (flash_fwd_d64_ks_kernel<72, split, quadratic>) on
 # the cfg3 window at one GPU, from one ncu capture of that kernel (47.95 MB read:
-# Q + K + V once; 2.07 MB written, O mostly still in L2 when the launch ends).  Used
+# Q + K + V once; 2.87 MB written, O mostly still in L2 when the launch ends; the
+# capture is `ncu ... -k regex:flash_fwd_d64_ks python bench.py --ncu-case flash`).  Used
 # for the roofline's `traffic` at N = 1; a rank's launch at N > 1 reads the whole
 # key window but only its own queries, so the figure does not carry over.
-FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.02e6}
+FLASH_DRAM_BYTES_PER_LAUNCH = {"cfg3_s12_global": 50.82e6}
 PARITY_ROWS = 256   # seeded output rows checked against the oracle at every N
 MAX_ABS, MIN_COS = 2e-2, 0.9999
 
