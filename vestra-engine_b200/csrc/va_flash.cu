@@ -201,6 +201,10 @@ struct Ctl {
   __device__ volatile int* merge_flag(int t) const {
     return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 24 + 4 * t);
   }
+  // Key-split form 13: 1 once query tile 0's softmax has loaded its first S.
+  __device__ volatile int* tile_go() const {
+    return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 32);
+  }
   __device__ uint32_t sQ(int t) const { return base + FlashSmem::kQ + t * kTileBytes; }
   __device__ uint32_t sK(int s) const { return base + FlashSmem::kK + s * kTileBytes; }
   __device__ uint32_t sV(int s) const { return base + FlashSmem::kV + s * kTileBytes; }
@@ -245,6 +249,7 @@ __device__ __forceinline__ uint32_t cta_setup(const Ctl& c, const Geom& g, int s
     *c.kv_consumed() = 0;
     *c.mma_done(0) = 0;
     *c.mma_done(1) = 0;
+    *c.tile_go() = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -366,7 +371,10 @@ __device__ __forceinline__ void run_producer(const Ctl& c, const Geom& g, const 
 // kSplitP: P arrives in two halves of 64 keys (p_full, then p_full_hi) and PV runs as
 // two groups of 4 UMMAs committed separately (pv_done, pv_done_hi), so the PV of the
 // first half overlaps the exponentials of the second.
-template <bool kF16, bool kSplitP = false>
+// kStagger: tile 1 issues its first QK only once tile 0's softmax has loaded S_0(0),
+// so the two tiles start out of phase (a one-time offset; the kernel does not hold
+// them apart afterwards).
+template <bool kF16, bool kSplitP = false, bool kStagger = false>
 __device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32_t tmem, int t,
                                              int* err) {
   constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
@@ -393,6 +401,22 @@ __device__ __forceinline__ void run_mma_tile(const Ctl& c, const Geom& g, uint32
     return r;
   };
   bool ok = mbar_wait(c.q_full(), 0, abort_flag, err, kDevTimeoutMma);
+  if (kStagger && ok && t == 1) {
+    const unsigned long long t0 = globaltimer_ns();
+    while (*c.tile_go() == 0) {
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        report_error(err, kDevTimeoutMma);
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
   if (ok) ok = qk(0);
   if (ok && g.num_kv > 1) ok = qk(1);
   for (int j = 0; ok && j < g.num_kv; ++j) {
@@ -1168,7 +1192,7 @@ __device__ __forceinline__ uint64_t exp2_fma_pair(uint64_t s2, uint64_t c2) {
 // waits for its UMMAs, P store and next S.
 template <int K0, int NK, bool kFma, bool kQuad, bool kTurns>
 __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uint32_t tS, uint32_t tP,
-                                         uint64_t sc2, float& l, int* err) {
+                                         uint64_t sc2, float& l, int* err, bool signal = false) {
   volatile int* abort_flag = c.abort_flag();
   for (int j = 0; j < g.num_kv; ++j) {
     bool ok = mbar_wait(c.s_full(t), j & 1, abort_flag, err, kDevTimeoutConsumer);
@@ -1179,6 +1203,7 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
     tmem_ld_cols<NK>(tS + K0, s);
     tc_fence_before();
     mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
+    if (signal && j == 0) *c.tile_go() = 1;
     if (kTurns && g.nq == 2 && (t == 1 || j > 0)) {
       ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
                      kDevTimeoutConsumer);
@@ -1238,7 +1263,7 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
   return true;
 }
 
-template <int KA, bool kSplit, bool kQuad, bool kTurns>
+template <int KA, bool kSplit, bool kQuad, bool kTurns, bool kStagger = false>
 __global__ void __launch_bounds__(kW20Threads, 1)
     flash_fwd_d64_ks_kernel(const __grid_constant__ CUtensorMap map_q,
                             const __grid_constant__ CUtensorMap map_k,
@@ -1255,7 +1280,7 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     if (warp == 0) {
       if (lane == 0) run_producer(c, g, fa, &map_q, &map_k, &map_v, err);
     } else if (warp < 3) {
-      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false>(c, g, tmem, warp - 1, err);
+      if (lane == 0 && warp - 1 < g.nq) run_mma_tile<false, false, kStagger>(c, g, tmem, warp - 1, err);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kW20HighRegs));
@@ -1273,7 +1298,9 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     float* red = reinterpret_cast<float*>(c.smem + FlashSmem::kRed);
     if (t < g.nq) {
       float l = 0.f;
-      bool ok = role == 0 ? ks_steps<0, KA, false, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err)
+      // Tile 0's first softmax thread lets tile 1's issuer start (form 13).
+      const bool signal = kStagger && t == 0 && role == 0 && quad == 0 && lane == 0;
+      bool ok = role == 0 ? ks_steps<0, KA, false, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err, signal)
                           : ks_steps<KA, kTileK - KA, true, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err);
       bool fin = ok && mbar_wait(c.o_final(t), 0, c.abort_flag(), err, kDevTimeoutConsumer);
       fin = __all_sync(0xffffffffu, fin);
@@ -1364,6 +1391,501 @@ __global__ void __launch_bounds__(kW20Threads, 1)
   cta_teardown(c, tmem);
 }
 
+// ============================================================== persistent key split
+// Form 14: the key-split softmax of form 10 in a persistent launch.  One CTA per SM
+// walks the work items w = blockIdx.x, + gridDim.x, ... (global: the units and split
+// pieces of the launch plan above; local: (segment, head, query pair)), with TMEM,
+// barriers and tensor maps set up once.  Q is double-buffered by item, every barrier
+// phase is counted over the whole walk (G = key tiles processed so far), and the
+// UMMA issuers keep issuing QK two tiles ahead across item boundaries, so the next
+// item's first scores are computed while this item's last P·V and its epilogue run.
+// Both query tiles of an item are always computed (rows past the item's queries are
+// computed and not stored), which keeps every role's control flow the same for all
+// items.  A tile's O is read out of TMEM by its softmax warps before the next item's
+// first P·V (o_free), and the row-sum exchange uses a buffer per item parity.
+constexpr int kPLowRegs = 32;
+constexpr int kPHighRegs = 112;
+static_assert(128 * kPLowRegs + 512 * kPHighRegs <= 640 * 96, "register split of the persistent layout");
+struct PSmem {
+  static constexpr uint32_t kQ = 0;                              // Q[item parity][tile]
+  static constexpr uint32_t kK = 4 * kTileBytes;                 // K ring
+  static constexpr uint32_t kV = kK + kStages * kTileBytes;      // V ring
+  static constexpr uint32_t kBar = kV + kStages * kTileBytes;
+  // q_full[2], q_empty[2], kv_full[S], kv_empty[S], then per tile s_full, s_free,
+  // p_full, pv_done, o_final, o_free
+  static constexpr uint32_t kNumBars = 4 + 2 * kStages + 12;
+  static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
+  static constexpr uint32_t kRed = kMisc + 64;                   // [2 items][2 tiles][2 roles][128] F32
+  static constexpr uint32_t kBytes = kRed + 2 * 2 * 2 * 128 * 4;
+  static constexpr uint32_t kLaunchBytes = kBytes + 1024;
+};
+
+struct PCtl {
+  uint32_t base;
+  uint8_t* smem;
+  __device__ uint32_t bar(int i) const { return base + PSmem::kBar + 8u * i; }
+  __device__ uint32_t q_full(int b) const { return bar(b); }
+  __device__ uint32_t q_empty(int b) const { return bar(2 + b); }
+  __device__ uint32_t kv_full(int s) const { return bar(4 + s); }
+  __device__ uint32_t kv_empty(int s) const { return bar(4 + kStages + s); }
+  __device__ uint32_t s_full(int t) const { return bar(4 + 2 * kStages + t); }
+  __device__ uint32_t s_free(int t) const { return bar(6 + 2 * kStages + t); }
+  __device__ uint32_t p_full(int t) const { return bar(8 + 2 * kStages + t); }
+  __device__ uint32_t pv_done(int t) const { return bar(10 + 2 * kStages + t); }
+  __device__ uint32_t o_final(int t) const { return bar(12 + 2 * kStages + t); }
+  __device__ uint32_t o_free(int t) const { return bar(14 + 2 * kStages + t); }
+  __device__ volatile int* misc(int i) const {
+    return reinterpret_cast<volatile int*>(smem + PSmem::kMisc + 4 * i);
+  }
+  __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(smem + PSmem::kMisc); }
+  __device__ volatile int* abort_flag() const { return misc(1); }
+  __device__ volatile int* kv_issued() const { return misc(2); }    // K/V tiles loaded so far
+  __device__ volatile int* kv_consumed() const { return misc(3); }  // K/V tiles seen by issuer 0
+  __device__ volatile int* q_issued() const { return misc(4); }     // items whose Q was loaded
+  __device__ volatile int* q_consumed() const { return misc(5); }   // items whose Q issuer 0 saw
+  __device__ volatile int* o_commits(int t) const { return misc(6 + t); }
+  __device__ volatile int* merge_flag(int t) const { return misc(8 + t); }
+  __device__ float* red(int i, int t, int role) const {
+    return reinterpret_cast<float*>(smem + PSmem::kRed) + (((i & 1) * 2 + t) * 2 + role) * kTileQ;
+  }
+  __device__ uint32_t sQ(int b, int t) const { return base + PSmem::kQ + (2 * b + t) * kTileBytes; }
+  __device__ uint32_t sK(int s) const { return base + PSmem::kK + s * kTileBytes; }
+  __device__ uint32_t sV(int s) const { return base + PSmem::kV + s * kTileBytes; }
+};
+
+__device__ __forceinline__ PCtl make_pctl() {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  PCtl c;
+  c.base = (raw_u32 + 1023u) & ~1023u;
+  c.smem = smem_raw + (c.base - raw_u32);
+  return c;
+}
+
+// Work item w of a persistent launch (see make_geom for the non-persistent form).
+__device__ __forceinline__ Geom geom_item(const FlashArgs& fa, int w, SplitPos* spo) {
+  Geom g;
+  SplitPos sp{w, 0, 1, 0};
+  if (fa.seg_len == 0) {
+    const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
+    if (w >= fa.n_full) {
+      const int r = w - fa.n_full;
+      sp.unit = fa.n_full + r / fa.splits;
+      sp.split = r % fa.splits;
+      sp.nsplit = fa.splits;
+      sp.tail_unit = sp.unit - fa.n_full;
+    }
+    g.head = sp.unit / qpairs;
+    g.q0 = (sp.unit % qpairs) * 2 * kTileQ;
+    g.q_end = fa.q_count;
+    const int total = (fa.kv_rows + kTileK - 1) / kTileK;
+    const int t0 = sp.split * total / sp.nsplit, t1 = (sp.split + 1) * total / sp.nsplit;
+    g.k0 = t0 * kTileK;
+    g.last_valid = min(fa.kv_rows, t1 * kTileK) - (t1 - 1) * kTileK;
+    g.num_kv = t1 - t0;
+    const int own_tile = (fa.own_begin + kTileK - 1) / kTileK;
+    g.rot = (fa.peer_flags && own_tile > t0 && own_tile < t1) ? own_tile - t0 : 0;
+    g.tail_iter = g.num_kv - 1 - g.rot;
+  } else {
+    const int qps = (fa.seg_len + 2 * kTileQ - 1) / (2 * kTileQ);
+    const int qp = w % qps;
+    g.head = (w / qps) % fa.heads;
+    const int seg = w / (qps * fa.heads);
+    const int q_seg0 = seg * fa.seg_len;
+    g.q_end = q_seg0 + fa.seg_len;
+    g.q0 = q_seg0 + qp * 2 * kTileQ;
+    g.k0 = fa.q_offset + q_seg0;
+    g.num_kv = (fa.seg_len + kTileK - 1) / kTileK;
+    g.last_valid = fa.seg_len - (g.num_kv - 1) * kTileK;
+    g.rot = 0;
+    g.tail_iter = g.num_kv - 1;
+  }
+  g.nq = 2;
+  g.col = g.head * kHeadDim;
+  if (spo) *spo = sp;
+  return g;
+}
+
+// The QK cursor of an issuer: the next key tile to multiply, possibly in a later item.
+struct QkCursor {
+  int i;       // item index of this CTA's walk
+  int j;       // key tile within the item
+  int num_kv;  // key tiles of the item (0: past the last item)
+};
+
+__device__ __forceinline__ void cursor_item(const FlashArgs& fa, QkCursor& q) {
+  const int w = blockIdx.x + q.i * gridDim.x;
+  q.num_kv = w < fa.items ? geom_item(fa, w, nullptr).num_kv : 0;
+}
+
+// Producer of the persistent walk (one thread): per item, Q into buffer i & 1 once
+// the issuers are done with item i - 2's Q, then the item's K/V tiles into the ring.
+__device__ __forceinline__ void prun_producer(const PCtl& c, const FlashArgs& fa, const CUtensorMap* mq,
+                                              const CUtensorMap* mk, const CUtensorMap* mv, int* err) {
+  volatile int* abort_flag = c.abort_flag();
+  int gj = 0;
+  for (int i = 0;; ++i) {
+    const int w = blockIdx.x + i * gridDim.x;
+    if (w >= fa.items) break;
+    const Geom g = geom_item(fa, w, nullptr);
+    const int b = i & 1;
+    if (i >= 2 && !mbar_wait(c.q_empty(b), ((i >> 1) - 1) & 1, abort_flag, err, kDevTimeoutProducer)) return;
+    mbar_arrive_expect_tx(c.q_full(b), 2 * kTileBytes);
+    tma_load_2d(c.sQ(b, 0), mq, c.q_full(b), g.col, g.q0);
+    // Tile 1 of an item whose queries end inside tile 0 loads tile 0's rows again
+    // (its results are computed and not stored); every box starts inside the tensor.
+    tma_load_2d(c.sQ(b, 1), mq, c.q_full(b), g.col, g.q0 + kTileQ < fa.q_count ? g.q0 + kTileQ : g.q0);
+    *c.q_issued() = i + 1;
+    PeerCover pc{fa.rank + 1 == fa.nranks ? 0 : fa.rank + 1, 0};
+    for (int j = 0; j < g.num_kv; ++j, ++gj) {
+      const int s = gj % kStages;
+      const uint32_t ph = (gj / kStages) & 1;
+      const int row = g.k0 + ((j + g.rot) % g.num_kv) * kTileK;
+      if (fa.peer_flags) {
+        const int need = tile_need(fa, row, min(row + kTileK, fa.kv_rows));
+        if (need > pc.covered && !wait_cover(fa, pc, need, abort_flag, err)) return;
+      }
+      if (!mbar_wait(c.kv_empty(s), ph ^ 1, abort_flag, err, kDevTimeoutProducer)) return;
+      mbar_arrive_expect_tx(c.kv_full(s), 2 * kTileBytes);
+      tma_load_2d(c.sK(s), mk, c.kv_full(s), g.col, row);
+      tma_load_2d(c.sV(s), mv, c.kv_full(s), g.col, row);
+      *c.kv_issued() = gj + 1;
+    }
+  }
+}
+
+// UMMA issuer of query tile t for the persistent walk.  PV runs over the key tiles
+// G = 0, 1, ... of all items in order; QK is issued two tiles ahead of PV, across
+// item boundaries (the next item's Q buffer, waited for at its first tile).
+__device__ __forceinline__ void prun_mma(const PCtl& c, const FlashArgs& fa, uint32_t tmem, int t, int* err) {
+  constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileQ, kHeadDim, false, true);
+  constexpr uint64_t kStageStep = kTileBytes >> 4;
+  volatile int* abort_flag = c.abort_flag();
+  const uint64_t dq0 = sdesc_sw128(c.sQ(0, t), 16, 1024);
+  const uint64_t dq1 = sdesc_sw128(c.sQ(1, t), 16, 1024);
+  const uint64_t dk0 = sdesc_sw128(c.sK(0), 16, 1024);
+  const uint64_t dv0 = sdesc_sw128(c.sV(0), 8192, 1024);
+  const uint32_t tS = tmem + col_s(t), tP = tmem + col_p(t), tO = tmem + col_o(t);
+  QkCursor cq{0, 0, 0};
+  cursor_item(fa, cq);
+  int gq = 0;  // cumulative index of the next QK
+  auto qk_next = [&]() -> bool {
+    if (cq.num_kv == 0) return true;  // past the last item
+    if (cq.j == 0) {
+      if (!mbar_wait(c.q_full(cq.i & 1), (cq.i >> 1) & 1, abort_flag, err, kDevTimeoutMma)) return false;
+      if (t == 0) *c.q_consumed() = cq.i + 1;
+    }
+    const int s = gq % kStages;
+    if (!mbar_wait(c.kv_full(s), (gq / kStages) & 1, abort_flag, err, kDevTimeoutMma)) return false;
+    if (t == 0) *c.kv_consumed() = gq + 1;
+    if (gq > 0 && !mbar_wait(c.s_free(t), (gq - 1) & 1, abort_flag, err, kDevTimeoutMma)) return false;
+    tc_fence_after();
+    umma_ss_k64(tS, (cq.i & 1) ? dq1 : dq0, dk0 + s * kStageStep, idesc_qk, 0u);
+    tc_commit(c.s_full(t));
+    ++gq;
+    if (++cq.j == cq.num_kv) {
+      ++cq.i;
+      cq.j = 0;
+      cursor_item(fa, cq);
+    }
+    return true;
+  };
+  bool ok = qk_next() && qk_next();
+  int G = 0;
+  for (int i = 0; ok; ++i) {
+    const int w = blockIdx.x + i * gridDim.x;
+    if (w >= fa.items) break;
+    const int num_kv = geom_item(fa, w, nullptr).num_kv;
+    for (int j = 0; ok && j < num_kv; ++j, ++G) {
+      ok = mbar_wait(c.p_full(t), G & 1, abort_flag, err, kDevTimeoutMma);
+      if (ok && j == 0 && i > 0) ok = mbar_wait(c.o_free(t), (i - 1) & 1, abort_flag, err, kDevTimeoutMma);
+      if (!ok) break;
+      tc_fence_after();
+      umma_ts_k128_mn(tO, tP, dv0 + (G % kStages) * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
+      tc_commit(c.pv_done(t));
+      tc_commit(c.kv_empty(G % kStages));
+      if (j + 1 == num_kv) {
+        tc_commit(c.o_final(t));
+        tc_commit(c.q_empty(i & 1));
+        *c.o_commits(t) = *c.o_commits(t) + 1;
+      }
+      ok = qk_next();
+    }
+  }
+  if (!ok) {
+    // Abort: one more commit marks the completion of every UMMA issued, which the
+    // teardown waits for before it frees TMEM.
+    tc_commit(c.o_final(t));
+    *c.o_commits(t) = *c.o_commits(t) + 1;
+  }
+}
+
+// One softmax thread's key range [K0, K0 + NK) of its row of tile t, over the
+// whole walk; after each item, the row's O half is read, normalised and stored
+// (or published for the split-tail merge).
+template <int K0, int NK, bool kFma, bool kQuad>
+__device__ __forceinline__ void prun_softmax(const PCtl& c, const FlashArgs& fa, int t, int role, int r,
+                                             int sw, int lane, uint32_t tS, uint32_t tP, uint32_t tO,
+                                             uint64_t sc2, int* err) {
+  volatile int* abort_flag = c.abort_flag();
+  int G = 0;
+  for (int i = 0;; ++i) {
+    const int w = blockIdx.x + i * gridDim.x;
+    if (w >= fa.items) break;
+    int num_kv, tail_iter, last_valid;
+    {
+      const Geom g0 = geom_item(fa, w, nullptr);
+      num_kv = g0.num_kv;
+      tail_iter = g0.tail_iter;
+      last_valid = g0.last_valid;
+    }
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < num_kv; ++j, ++G) {
+      ok = mbar_wait(c.s_full(t), G & 1, abort_flag, err, kDevTimeoutConsumer);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      // S in two chunks of columns, so that only one chunk of scores is live beside
+      // the packed probabilities (the persistent walk keeps more state in registers).
+      constexpr int C1 = ((NK / 2 + 7) / 8) * 8, C2 = NK - C1;
+      uint32_t pk[NK / 2];
+      uint64_t acc[2];
+      const bool tail = j == tail_iter && last_valid < K0 + NK;
+      auto chunk = [&](auto off_c, auto len_c, const float* sc, auto masked_c) {
+        constexpr int OFF = decltype(off_c)::value, LEN = decltype(len_c)::value;
+        constexpr bool kMasked = decltype(masked_c)::value;
+        const int valid = last_valid - K0 - OFF;
+#pragma unroll
+        for (int q = 0; q < LEN / 2; ++q) {
+          const uint64_t s2 = f32x2_pack(sc[2 * q], sc[2 * q + 1]);
+          float p0, p1;
+          if constexpr (kFma) {
+            f32x2_unpack(exp2_fma_pair<kQuad>(s2, sc2), p0, p1);
+          } else {
+            float x0, x1;
+            f32x2_unpack(f32x2_mul(s2, sc2), x0, x1);
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          if constexpr (kMasked) {
+            p0 = 2 * q < valid ? p0 : 0.0f;
+            p1 = 2 * q + 1 < valid ? p1 : 0.0f;
+          }
+          const uint64_t pp = f32x2_pack(p0, p1);
+          constexpr int kq0 = OFF / 2;
+          acc[(kq0 + q) & 1] = (kq0 + q) < 2 ? pp : f32x2_add(acc[(kq0 + q) & 1], pp);
+          pk[kq0 + q] = pack_bf16x2(p0, p1);
+        }
+      };
+      {
+        float sc[C1];
+        tmem_ld_cols<C1>(tS + K0, sc);
+        if (tail)
+          chunk(std::integral_constant<int, 0>{}, std::integral_constant<int, C1>{}, sc, std::true_type{});
+        else
+          chunk(std::integral_constant<int, 0>{}, std::integral_constant<int, C1>{}, sc, std::false_type{});
+      }
+      {
+        float sc[C2];
+        tmem_ld_cols<C2>(tS + K0 + C1, sc);
+        tc_fence_before();
+        mbar_arrive(c.s_free(t));  // every column of S_t is in registers
+        if (tail)
+          chunk(std::integral_constant<int, C1>{}, std::integral_constant<int, C2>{}, sc, std::true_type{});
+        else
+          chunk(std::integral_constant<int, C1>{}, std::integral_constant<int, C2>{}, sc, std::false_type{});
+      }
+      if (G > 0) {
+        ok = mbar_wait(c.pv_done(t), (G - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      tmem_st_cols<NK / 2>(tP + K0 / 2, pk);
+      tmem_wait_st();
+      float a0, a1, b0, b1;
+      f32x2_unpack(acc[0], a0, a1);
+      f32x2_unpack(acc[1], b0, b1);
+      l += (a0 + a1) + (b0 + b1);
+      tc_fence_before();
+      mbar_arrive(c.p_full(t));
+    }
+    bool fin = ok && mbar_wait(c.o_final(t), i & 1, abort_flag, err, kDevTimeoutConsumer);
+    fin = __all_sync(0xffffffffu, fin);
+    SplitPos sp;
+    const Geom g = geom_item(fa, w, &sp);
+    float o[32];
+    if (fin) {
+      tc_fence_after();
+      tmem_ld32(tO + 32 * role, o);
+    }
+    tc_fence_before();
+    mbar_arrive(c.o_free(t));  // the next item's first P·V may overwrite O_t
+    c.red(i, t, role)[r] = l;
+    named_bar_sync(1 + t, 256);
+    l += c.red(i, t, role ^ 1)[r];
+    if (sp.nsplit > 1) {
+      const int slot = (sp.tail_unit * sp.nsplit + sp.split) * 2 + t;
+      if (fin) {
+        float4* po = reinterpret_cast<float4*>(fa.part_o + (static_cast<size_t>(slot) * kTileQ + r) * kHeadDim +
+                                               32 * role);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) po[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+        if (role == 0)
+          reinterpret_cast<float2*>(fa.part_ml + static_cast<size_t>(slot) * kTileQ * 2)[r] = make_float2(0.f, l);
+      }
+      __threadfence();
+      named_bar_sync(1 + t, 256);
+      if (sw == 8 * t && lane == 0) {
+        const int old = atomicAdd(fa.counters + sp.tail_unit * 2 + t, 1);
+        const bool last = old == sp.nsplit - 1;
+        if (last) atomicExch(fa.counters + sp.tail_unit * 2 + t, 0);
+        *c.merge_flag(t) = last ? 1 : 0;
+      }
+      named_bar_sync(1 + t, 256);
+      if (*c.merge_flag(t) == 0) {
+        fin = false;
+      } else if (fin) {
+        __threadfence();
+        float mx = -INFINITY;
+        for (int q = 0; q < sp.nsplit; ++q) {
+          const int sl = (sp.tail_unit * sp.nsplit + q) * 2 + t;
+          mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r).x);
+        }
+        l = 0.f;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) o[q] = 0.f;
+        for (int q = 0; q < sp.nsplit; ++q) {
+          const int sl = (sp.tail_unit * sp.nsplit + q) * 2 + t;
+          const float2 a = __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r);
+          const float wq = ex2(a.x - mx);
+          l += wq * a.y;
+          const float4* po = reinterpret_cast<const float4*>(
+              fa.part_o + (static_cast<size_t>(sl) * kTileQ + r) * kHeadDim + 32 * role);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 u = __ldcg(po + e);
+            o[4 * e] += wq * u.x;
+            o[4 * e + 1] += wq * u.y;
+            o[4 * e + 2] += wq * u.z;
+            o[4 * e + 3] += wq * u.w;
+          }
+        }
+      }
+    }
+    const int token = g.q0 + t * kTileQ + r;
+    if (fin && token < g.q_end) {
+      const float inv = 1.0f / l;
+      if (fa.out_mode == 0) {
+        uint4* d = reinterpret_cast<uint4*>(fa.o_tok + static_cast<size_t>(token) * fa.embed + g.col + 32 * role);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          d[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
+                            pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                            pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                            pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+      } else {
+        float4* d = reinterpret_cast<float4*>(
+            fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim + 32 * role);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          d[q] = make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv, o[4 * q + 3] * inv);
+      }
+    }
+    if (!ok || !fin) {
+      if (*abort_flag) return;
+    }
+  }
+}
+
+template <int KA, bool kQuad>
+__global__ void __launch_bounds__(kW20Threads, 1)
+    flash_fwd_d64_ksp_kernel(const __grid_constant__ CUtensorMap map_q,
+                             const __grid_constant__ CUtensorMap map_k,
+                             const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  static_assert(KA % 8 == 0 && KA >= 8 && KA <= kTileK - 8, "key split");
+  const PCtl c = make_pctl();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(c.q_full(b), 1);
+      mbar_init(c.q_empty(b), 2);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(c.kv_full(s), 1);
+      mbar_init(c.kv_empty(s), 2);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(c.s_full(t), 1);
+      mbar_init(c.s_free(t), 256);
+      mbar_init(c.p_full(t), 256);
+      mbar_init(c.pv_done(t), 1);
+      mbar_init(c.o_final(t), 1);
+      mbar_init(c.o_free(t), 256);
+    }
+    for (int i = 1; i < 16; ++i) *c.misc(i) = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(c.tmem_slot()), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *c.tmem_slot();
+
+  // 128 x 32 + 512 x 112 = 61,440 registers: the launch's 640 x 96.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPLowRegs));
+    if (warp == 0) {
+      if (lane == 0) prun_producer(c, fa, &map_q, &map_k, &map_v, err);
+    } else if (warp < 3) {
+      if (lane == 0) prun_mma(c, fa, tmem, warp - 1, err);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPHighRegs));
+    const int sw = warp - 4;
+    const int t = sw >> 3;
+    const int role = (sw >> 2) & 1;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint64_t sc2 = f32x2_pack(fa.scale_log2, fa.scale_log2);
+    const uint32_t tS = tmem + lane_off + col_s(t), tP = tmem + lane_off + col_p(t),
+                   tO = tmem + lane_off + col_o(t);
+    if (role == 0)
+      prun_softmax<0, KA, false, kQuad>(c, fa, t, role, r, sw, lane, tS, tP, tO, sc2, err);
+    else
+      prun_softmax<KA, kTileK - KA, true, kQuad>(c, fa, t, role, r, sw, lane, tS, tP, tO, sc2, err);
+  }
+
+  // Teardown: after an abort, wait (bounded) for the copies and UMMAs still in flight,
+  // then free TMEM.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *c.abort_flag()) {
+    for (int q = *c.q_consumed(); q < *c.q_issued(); ++q) drain(c.q_full(q & 1), (q >> 1) & 1);
+    for (int j = *c.kv_consumed(); j < *c.kv_issued(); ++j) drain(c.kv_full(j % kStages), (j / kStages) & 1);
+    for (int t = 0; t < 2; ++t)
+      if (*c.o_commits(t) > 0) drain(c.o_final(t), (*c.o_commits(t) - 1) & 1);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
@@ -1420,24 +1942,32 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
   // form 9..12: key split (fixed exponent offset only), KA = 64 + 8 * poly MUFU
   // keys; the FMA-pipe exp2 by the cubic (9, 11) or the quadratic (10, 12); in
   // forms 11 and 12 the two query tiles take turns in the exponential section.
-#define VA_KS(KA, Q, T) {flash_fwd_d64_ks_kernel<KA, false, Q, T>, flash_fwd_d64_ks_kernel<KA, true, Q, T>}
-#define VA_KS_FORM(Q, T) {VA_KS(64, Q, T), VA_KS(72, Q, T), VA_KS(80, Q, T), VA_KS(88, Q, T), VA_KS(96, Q, T)}
-  static const Kern ks[4][5][2] = {VA_KS_FORM(false, false), VA_KS_FORM(true, false), VA_KS_FORM(false, true),
-                                   VA_KS_FORM(true, true)};
+#define VA_KS(KA, Q, T, O) {flash_fwd_d64_ks_kernel<KA, false, Q, T, O>, flash_fwd_d64_ks_kernel<KA, true, Q, T, O>}
+#define VA_KS_FORM(Q, T, O) {VA_KS(64, Q, T, O), VA_KS(72, Q, T, O), VA_KS(80, Q, T, O), VA_KS(88, Q, T, O), VA_KS(96, Q, T, O)}
+  // form 13: form 10 with the one-time start offset between the query tiles.
+  static const Kern ks[5][5][2] = {VA_KS_FORM(false, false, false), VA_KS_FORM(true, false, false),
+                                   VA_KS_FORM(false, true, false), VA_KS_FORM(true, true, false),
+                                   VA_KS_FORM(true, false, true)};
 #undef VA_KS_FORM
 #undef VA_KS
+  // form 14: the persistent key split (quadratic), KA = 64 + 8 * poly.
+  static const Kern ksp[5] = {flash_fwd_d64_ksp_kernel<64, true>, flash_fwd_d64_ksp_kernel<72, true>,
+                              flash_fwd_d64_ksp_kernel<80, true>, flash_fwd_d64_ksp_kernel<88, true>,
+                              flash_fwd_d64_ksp_kernel<96, true>};
+  bool persistent = false;
   Kern kern;
   int threads = kRowsThreads;
   bool w20_kernel = false, no_split = false;
   if (fa.poly_per8 < 0) fa.poly_per8 = fa.fixed_offset && !fa.v_f16 ? kDefaultKeySplit : kDefaultPolyPer8;
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (form >= 9 && form <= 12) {
+    if (form >= 9 && form <= 14) {
       if (poly > 4 || !fa.fixed_offset) return cudaErrorInvalidValue;
     } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
       return cudaErrorInvalidValue;
     }
-    w20_kernel = form == 3 || (form >= 5 && form <= 12);
+    w20_kernel = form == 3 || (form >= 5 && form <= 14);
+    persistent = form == 14;
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
@@ -1475,6 +2005,19 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     }
     grid = dim3(fa.n_full + (units - fa.n_full) * fa.splits, 1, 1);
   }
+  if (persistent) {
+    // One CTA per SM walks the items (global: the launch plan's units and split
+    // pieces in grid order; local: (segment, head, query pair)).
+    fa.items = static_cast<int>(grid.x * grid.y * grid.z);
+    int sms = fa.sms;
+    if (sms <= 0) {
+      int dev = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return e;
+    }
+    grid = dim3(std::min(fa.items, sms), 1, 1);
+  }
   if (fa.v_f16) {
     kern = flash_fwd_d64_kernel<true, 0, 0>;
   } else {
@@ -1482,7 +2025,8 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = form >= 9      ? ks[form - 9][poly][fa.splits > 1]
+      kern = form == 14     ? ksp[poly]
+             : form >= 9    ? ks[form - 9][poly][fa.splits > 1]
              : form == 8    ? w20_half[fa.splits > 1]
              : form == 7    ? w20_sp[fa.splits > 1][poly]
              : fa.splits > 1 ? w20[form == 5][poly]
@@ -1498,10 +2042,10 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
       kern = rows[form][poly];
     }
   }
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       FlashSmem::kLaunchBytes);
+  const uint32_t smem_bytes = persistent ? PSmem::kLaunchBytes : FlashSmem::kLaunchBytes;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
-  kern<<<grid, threads, FlashSmem::kLaunchBytes, st>>>(mq, mk, mv, fa, err);
+  kern<<<grid, threads, smem_bytes, st>>>(mq, mk, mv, fa, err);
   return cudaGetLastError();
 }
 

@@ -126,6 +126,7 @@ struct FlashArgs {
   // Filled in by launch_flash (kernel-side view of the plan).
   int n_full = 0;
   int splits = 1;
+  int items = 0;  // persistent layout: work items (units, split pieces or (segment, head, pair))
   // K'/V exchange of a sharded global block: key rows outside this rank's own rows
   // [own_begin, own_end) arrive from the peers.  peer_flags[r] = epoch << 32 |
   // complete << 31 | end once peer r's rows up to window row `end` are in place
