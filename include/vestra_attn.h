@@ -306,13 +306,15 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
  * the two query tiles taking turns in the exponential section, form 6 = form 3
  * with the split tail off (one CTA per unit), form 7 = form 3 with P handed over
  * in two 64-key halves, variant 64 = 64-key half-steps with S and P
- * double-buffered in TMEM; with the fixed offset (variant + 256) also form 9..14 +
+ * double-buffered in TMEM; with the fixed offset (variant + 256) also form 9..15 +
  * i: keys 0..63+8i of every 128 exponentiated on MUFU and the rest on the FMA pipe by
  * other warps (9: cubic, 10: quadratic, 11/12: the same with the two query tiles
  * taking turns, 13: 10 with a start offset between the tiles, 14: 10 as a persistent
- * walk over the launch's work items); 511 = the fixed offset with the library's
- * default layout (form 10, i = 1).  variant + 256: exponents relative to 0 instead of
- * the running row max (forms 3 and 9..14; others ignore it), for callers that guarantee
+ * walk over the launch's work items, 15: 10 with one query tile per CTA and two CTAs
+ * per SM, i = 0..2 only); 511 = the fixed offset with the library's
+ * default layout (form 15, i = 1 for local attention and for global launches of
+ * fewer than two waves of 256-query units; else form 10, i = 1).  variant + 256: exponents relative to 0 instead of
+ * the running row max (forms 3 and 9..15; others ignore it), for callers that guarantee
  * |q.k| / 8 * log2(e) <= 64 for every query/key pair (bf16 V only); the layer entry
  * points choose this themselves for QK-normalised layers whose norm weights bound
  * the scores that far (VA_SOFTMAX_FIXED_OFFSET=0 turns it off).  Query i is row

@@ -114,7 +114,8 @@ def test_flash_kernel_variants_match_oracle_core(ctx, oracle_mod, heads, seg, se
     assert_close(got, ref, what=f"flash variant {variant} h{heads} n{seg}x{segs}")
 
 
-@pytest.mark.parametrize("variant", [511] + [256 + 8 * form + i for form in (9, 10, 11, 12, 13, 14) for i in range(5)])
+@pytest.mark.parametrize("variant", [511] + [256 + 8 * form + i for form in (9, 10, 11, 12, 13, 14) for i in range(5)]
+                         + [256 + 8 * 15 + i for i in range(3)])
 @pytest.mark.parametrize("heads,seg,segs", [(1, 5, 1), (2, 129, 1), (2, 300, 1), (12, 866, 1), (4, 865, 3),
                                             (12, 1732, 1), (12, 10392, 1)])
 def test_flash_key_split_matches_oracle_core(ctx, oracle_mod, heads, seg, segs, variant):

@@ -2077,10 +2077,10 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   }
   if (variant >= 0) {
     const int poly = variant & 7, form = variant >> 3;
-    const bool key_split = form >= 9 && form <= 14 && poly <= 4 && fa.fixed_offset;
+    const bool key_split = form >= 9 && form <= 15 && poly <= (form == 15 ? 2 : 4) && fa.fixed_offset;
     if (!key_split && (poly > 2 || form > 8 || (form == 8 && poly != 0)))
       return fail(c, VA_ERR_INVALID,
-                  "variant must be poly (0..2) + 8 * form (0..7), 64, or with the fixed offset 8 * (9..14) + (0..4)");
+                  "variant must be poly (0..2) + 8 * form (0..7), 64, or with the fixed offset 8 * (9..14) + (0..4) or 8 * 15 + (0..2)");
     fa.poly_per8 = variant;
   }
   set_split_workspace(c, &fa);

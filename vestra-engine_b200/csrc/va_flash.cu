@@ -132,15 +132,17 @@ __device__ __forceinline__ SplitPos split_pos(const FlashArgs& fa) {
 // Global attention: a 1-D grid of units (head, query pair), query pair fastest so
 // the CTAs of one head (same K/V) run together; units >= n_full are split over
 // `splits` key ranges of whole 128-key tiles.  Local attention: grid (query pairs
-// of a segment, heads, segments), never split.
-template <bool kSplit = true>
+// of a segment, heads, segments), never split.  kTile1: units of one query tile
+// (128 rows) instead of a pair.
+template <bool kSplit = true, bool kTile1 = false>
 __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
+  constexpr int kUnitRows = kTile1 ? kTileQ : 2 * kTileQ;
   Geom g;
   if (fa.seg_len == 0) {
-    const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
+    const int qpairs = (fa.q_count + kUnitRows - 1) / kUnitRows;
     const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{static_cast<int>(blockIdx.x), 0, 1, 0};
     g.head = sp.unit / qpairs;
-    g.q0 = (sp.unit % qpairs) * 2 * kTileQ;
+    g.q0 = (sp.unit % qpairs) * kUnitRows;
     g.q_end = fa.q_count;
     const int total = (fa.kv_rows + kTileK - 1) / kTileK;
     const int t0 = sp.split * total / sp.nsplit, t1 = (sp.split + 1) * total / sp.nsplit;
@@ -154,7 +156,7 @@ __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
   } else {
     const int q_seg0 = blockIdx.z * fa.seg_len;
     g.q_end = q_seg0 + fa.seg_len;
-    g.q0 = q_seg0 + blockIdx.x * 2 * kTileQ;
+    g.q0 = q_seg0 + blockIdx.x * kUnitRows;
     g.k0 = fa.q_offset + q_seg0;
     g.num_kv = (fa.seg_len + kTileK - 1) / kTileK;
     g.last_valid = fa.seg_len - (g.num_kv - 1) * kTileK;
@@ -162,7 +164,7 @@ __device__ __forceinline__ Geom make_geom(const FlashArgs& fa) {
     g.rot = 0;
     g.tail_iter = g.num_kv - 1;
   }
-  g.nq = (g.q_end - g.q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
+  g.nq = !kTile1 && (g.q_end - g.q0) > kTileQ ? 2 : 1;  // query tiles with valid rows
   g.col = g.head * kHeadDim;
   return g;
 }
@@ -205,6 +207,8 @@ struct Ctl {
   __device__ volatile int* tile_go() const {
     return reinterpret_cast<volatile int*>(smem + FlashSmem::kMisc + 32);
   }
+  // Key-split layout: partial row sums [tile][role][128].
+  __device__ float* red() const { return reinterpret_cast<float*>(smem + FlashSmem::kRed); }
   __device__ uint32_t sQ(int t) const { return base + FlashSmem::kQ + t * kTileBytes; }
   __device__ uint32_t sK(int s) const { return base + FlashSmem::kK + s * kTileBytes; }
   __device__ uint32_t sV(int s) const { return base + FlashSmem::kV + s * kTileBytes; }
@@ -1190,8 +1194,10 @@ __device__ __forceinline__ uint64_t exp2_fma_pair(uint64_t s2, uint64_t c2) {
 // step j, tile 1 of step j, tile 0 of step j + 1, ...), so each tile's softmax has
 // MUFU and the issue slots of the sub-partition to itself while the other tile
 // waits for its UMMAs, P store and next S.
-template <int K0, int NK, bool kFma, bool kQuad, bool kTurns>
-__device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uint32_t tS, uint32_t tP,
+// C: the CTA's shared-memory handles (Ctl of the two-tile layout, T1Ctl of the
+// one-tile layout; kTurns needs two tiles).
+template <int K0, int NK, bool kFma, bool kQuad, bool kTurns, class C>
+__device__ __forceinline__ bool ks_steps(const C& c, const Geom& g, int t, uint32_t tS, uint32_t tP,
                                          uint64_t sc2, float& l, int* err, bool signal = false) {
   volatile int* abort_flag = c.abort_flag();
   for (int j = 0; j < g.num_kv; ++j) {
@@ -1204,11 +1210,13 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
     tc_fence_before();
     mbar_arrive(c.s_free(t));  // the UMMA warp may overwrite S_t now
     if (signal && j == 0) *c.tile_go() = 1;
-    if (kTurns && g.nq == 2 && (t == 1 || j > 0)) {
-      ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
-                     kDevTimeoutConsumer);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) return false;
+    if constexpr (kTurns) {
+      if (g.nq == 2 && (t == 1 || j > 0)) {
+        ok = mbar_wait(c.ex_done(t ^ 1), t == 1 ? (j & 1) : ((j - 1) & 1), abort_flag, err,
+                       kDevTimeoutConsumer);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) return false;
+      }
     }
     uint32_t pk[NK / 2];
     uint64_t acc[2];
@@ -1243,7 +1251,9 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
       body(std::true_type{});
     else
       body(std::false_type{});
-    if (kTurns && g.nq == 2) mbar_arrive(c.ex_done(t));
+    if constexpr (kTurns) {
+      if (g.nq == 2) mbar_arrive(c.ex_done(t));
+    }
     if (j > 0) {
       // PV_t(j-1) has finished reading P_t.
       ok = mbar_wait(c.pv_done(t), (j - 1) & 1, abort_flag, err, kDevTimeoutConsumer);
@@ -1261,6 +1271,101 @@ __device__ __forceinline__ bool ks_steps(const Ctl& c, const Geom& g, int t, uin
     mbar_arrive(c.p_full(t));
   }
   return true;
+}
+
+// End of a key-split query tile, by its 256 softmax threads: the row sum of the two
+// key ranges (MUFU and FMA warps) meets in shared memory, each warp reads its half of
+// the row's O (columns 32 * role ..), and, for a piece of the split tail, the partial
+// rows go to the workspace and the CTA that arrives last merges every piece.  `lead`
+// marks one thread of the tile (it counts the arrival); named barrier 1 + t.
+template <bool kSplit, class C>
+__device__ __forceinline__ void ks_finish(const C& c, const Geom& g, const FlashArgs& fa, int t, int role,
+                                          int r, bool lead, float l, bool ok, uint32_t tO, int* err) {
+  float* red = c.red();
+  bool fin = ok && mbar_wait(c.o_final(t), 0, c.abort_flag(), err, kDevTimeoutConsumer);
+  fin = __all_sync(0xffffffffu, fin);
+  // The row sum: this thread's keys plus the other warp's (every thread of the
+  // tile's 8 warps reaches the barrier; each wait above is bounded).
+  red[(t * 2 + role) * kTileQ + r] = l;
+  named_bar_sync(1 + t, 256);
+  l += red[(t * 2 + (role ^ 1)) * kTileQ + r];
+  float o[32];  // O columns [32 * role, 32 * role + 32) of this row, unnormalised
+  if (fin) {
+    tc_fence_after();
+    tmem_ld32(tO + 32 * role, o);
+  }
+  const float mrow = 0.f;  // reference exponent of this row (0: fixed offset)
+  const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{0, 0, 1, 0};
+  if (kSplit && sp.nsplit > 1) {
+    // Split tail: publish this key range's partial rows, count the arrival, and
+    // let the CTA that arrives last merge every split (as in the w20 layout).
+    const int slot = (sp.tail_unit * sp.nsplit + sp.split) * 2 + t;
+    if (fin) {
+      float4* po = reinterpret_cast<float4*>(fa.part_o + (static_cast<size_t>(slot) * kTileQ + r) * kHeadDim +
+                                             32 * role);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) po[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      if (role == 0)
+        reinterpret_cast<float2*>(fa.part_ml + static_cast<size_t>(slot) * kTileQ * 2)[r] = make_float2(mrow, l);
+    }
+    __threadfence();
+    named_bar_sync(1 + t, 256);
+    if (lead) {
+      const int old = atomicAdd(fa.counters + sp.tail_unit * 2 + t, 1);
+      const bool last = old == sp.nsplit - 1;
+      if (last) atomicExch(fa.counters + sp.tail_unit * 2 + t, 0);  // ready for the next launch
+      *c.merge_flag(t) = last ? 1 : 0;
+    }
+    named_bar_sync(1 + t, 256);
+    if (*c.merge_flag(t) == 0) {
+      fin = false;  // another split's CTA merges this tile
+    } else if (fin) {
+      __threadfence();
+      float mx = -INFINITY;
+      for (int s = 0; s < sp.nsplit; ++s) {
+        const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+        mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r).x);
+      }
+      l = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      for (int s = 0; s < sp.nsplit; ++s) {
+        const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
+        const float2 a = __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r);
+        const float w = ex2(a.x - mx);
+        l += w * a.y;
+        const float4* po = reinterpret_cast<const float4*>(
+            fa.part_o + (static_cast<size_t>(sl) * kTileQ + r) * kHeadDim + 32 * role);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 u = __ldcg(po + q);
+          o[4 * q] += w * u.x;
+          o[4 * q + 1] += w * u.y;
+          o[4 * q + 2] += w * u.z;
+          o[4 * q + 3] += w * u.w;
+        }
+      }
+    }
+  }
+  const int token = g.q0 + t * kTileQ + r;  // row of the local Q / O buffers
+  if (fin && token < g.q_end) {
+    const float inv = 1.0f / l;
+    if (fa.out_mode == 0) {
+      uint4* d = reinterpret_cast<uint4*>(fa.o_tok + static_cast<size_t>(token) * fa.embed + g.col + 32 * role);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        d[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
+                          pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
+                          pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
+                          pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
+    } else {
+      float4* d = reinterpret_cast<float4*>(
+          fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim + 32 * role);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d[q] = make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv, o[4 * q + 3] * inv);
+    }
+  }
 }
 
 template <int KA, bool kSplit, bool kQuad, bool kTurns, bool kStagger = false>
@@ -1294,101 +1399,253 @@ __global__ void __launch_bounds__(kW20Threads, 1)
     const uint32_t tP = tmem + lane_off + col_p(t);
     const uint32_t tO = tmem + lane_off + col_o(t);
     const uint64_t sc2 = f32x2_pack(fa.scale_log2, fa.scale_log2);
-    // Partial row sums of the two key ranges: [tile][role][row].
-    float* red = reinterpret_cast<float*>(c.smem + FlashSmem::kRed);
     if (t < g.nq) {
       float l = 0.f;
       // Tile 0's first softmax thread lets tile 1's issuer start (form 13).
       const bool signal = kStagger && t == 0 && role == 0 && quad == 0 && lane == 0;
       bool ok = role == 0 ? ks_steps<0, KA, false, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err, signal)
                           : ks_steps<KA, kTileK - KA, true, kQuad, kTurns>(c, g, t, tS, tP, sc2, l, err);
-      bool fin = ok && mbar_wait(c.o_final(t), 0, c.abort_flag(), err, kDevTimeoutConsumer);
-      fin = __all_sync(0xffffffffu, fin);
-      // The row sum: this thread's keys plus the other warp's (every thread of the
-      // tile's 8 warps reaches the barrier; each wait above is bounded).
-      red[(t * 2 + role) * kTileQ + r] = l;
-      named_bar_sync(1 + t, 256);
-      l += red[(t * 2 + (role ^ 1)) * kTileQ + r];
-      float o[32];  // O columns [32 * role, 32 * role + 32) of this row, unnormalised
-      if (fin) {
-        tc_fence_after();
-        tmem_ld32(tO + 32 * role, o);
-      }
-      const float mrow = 0.f;  // reference exponent of this row (0: fixed offset)
-      const SplitPos sp = kSplit ? split_pos(fa) : SplitPos{0, 0, 1, 0};
-      if (kSplit && sp.nsplit > 1) {
-        // Split tail: publish this key range's partial rows, count the arrival, and
-        // let the CTA that arrives last merge every split (as in the w20 layout).
-        const int slot = (sp.tail_unit * sp.nsplit + sp.split) * 2 + t;
-        if (fin) {
-          float4* po = reinterpret_cast<float4*>(fa.part_o + (static_cast<size_t>(slot) * kTileQ + r) * kHeadDim +
-                                                 32 * role);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) po[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-          if (role == 0)
-            reinterpret_cast<float2*>(fa.part_ml + static_cast<size_t>(slot) * kTileQ * 2)[r] = make_float2(mrow, l);
-        }
-        __threadfence();
-        named_bar_sync(1 + t, 256);
-        if (sw == 8 * t && lane == 0) {
-          const int old = atomicAdd(fa.counters + sp.tail_unit * 2 + t, 1);
-          const bool last = old == sp.nsplit - 1;
-          if (last) atomicExch(fa.counters + sp.tail_unit * 2 + t, 0);  // ready for the next launch
-          *c.merge_flag(t) = last ? 1 : 0;
-        }
-        named_bar_sync(1 + t, 256);
-        if (*c.merge_flag(t) == 0) {
-          fin = false;  // another split's CTA merges this tile
-        } else if (fin) {
-          __threadfence();
-          float mx = -INFINITY;
-          for (int s = 0; s < sp.nsplit; ++s) {
-            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
-            mx = fmaxf(mx, __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r).x);
-          }
-          l = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
-          for (int s = 0; s < sp.nsplit; ++s) {
-            const int sl = (sp.tail_unit * sp.nsplit + s) * 2 + t;
-            const float2 a = __ldcg(reinterpret_cast<const float2*>(fa.part_ml + static_cast<size_t>(sl) * kTileQ * 2) + r);
-            const float w = ex2(a.x - mx);
-            l += w * a.y;
-            const float4* po = reinterpret_cast<const float4*>(
-                fa.part_o + (static_cast<size_t>(sl) * kTileQ + r) * kHeadDim + 32 * role);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 u = __ldcg(po + q);
-              o[4 * q] += w * u.x;
-              o[4 * q + 1] += w * u.y;
-              o[4 * q + 2] += w * u.z;
-              o[4 * q + 3] += w * u.w;
-            }
-          }
-        }
-      }
-      const int token = g.q0 + t * kTileQ + r;  // row of the local Q / O buffers
-      if (fin && token < g.q_end) {
-        const float inv = 1.0f / l;
-        if (fa.out_mode == 0) {
-          uint4* d = reinterpret_cast<uint4*>(fa.o_tok + static_cast<size_t>(token) * fa.embed + g.col + 32 * role);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            d[q] = make_uint4(pack_bf16x2(o[8 * q] * inv, o[8 * q + 1] * inv),
-                              pack_bf16x2(o[8 * q + 2] * inv, o[8 * q + 3] * inv),
-                              pack_bf16x2(o[8 * q + 4] * inv, o[8 * q + 5] * inv),
-                              pack_bf16x2(o[8 * q + 6] * inv, o[8 * q + 7] * inv));
-        } else {
-          float4* d = reinterpret_cast<float4*>(
-              fa.o_hnd + (static_cast<size_t>(g.head) * fa.q_count + token) * kHeadDim + 32 * role);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            d[q] = make_float4(o[4 * q] * inv, o[4 * q + 1] * inv, o[4 * q + 2] * inv, o[4 * q + 3] * inv);
-        }
-      }
+      ks_finish<kSplit>(c, g, fa, t, role, r, sw == 8 * t && lane == 0, l, ok, tO, err);
     }
   }
   cta_teardown(c, tmem);
+}
+
+// ============================================================== one-tile key split
+// Form 15: the key-split softmax of form 10 with one 128-row query tile per CTA and
+// two CTAs per SM (320 threads at up to 96 registers, 256 TMEM columns and under
+// 113 KB of shared memory each).  The two CTAs of an SM are independent: while one
+// sets up, waits for its first scores or drains its last P·V and epilogue, the
+// other's steps keep the tensor pipe and the softmax pipes busy, and a short key
+// range (local attention, one rank's slice) pays less for its fill and drain.  The
+// units are single query tiles, so an 866-row segment takes 7 tiles (896 query slots)
+// instead of 4 pairs (1,024).  Each CTA streams its own K/V: a ring of 3 K stages
+// (free once QK has read them) and 2 V stages (free once P·V has), loaded in the
+// order the UMMA chain uses them (K0, K1, V0, K2, V1, K3, ...).
+// Warp 0: TMA producer; warp 1: TMEM allocation and UMMA issuer; warps 2..9: the
+// softmax, warp w on TMEM lane quadrant w % 4 (role 0 = warps 2..5, role 1 = 6..9).
+// No setmaxnreg split: every warp keeps the launch's registers.
+constexpr int kT1Threads = 320;
+constexpr int kT1KStages = 3;
+constexpr int kT1VStages = 2;
+constexpr uint32_t kT1TmemCols = 256;
+struct T1Smem {
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK = kTileBytes;
+  static constexpr uint32_t kV = kK + kT1KStages * kTileBytes;
+  static constexpr uint32_t kBar = kV + kT1VStages * kTileBytes;
+  // q_full, k_full[3], k_empty[3], v_full[2], v_empty[2], s_full, s_free, p_full,
+  // pv_done, o_final
+  static constexpr uint32_t kNumBars = 1 + 2 * kT1KStages + 2 * kT1VStages + 5;
+  static constexpr uint32_t kMisc = kBar + 8 * kNumBars;
+  static constexpr uint32_t kRed = kMisc + 64;  // partial row sums [role][128] F32
+  static constexpr uint32_t kBytes = kRed + 2 * 128 * 4;
+  static constexpr uint32_t kLaunchBytes = kBytes + 1024;
+};
+static_assert(2 * (T1Smem::kLaunchBytes + 1024) <= 228 * 1024, "two one-tile CTAs per SM");
+
+struct T1Ctl {
+  uint32_t base;
+  uint8_t* smem;
+  __device__ uint32_t bar(int i) const { return base + T1Smem::kBar + 8u * i; }
+  __device__ uint32_t q_full() const { return bar(0); }
+  __device__ uint32_t k_full(int s) const { return bar(1 + s); }
+  __device__ uint32_t k_empty(int s) const { return bar(1 + kT1KStages + s); }
+  __device__ uint32_t v_full(int s) const { return bar(1 + 2 * kT1KStages + s); }
+  __device__ uint32_t v_empty(int s) const { return bar(1 + 2 * kT1KStages + kT1VStages + s); }
+  __device__ uint32_t s_full(int) const { return bar(11); }
+  __device__ uint32_t s_free(int) const { return bar(12); }
+  __device__ uint32_t p_full(int) const { return bar(13); }
+  __device__ uint32_t pv_done(int) const { return bar(14); }
+  __device__ uint32_t o_final(int) const { return bar(15); }
+  __device__ int* misc(int i) const { return reinterpret_cast<int*>(smem + T1Smem::kMisc) + i; }
+  __device__ uint32_t* tmem_slot() const { return reinterpret_cast<uint32_t*>(misc(0)); }
+  __device__ volatile int* abort_flag() const { return misc(1); }
+  __device__ volatile int* k_issued() const { return misc(2); }
+  __device__ volatile int* k_consumed() const { return misc(3); }
+  __device__ volatile int* v_issued() const { return misc(4); }
+  __device__ volatile int* v_consumed() const { return misc(5); }
+  __device__ volatile int* mma_done() const { return misc(6); }
+  __device__ volatile int* merge_flag(int) const { return misc(7); }
+  __device__ volatile int* tile_go() const { return misc(8); }  // unused (form 13 only)
+  __device__ float* red() const { return reinterpret_cast<float*>(smem + T1Smem::kRed); }
+  __device__ uint32_t sQ() const { return base + T1Smem::kQ; }
+  __device__ uint32_t sK(int s) const { return base + T1Smem::kK + s * kTileBytes; }
+  __device__ uint32_t sV(int s) const { return base + T1Smem::kV + s * kTileBytes; }
+};
+static_assert(1 + 2 * kT1KStages + 2 * kT1VStages == 11, "T1Ctl barrier numbering");
+
+__device__ __forceinline__ T1Ctl make_t1_ctl() {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  T1Ctl c;
+  c.base = (raw_u32 + 1023u) & ~1023u;
+  c.smem = smem_raw + (c.base - raw_u32);
+  return c;
+}
+
+// TMA producer of the one-tile layout (one thread): Q, then K and V in the order the
+// UMMA chain reads them; the peer-row wait (sharded global blocks) comes before each
+// key tile's K.
+__device__ __forceinline__ void t1_producer(const T1Ctl& c, const Geom& g, const FlashArgs& fa,
+                                            const CUtensorMap* mq, const CUtensorMap* mk,
+                                            const CUtensorMap* mv, int* err) {
+  volatile int* abort_flag = c.abort_flag();
+  mbar_arrive_expect_tx(c.q_full(), kTileBytes);
+  tma_load_2d(c.sQ(), mq, c.q_full(), g.col, g.q0);
+  PeerCover pc{fa.rank + 1 == fa.nranks ? 0 : fa.rank + 1, 0};
+  auto row_of = [&](int j) { return g.k0 + ((j + g.rot) % g.num_kv) * kTileK; };
+  auto load_k = [&](int j) {
+    const int s = j % kT1KStages, row = row_of(j);
+    if (fa.peer_flags) {
+      const int need = tile_need(fa, row, min(row + kTileK, fa.kv_rows));
+      if (need > pc.covered && !wait_cover(fa, pc, need, abort_flag, err)) return false;
+    }
+    if (!mbar_wait(c.k_empty(s), ((j / kT1KStages) & 1) ^ 1, abort_flag, err, kDevTimeoutProducer)) return false;
+    mbar_arrive_expect_tx(c.k_full(s), kTileBytes);
+    tma_load_2d(c.sK(s), mk, c.k_full(s), g.col, row);
+    *c.k_issued() = j + 1;
+    return true;
+  };
+  auto load_v = [&](int j) {
+    const int s = j % kT1VStages;
+    if (!mbar_wait(c.v_empty(s), ((j / kT1VStages) & 1) ^ 1, abort_flag, err, kDevTimeoutProducer)) return false;
+    mbar_arrive_expect_tx(c.v_full(s), kTileBytes);
+    tma_load_2d(c.sV(s), mv, c.v_full(s), g.col, row_of(j));
+    *c.v_issued() = j + 1;
+    return true;
+  };
+  bool ok = load_k(0);
+  if (ok && g.num_kv > 1) ok = load_k(1);
+  for (int j = 0; ok && j < g.num_kv; ++j) {
+    ok = load_v(j);
+    if (ok && j + 2 < g.num_kv) ok = load_k(j + 2);
+  }
+}
+
+// UMMA issuer of the one-tile layout (one thread): QK(0), QK(1), then per step j:
+// PV(j), QK(j+2).  QK(jj) frees K stage jj, PV(j) frees V stage j.
+__device__ __forceinline__ void t1_mma(const T1Ctl& c, const Geom& g, uint32_t tmem, int* err) {
+  constexpr uint32_t idesc_qk = idesc_bf16_f32(kTileQ, kTileK, false, false);
+  constexpr uint32_t idesc_pv = idesc_bf16_f32(kTileQ, kHeadDim, false, true);
+  constexpr uint64_t kStageStep = kTileBytes >> 4;  // descriptor start-field step per stage
+  volatile int* abort_flag = c.abort_flag();
+  const uint64_t dq = sdesc_sw128(c.sQ(), 16, 1024);
+  const uint64_t dk0 = sdesc_sw128(c.sK(0), 16, 1024);
+  const uint64_t dv0 = sdesc_sw128(c.sV(0), 8192, 1024);  // V tile, MN-major
+  const uint32_t tS = tmem + col_s(0), tP = tmem + col_p(0), tO = tmem + col_o(0);
+  auto qk = [&](int jj) {
+    const int s = jj % kT1KStages;
+    bool r = mbar_wait(c.k_full(s), (jj / kT1KStages) & 1, abort_flag, err, kDevTimeoutMma);
+    if (r) *c.k_consumed() = jj + 1;
+    if (r && jj > 0) r = mbar_wait(c.s_free(0), (jj - 1) & 1, abort_flag, err, kDevTimeoutMma);
+    if (r) {
+      tc_fence_after();
+      umma_ss_k64(tS, dq, dk0 + s * kStageStep, idesc_qk, 0u);
+      tc_commit(c.s_full(0));
+      tc_commit(c.k_empty(s));
+    }
+    return r;
+  };
+  bool ok = mbar_wait(c.q_full(), 0, abort_flag, err, kDevTimeoutMma);
+  if (ok) ok = qk(0);
+  if (ok && g.num_kv > 1) ok = qk(1);
+  for (int j = 0; ok && j < g.num_kv; ++j) {
+    const int s = j % kT1VStages;
+    ok = mbar_wait(c.v_full(s), (j / kT1VStages) & 1, abort_flag, err, kDevTimeoutMma);
+    if (ok) *c.v_consumed() = j + 1;
+    if (ok) ok = mbar_wait(c.p_full(0), j & 1, abort_flag, err, kDevTimeoutMma);
+    if (!ok) break;
+    tc_fence_after();
+    umma_ts_k128_mn(tO, tP, dv0 + s * kStageStep, idesc_pv, j > 0 ? 1u : 0u);
+    tc_commit(c.pv_done(0));
+    tc_commit(c.v_empty(s));
+    if (j + 2 < g.num_kv) ok = qk(j + 2);
+  }
+  // Always committed, also after an abort (the teardown waits for it before it frees
+  // TMEM).
+  tc_commit(c.o_final(0));
+  *c.mma_done() = 1;
+}
+
+template <int KA, bool kSplit, bool kQuad>
+__global__ void __launch_bounds__(kT1Threads, 2)
+    flash_fwd_d64_ks1_kernel(const __grid_constant__ CUtensorMap map_q,
+                             const __grid_constant__ CUtensorMap map_k,
+                             const __grid_constant__ CUtensorMap map_v, FlashArgs fa, int* err) {
+  static_assert(KA % 8 == 0 && KA >= 8 && KA <= kTileK - 8, "key split");
+  const T1Ctl c = make_t1_ctl();
+  const Geom g = make_geom<kSplit, true>(fa);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(c.q_full(), 1);
+    for (int s = 0; s < kT1KStages; ++s) {
+      mbar_init(c.k_full(s), 1);
+      mbar_init(c.k_empty(s), 1);
+    }
+    for (int s = 0; s < kT1VStages; ++s) {
+      mbar_init(c.v_full(s), 1);
+      mbar_init(c.v_empty(s), 1);
+    }
+    mbar_init(c.s_full(0), 1);
+    mbar_init(c.s_free(0), 256);
+    mbar_init(c.p_full(0), 256);
+    mbar_init(c.pv_done(0), 1);
+    mbar_init(c.o_final(0), 1);
+    for (int i = 1; i < 9; ++i) *c.misc(i) = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(c.tmem_slot()), kT1TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *c.tmem_slot();
+
+  if (warp == 0) {
+    if (lane == 0) t1_producer(c, g, fa, &map_q, &map_k, &map_v, err);
+  } else if (warp == 1) {
+    if (lane == 0) t1_mma(c, g, tmem, err);
+  } else {
+    const int sw = warp - 2;         // 0..7
+    const int role = sw >> 2;        // 0: MUFU keys [0, KA); 1: FMA keys [KA, 128)
+    const int quad = warp & 3;       // TMEM lane quadrant
+    const int r = quad * 32 + lane;  // row of the query tile
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + col_s(0);
+    const uint32_t tP = tmem + lane_off + col_p(0);
+    const uint32_t tO = tmem + lane_off + col_o(0);
+    const uint64_t sc2 = f32x2_pack(fa.scale_log2, fa.scale_log2);
+    float l = 0.f;
+    const bool ok = role == 0 ? ks_steps<0, KA, false, kQuad, false>(c, g, 0, tS, tP, sc2, l, err)
+                              : ks_steps<KA, kTileK - KA, true, kQuad, false>(c, g, 0, tS, tP, sc2, l, err);
+    ks_finish<kSplit>(c, g, fa, 0, role, r, sw == 0 && lane == 0, l, ok, tO, err);
+  }
+
+  // Teardown: after an abort, wait (bounded) for the copies and UMMAs still in
+  // flight, then free TMEM.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *c.abort_flag()) {
+    if (*c.k_consumed() == 0) drain(c.q_full(), 0);
+    for (int j = *c.k_consumed(); j < *c.k_issued(); ++j) drain(c.k_full(j % kT1KStages), (j / kT1KStages) & 1);
+    for (int j = *c.v_consumed(); j < *c.v_issued(); ++j) drain(c.v_full(j % kT1VStages), (j / kT1VStages) & 1);
+    if (*c.mma_done()) drain(c.o_final(0), 0);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kT1TmemCols);
+  }
 }
 
 // ============================================================== persistent key split
@@ -1954,45 +2211,82 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
   static const Kern ksp[5] = {flash_fwd_d64_ksp_kernel<64, true>, flash_fwd_d64_ksp_kernel<72, true>,
                               flash_fwd_d64_ksp_kernel<80, true>, flash_fwd_d64_ksp_kernel<88, true>,
                               flash_fwd_d64_ksp_kernel<96, true>};
-  bool persistent = false;
+  // form 15: one query tile per CTA, two CTAs per SM (quadratic), KA = 64 + 8 * poly,
+  // poly 0..2 (a MUFU warp holds its KA scores in registers at once, within the 96 a
+  // thread has at two CTAs per SM).
+#define VA_KS1(KA) {flash_fwd_d64_ks1_kernel<KA, false, true>, flash_fwd_d64_ks1_kernel<KA, true, true>}
+  static const Kern ks1[3][2] = {VA_KS1(64), VA_KS1(72), VA_KS1(80)};
+#undef VA_KS1
+  bool persistent = false, tile1 = false;
   Kern kern;
   int threads = kRowsThreads;
   bool w20_kernel = false, no_split = false;
-  if (fa.poly_per8 < 0) fa.poly_per8 = fa.fixed_offset && !fa.v_f16 ? kDefaultKeySplit : kDefaultPolyPer8;
+  if (fa.poly_per8 < 0) {
+    fa.poly_per8 = kDefaultPolyPer8;
+    if (fa.fixed_offset && !fa.v_f16) {
+      int sms = fa.sms;
+      if (sms <= 0) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+      }
+      const int64_t pair_units = static_cast<int64_t>((fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ)) * fa.heads;
+      fa.poly_per8 = fa.seg_len > 0 || pair_units < 2 * sms ? kDefaultKeySplit1 : kDefaultKeySplit;
+    }
+  }
   if (!fa.v_f16) {
     const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (form >= 9 && form <= 14) {
-      if (poly > 4 || !fa.fixed_offset) return cudaErrorInvalidValue;
+    if (form >= 9 && form <= 15) {
+      if (poly > (form == 15 ? 2 : 4) || !fa.fixed_offset) return cudaErrorInvalidValue;
     } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
       return cudaErrorInvalidValue;
     }
-    w20_kernel = form == 3 || (form >= 5 && form <= 14);
+    w20_kernel = form == 3 || (form >= 5 && form <= 15);
     persistent = form == 14;
+    tile1 = form == 15;
     // form 6: form 3 with the split tail turned off (one CTA per unit).
     no_split = form == 6;
   }
+  // Query rows of one unit (a CTA before any key split) and CTAs resident per SM.
+  const int unit_rows = tile1 ? kTileQ : 2 * kTileQ;
+  int per_sm = 1;
+  if (tile1) {
+    static int t1_per_sm = 0;  // measured once: two unless the device disagrees
+    if (t1_per_sm == 0) {
+      cudaError_t e = cudaFuncSetAttribute(ks1[0][0], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           T1Smem::kLaunchBytes);
+      int nb = 0;
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, ks1[0][0], kT1Threads, T1Smem::kLaunchBytes);
+      if (e != cudaSuccess) return e;
+      t1_per_sm = std::max(1, std::min(nb, 2));
+    }
+    per_sm = t1_per_sm;
+  }
   dim3 grid;
   if (fa.seg_len > 0) {
-    grid = dim3((fa.seg_len + 2 * kTileQ - 1) / (2 * kTileQ), fa.heads, segs);
+    grid = dim3((fa.seg_len + unit_rows - 1) / unit_rows, fa.heads, segs);
     fa.n_full = 0;
     fa.splits = 1;
   } else {
-    // Units (head, query pair); the partial last wave is split over key ranges when
-    // the caller gave a partial-result workspace (four-threads-per-row kernel).
-    const int qpairs = (fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ);
+    // Units (head, query pair, or query tile for form 15); the partial last wave is
+    // split over key ranges when the caller gave a partial-result workspace.
+    const int qpairs = (fa.q_count + unit_rows - 1) / unit_rows;
     const int units = qpairs * fa.heads;
     const int num_kv = (fa.kv_rows + kTileK - 1) / kTileK;
     fa.n_full = units;
     fa.splits = 1;
     if (w20_kernel && !no_split && fa.part_o && fa.part_ml && fa.counters && fa.sms > 0) {
-      // The tail of `rem` units cut into s key ranges takes ceil(rem*s/sms) rounds
+      // The tail of `rem` units cut into s key ranges takes ceil(rem*s/slots) rounds
       // of 1/s unit time; pick the s with the shortest tail (each split also pays
       // a few percent for its own setup and the merge).
-      const int rem = units % fa.sms;
+      const int slots = fa.sms * per_sm;
+      const int rem = units % slots;
       int best = 1;
       double best_cost = 1.0;
       for (int sp = 2; rem && sp <= std::min(kMaxSplits, num_kv); ++sp) {
-        const double cost = static_cast<double>((rem * sp + fa.sms - 1) / fa.sms) / sp + 0.03;
+        const double cost = static_cast<double>((rem * sp + slots - 1) / slots) / sp + 0.03;
         if (cost < best_cost && rem * sp * 2 <= fa.part_slots) {
           best = sp;
           best_cost = cost;
@@ -2025,24 +2319,25 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
     if (w20_kernel) {
       // A launch without a split (local, or global with splits == 1) runs the
       // instance without the merge code.
-      kern = form == 14     ? ksp[poly]
+      kern = form == 15     ? ks1[poly][fa.splits > 1]
+             : form == 14   ? ksp[poly]
              : form >= 9    ? ks[form - 9][poly][fa.splits > 1]
              : form == 8    ? w20_half[fa.splits > 1]
              : form == 7    ? w20_sp[fa.splits > 1][poly]
              : fa.splits > 1 ? w20[form == 5][poly]
              : form == 5     ? w20[1][poly]
                              : w20_nosplit[poly];
-      threads = kW20Threads;
+      threads = tile1 ? kT1Threads : kW20Threads;
       // setmaxnreg.inc draws on the registers the CTA launched with.
       cudaFuncAttributes attr;
       cudaError_t e = cudaFuncGetAttributes(&attr, kern);
       if (e != cudaSuccess) return e;
-      if (attr.numRegs < kW20MinLaunchRegs) return cudaErrorInvalidConfiguration;
+      if (!tile1 && attr.numRegs < kW20MinLaunchRegs) return cudaErrorInvalidConfiguration;
     } else {
       kern = rows[form][poly];
     }
   }
-  const uint32_t smem_bytes = persistent ? PSmem::kLaunchBytes : FlashSmem::kLaunchBytes;
+  const uint32_t smem_bytes = persistent ? PSmem::kLaunchBytes : tile1 ? T1Smem::kLaunchBytes : FlashSmem::kLaunchBytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
   if (e != cudaSuccess) return e;
   kern<<<grid, threads, smem_bytes, st>>>(mq, mk, mv, fa, err);
