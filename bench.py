@@ -74,6 +74,8 @@ def default_flash_kernel(q_count, heads, seg_len=0):
     (launch_flash): one query tile per CTA, two CTAs per SM (ks1) for local attention
     and for global launches of fewer than two waves of 256-query units, else the
     two-tile kernel (ks)."""
+    import torch
+
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     pair_units = -(-q_count // 256) * heads
     return "flash_fwd_d64_ks1_kernel" if seg_len > 0 or pair_units < 2 * sms else "flash_fwd_d64_ks_kernel"

@@ -64,6 +64,28 @@ def test_linear_bf16_matches_torch(ctx, m, n, k):
     assert_close(out.cpu().numpy(), ref.cpu().numpy(), max_abs=1e-3, min_cos=0.999999, what="linear")
 
 
+# The epilogue with scale and residual, in place (out is the residual: the wide
+# 256 x 256 tiles send their rows as TMA add-reductions) and out of place, across
+# the row counts where the launch changes form (one wave of 256 x 256 tiles, the
+# persistent 256 x 128 kernel, 128-row tiles for short calls).
+@pytest.mark.parametrize("m,n,k", [(1299, 768, 768), (5196, 768, 768), (8448, 768, 768), (10392, 768, 768),
+                                   (10392, 768, 3072), (12544, 768, 768), (12545, 768, 768), (3000, 1024, 1024)])
+@pytest.mark.parametrize("inplace", [True, False])
+def test_linear_bf16_scale_residual_matches_torch(ctx, m, n, k, inplace):
+    g = torch.Generator(device="cpu").manual_seed(m + n + k + inplace)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (0.02 * torch.randn(n, k, generator=g)).to(torch.bfloat16).cuda()
+    bias = torch.randn(n, generator=g).cuda()
+    scale = (torch.rand(n, generator=g) + 0.5).cuda()
+    res = torch.randn(m, n, generator=g).cuda()
+    out = res.clone() if inplace else torch.full((m, n), float("nan"), device="cuda")
+    ctx.linear_bf16(a, w, out, bias=bias, scale=scale, residual=out if inplace else res)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    ref = (a.float() @ w.float().t() + bias) * scale + res
+    assert_close(out.cpu().numpy(), ref.cpu().numpy(), max_abs=2e-3, min_cos=0.999999, what="linear+residual")
+
+
 # ---------------------------------------------------------------- K2 alone
 def _tok(x, dtype=None):
     """[heads, rows, 64] -> token-major CUDA [rows, heads*64] (bf16 unless dtype given)."""

@@ -860,6 +860,222 @@ cudaError_t launch_gemm_persistent(const __nv_bfloat16* a, const __nv_bfloat16* 
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Wide projection tile (K3 and fc2 when the call has few tiles): one 256 x 256
+// output tile per CTA, one launch wave.  A narrow output (N = E) cut into 256 x 128
+// tiles re-reads every A row block N/128 times and leaves 1.66 waves at the DA3
+// window's row count; a 256 x 256 tile reads A N/256 times and B M/256 times (a
+// third less operand traffic per FLOP than 256 x 128), the tiles of a window fit in
+// one wave, and with one tile per CTA the operand ring is free for the epilogue once
+// the accumulator is final, so all of a 128-row pass is staged at once.
+//   warp 0      TMA producer: 3 stages of A [256 x 64] + B [256 x 64] (64 KB each)
+//   warp 1      TMEM (512 columns: two M=128 accumulators of N=256) + UMMA issuer
+//   warps 2..9  epilogue: two 128-row passes; warp w reads TMEM lanes 32*(w%4)..,
+//               warps 2..5 columns [0, 128), warps 6..9 [128, 256), four 32-column
+//               SWIZZLE_128B F32 tiles each, sent by TMA.  With the residual in
+//               place (out == residual) the tiles go out as TMA add-reductions:
+//               out = residual + (acc + bias) * scale, one F32 add per element at
+//               L2, the same single rounding as adding in registers.
+// ---------------------------------------------------------------------------
+struct WideSmem {
+  static constexpr int kStages = 3;
+  static constexpr uint32_t kABytes = 2 * kBM * kBK * 2;   // 256 rows x 64 bf16
+  static constexpr uint32_t kStageBytes = kABytes + 256 * kBK * 2;
+  static constexpr uint32_t kBarOffset = kStages * kStageBytes;
+  // full[3], empty[3], tfull; then the TMEM slot and flags
+  static constexpr uint32_t kNumBars = 2 * kStages + 1;
+  static constexpr uint32_t kSlotOffset = kBarOffset + 8 * kNumBars;
+  static constexpr uint32_t kConstOffset = kBarOffset + 128;
+  static constexpr uint32_t kBytes = kConstOffset + 512 * 4;  // bias[256], scale[256]
+  static constexpr uint32_t kLaunchBytes = kBytes + 1024;
+  static_assert(kSlotOffset + 32 <= kConstOffset, "barrier region too small");
+  static_assert(8 * kOutTileBytes <= kBarOffset, "a 128-row pass is staged in the operand ring");
+  static_assert(kLaunchBytes <= 227 * 1024, "shared memory budget");
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_wide_proj(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_out, ProjEpilogueArgs args, int M, int K,
+                        int n_tiles_n, int reduce, int* err) {
+  using L = WideSmem;
+  constexpr uint32_t kTmemCols = 512;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - raw_u32);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = K / kBK;
+  const int m0 = (blockIdx.x / n_tiles_n) * 2 * kBM, n0 = (blockIdx.x % n_tiles_n) * 256;
+
+  const uint32_t bar0 = base_u32 + L::kBarOffset;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (L::kStages + s); };
+  const uint32_t tfull_bar = bar0 + 8u * (2 * L::kStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kSlotOffset);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* issued = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* consumed = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* mma_started = reinterpret_cast<volatile int*>(tmem_slot + 4);
+  auto sA = [&](int s) { return base_u32 + s * L::kStageBytes; };
+  auto sB = [&](int s) { return base_u32 + s * L::kStageBytes + L::kABytes; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(tfull_bar, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    *mma_started = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    tma_prefetch_desc(&map_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % L::kStages;
+        if (!mbar_wait(empty_bar(s), ((kb / L::kStages) & 1) ^ 1, abort_flag, err, kDevTimeoutProducer)) break;
+        mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
+        tma_load_2d(sA(s), &map_a, full_bar(s), kb * kBK, m0);
+        tma_load_2d(sB(s), &map_b, full_bar(s), kb * kBK, n0);
+        *issued = kb + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, 256, false, false);
+      *mma_started = 1;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % L::kStages;
+        if (!mbar_wait(full_bar(s), (kb / L::kStages) & 1, abort_flag, err, kDevTimeoutMma)) break;
+        *consumed = kb + 1;
+        tc_fence_after();
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = sdesc_sw128(sA(s) + mt * kBM * 128 + k * 32, 16, 1024);
+            const uint64_t bd = sdesc_sw128(sB(s) + k * 32, 16, 1024);
+            umma_ss(tmem + mt * 256, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+        tc_commit(empty_bar(s));
+      }
+      // Always committed, also after an abort: it marks the moment every UMMA of
+      // this CTA has finished (the epilogue and the teardown wait for it).
+      tc_commit(tfull_bar);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;  // warps 2..5 -> 0, 6..9 -> 1
+    const int row = quad * 32 + lane;
+    const int t = threadIdx.x - 64;
+    const bool store_thread = ((warp - 2) & 3) == 0 && lane == 0;
+    float* cbuf = reinterpret_cast<float*>(smem + L::kConstOffset);
+    for (int c = t; c < 512; c += 256)
+      cbuf[c] = c < 256 ? (args.bias ? args.bias[n0 + c] : 0.0f) : (args.ls1 ? args.ls1[n0 + c - 256] : 1.0f);
+    named_bar_sync(1, 256);
+    bool ok = mbar_wait(tfull_bar, 0, abort_flag, err, kDevTimeoutConsumer) && !*abort_flag;
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+    for (int pass = 0; pass < 2; ++pass) {
+      const int mp = m0 + pass * kBM;
+      if (pass == 1) {
+        // Pass 0's stores have read this half's staging tiles.
+        if (store_thread) bulk_wait_all_read();
+        named_bar_sync(2 + half, 128);
+      }
+      if (ok) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = half * 4 + j;  // 32 columns
+          float x[32];
+          tmem_ld32(tmem + pass * 256 + chunk * 32 + (static_cast<uint32_t>(quad * 32) << 16), x);
+          const float* bias = cbuf + chunk * 32;
+          const float* scale = cbuf + 256 + chunk * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] = (x[i] + bias[i]) * scale[i];
+          const uint32_t tile = base_u32 + chunk * kOutTileBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            st_shared_v4(tile + sw128_offset(row, c),
+                         make_uint4(__float_as_uint(x[4 * c]), __float_as_uint(x[4 * c + 1]),
+                                    __float_as_uint(x[4 * c + 2]), __float_as_uint(x[4 * c + 3])));
+        }
+      }
+      fence_proxy_async_smem();  // the staged tiles are read by the TMA stores
+      named_bar_sync(2 + half, 128);
+      if (ok && mp < M && store_thread) {
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = half * 4 + j;
+          if (reduce)
+            tma_reduce_add_2d(&map_out, base_u32 + chunk * kOutTileBytes, n0 + chunk * 32, mp);
+          else
+            tma_store_2d(&map_out, base_u32 + chunk * kOutTileBytes, n0 + chunk * 32, mp);
+        }
+        bulk_commit_group();
+      }
+    }
+    if (store_thread) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (*abort_flag)
+      for (int kb = *consumed; kb < *issued; ++kb) drain_wait(full_bar(kb % L::kStages), (kb / L::kStages) & 1);
+    if (*mma_started) drain_wait(tfull_bar, 0);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// 256 x 256 tiles in one wave when the call has between two thirds of and as many
+// tiles as SMs (measured on B200: 123 tiles of the DA3 window 24.6 vs 26.7 us, fc2
+// 51.7 vs 61.3 us; 63 tiles 22.7 vs 20.4 us, slower than the persistent kernel), N is a
+// multiple of 256 and the residual, if any, is the output itself; otherwise the
+// caller takes the persistent kernel.
+cudaError_t launch_wide_proj(const __nv_bfloat16* a, const __nv_bfloat16* w_t, int M, int N, int K,
+                             const ProjEpilogueArgs& args, int* err, cudaStream_t st, bool* used) {
+  *used = false;
+  if (N % 256 != 0 || K % kBK != 0 || K <= 0 || (args.residual && args.residual != args.out)) return cudaSuccess;
+  const int n_tiles_n = N / 256;
+  const int64_t tiles = static_cast<int64_t>((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles_n;
+  const int sms = device_sms();
+  if (tiles > sms || 3 * tiles < 2 * sms) return cudaSuccess;
+  CUtensorMap map_a, map_b, map_out;
+  if (!encode_tma_2d_bf16(&map_a, a, K, M, kBK, 2 * kBM) || !encode_tma_2d_bf16(&map_b, w_t, K, N, kBK, 256) ||
+      !encode_tma_2d_f32(&map_out, args.out, N, M, 32, kBM))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_wide_proj, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       WideSmem::kLaunchBytes);
+  if (e != cudaSuccess) return e;
+  gemm_bf16_wide_proj<<<static_cast<int>(tiles), kGemmThreads, WideSmem::kLaunchBytes, st>>>(
+      map_a, map_b, map_out, args, M, K, n_tiles_n, args.residual ? 1 : 0, err);
+  *used = true;
+  return cudaGetLastError();
+}
+
 bool gemm_per_tile() {
   static const bool per_tile = std::getenv("VA_GEMM_PER_TILE") != nullptr;
   return per_tile;
@@ -908,6 +1124,11 @@ cudaError_t launch_proj_gemm(const __nv_bfloat16* a, const __nv_bfloat16* w_t, i
   ProjEpilogue e{};
   e.a = epi;
   if (!encode_tma_2d_f32(&e.map_out, epi.out, n, m, 32, kBM)) return cudaErrorInvalidValue;
+  if (!gemm_per_tile()) {
+    bool used = false;
+    const cudaError_t w = launch_wide_proj(a, w_t, m, n, k, epi, err, st, &used);
+    if (w != cudaSuccess || used) return w;
+  }
   if (epi.residual && !gemm_per_tile()) {
     if (!encode_tma_2d_f32(&e.map_res, epi.residual, n, m, 32, kBM)) return cudaErrorInvalidValue;
     e.res_staged = 1;
