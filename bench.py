@@ -90,16 +90,18 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-NCU_CASES = ("subblock", "block", "fc2", "tokens", "capture", "gguf", "flash", "flash_slice8")
+NCU_CASES = ("subblock", "block", "fc2", "tokens", "capture", "gguf", "flash", "flash_slice8", "flash_local")
 
 
 def run_ncu_case(name):
     """One small case of a kernel family on cuda:0 at the cfg3 shapes, run a few times
     (the profiler skips the first launches): subblock / block (LN1, QKV, attention,
-    proj / + LN2, fc1, fc2), fc2 (the K3 GEMM at fc2's K = 3072), tokens (patchify +
+    proj / + LN2, fc1, fc2), fc2 (the K3 GEMM at fc2's K = 3072, residual in place as in
+    a block), tokens (patchify +
     patch projection), capture (two capture launches), gguf (device decoding of a
     2-block Q8_0 file), flash (the default fixed-offset attention launch over the
-    window) and flash_slice8 (one rank's 1,299 queries of 8 against the window)."""
+    window), flash_slice8 (one rank's 1,299 queries of 8 against the window) and
+    flash_local (local attention over the window's 12 views of 866 tokens)."""
     import numpy as np
     import torch
     import vestra_attn as va
@@ -127,9 +129,9 @@ def run_ncu_case(name):
     elif name == "fc2":
         h = torch.randn(wl.rows, 4 * E, device="cuda").to(torch.bfloat16)
         w = (0.02 * torch.randn(E, 4 * E, device="cuda")).to(torch.bfloat16)
-        out = torch.empty(wl.rows, E, device="cuda")
+        out = x.clone()
         for _ in range(3):
-            ctx.linear_bf16(h, w, out, bias=torch.zeros(E, device="cuda"), residual=x)
+            ctx.linear_bf16(h, w, out, bias=torch.zeros(E, device="cuda"), residual=out)
     elif name == "tokens":
         pw = syn.patch_embed_weights(E, 14, 37, 1, seed=0)
         ctx.load_patch_embed(pw["weight"], pw["bias"], pw["cls"], pw["pos_embed"], pw["registers"], 14)
@@ -153,13 +155,14 @@ def run_ncu_case(name):
         def hn(t):
             return torch.nn.functional.layer_norm(t.view(t.shape[0], wl.heads, 64), (64,)).view(t.shape[0], -1)
 
-        local = wl.rows if name == "flash" else wl.rows // 8
+        local = wl.rows // 8 if name == "flash_slice8" else wl.rows
+        seg = wl.rows // wl.views if name == "flash_local" else 0
         q = hn(torch.randn(local, E, device="cuda", generator=g)).to(torch.bfloat16)
         k = hn(torch.randn(wl.rows, E, device="cuda", generator=g)).to(torch.bfloat16)
         v = torch.randn(wl.rows, E, device="cuda", generator=g).to(torch.bfloat16)
         o = torch.empty_like(q)
         for _ in range(3):
-            ctx.flash_bf16(q, k, v, wl.heads, o, q_offset=wl.rows - local, variant=511)
+            ctx.flash_bf16(q, k, v, wl.heads, o, q_offset=wl.rows - local, seg_len=seg, variant=511)
     torch.cuda.synchronize()
     ctx.check_device()
     ctx.close()
