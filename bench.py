@@ -72,13 +72,14 @@ def parse_args():
 def default_flash_kernel(q_count, heads, seg_len=0):
     """The attention kernel the library's default picks for a fixed-offset launch
     (launch_flash): one query tile per CTA, two CTAs per SM (ks1) for local attention
-    and for global launches of fewer than two waves of 256-query units, else the
-    two-tile kernel (ks)."""
+    and for global launches whose 256-query units fill 1.5 to 2 waves of the SMs, else
+    the two-tile kernel (ks)."""
     import torch
 
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     pair_units = -(-q_count // 256) * heads
-    return "flash_fwd_d64_ks1_kernel" if seg_len > 0 or pair_units < 2 * sms else "flash_fwd_d64_ks_kernel"
+    one_tile = seg_len > 0 or 3 * sms <= 2 * pair_units < 4 * sms
+    return "flash_fwd_d64_ks1_kernel" if one_tile else "flash_fwd_d64_ks_kernel"
 
 
 def cpu_threads():

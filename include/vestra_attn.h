@@ -312,8 +312,8 @@ int va_attention_device_sharded(va_ctx* ctx, int layer, const float* ln1_local,
  * taking turns, 13: 10 with a start offset between the tiles, 14: 10 as a persistent
  * walk over the launch's work items, 15: 10 with one query tile per CTA and two CTAs
  * per SM, i = 0..2 only); 511 = the fixed offset with the library's
- * default layout (form 15, i = 1 for local attention and for global launches of
- * fewer than two waves of 256-query units; else form 10, i = 1).  variant + 256: exponents relative to 0 instead of
+ * default layout (form 15, i = 1 for local attention and for global launches whose
+ * 256-query units fill 1.5 to 2 waves of the SMs; else form 10, i = 1).  variant + 256: exponents relative to 0 instead of
  * the running row max (forms 3 and 9..15; others ignore it), for callers that guarantee
  * |q.k| / 8 * log2(e) <= 64 for every query/key pair (bf16 V only); the layer entry
  * points choose this themselves for QK-normalised layers whose norm weights bound

@@ -2231,8 +2231,12 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess) return e;
       }
+      // Global: the one-tile form where the two-tile units fill 1.5 to 2 waves (their
+      // split tail is then half a wave or more); measured on B200 it loses below
+      // (2,598 queries of 10,392: 549 vs 715 TFLOP/s) and on full windows.
       const int64_t pair_units = static_cast<int64_t>((fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ)) * fa.heads;
-      fa.poly_per8 = fa.seg_len > 0 || pair_units < 2 * sms ? kDefaultKeySplit1 : kDefaultKeySplit;
+      const bool tail_heavy = 2 * pair_units >= 3 * static_cast<int64_t>(sms) && pair_units < 2 * sms;
+      fa.poly_per8 = fa.seg_len > 0 || tail_heavy ? kDefaultKeySplit1 : kDefaultKeySplit;
     }
   }
   if (!fa.v_f16) {

@@ -91,9 +91,9 @@ constexpr int kDefaultPolyPer8 = 24;
 // keys of every 128 on MUFU (the fastest split measured at S=12).
 constexpr int kDefaultKeySplit = 10 * 8 + 1;
 // The same softmax with one query tile per CTA and two CTAs per SM (form 15, KA = 72):
-// the default for local attention and for global launches of fewer than two waves of
-// query pairs (one rank's slice of a sharded window), where a CTA's fill and drain
-// are a large share of its time and the other CTA on the SM covers them.
+// the default for local attention (few key tiles per CTA, so a CTA's fill and drain
+// are a large share of its time and the other CTA on the SM covers them) and for
+// global launches whose query pairs fill 1.5 to 2 waves (one rank's half window).
 constexpr int kDefaultKeySplit1 = 15 * 8 + 1;
 // Q is [q_count][E] token-major (this rank's queries, the first of which is row
 // q_offset of the key window); K and V are [kv_rows][E] token-major.
@@ -113,8 +113,8 @@ struct FlashArgs {
   int embed;
   int v_f16;              // 1: V holds f16 and P is formed in f16; 0: V and P are bf16
   // bf16 path: variant = poly + 8 * form (see launch_flash); < 0: the library default
-  // (with fixed_offset kDefaultKeySplit1 for local attention and short global
-  // launches, else kDefaultKeySplit; without it kDefaultPolyPer8)
+  // (with fixed_offset kDefaultKeySplit1 for local attention and global launches of
+  // 1.5 to 2 waves of query pairs, else kDefaultKeySplit; without it kDefaultPolyPer8)
   int poly_per8 = -1;
   // 1: exponents relative to 0 instead of the running row max (w20 kernel, bf16 P;
   // other forms ignore it).  Only for inputs with |q.k| * scale * log2(e) <= 64.
