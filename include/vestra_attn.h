@@ -147,9 +147,10 @@ int va_op_attention_device(va_ctx* ctx, const float* q, const float* k, const fl
  * [n, 2] F32 (rounded half away from zero; each in [0, 65535], else VA_ERR_INVALID) or
  * NULL; rope_pairing as in va_config.  Limit: heads * n * 64
  * <= 2,097,152, else VA_ERR_CAPACITY.  The first call on a device looks up the
- * scratch address with that device current and should come before any stream
- * capture.  Calls share the scratch: calls that overlap on the GPU race.  The call
- * waits for `stream` and returns VA_ERR_DEVICE if a kernel gave up on a bounded wait. */
+ * scratch address with that device current.  Calls share the scratch: calls that
+ * overlap on the GPU race.  The call waits for `stream` (it synchronizes it and reads
+ * the device error word back) and returns VA_ERR_DEVICE if a kernel gave up on a
+ * bounded wait. */
 int va_op_attention_noalloc(const float* q, const float* k, const float* v, int heads,
                             int64_t n, int head_dim, const float* qn_g, const float* qn_b,
                             const float* kn_g, const float* kn_b, float qk_norm_eps,
