@@ -69,19 +69,6 @@ def parse_args():
     return ap.parse_args()
 
 
-def default_flash_kernel(q_count, heads, seg_len=0):
-    """The attention kernel the library's default picks for a fixed-offset launch
-    (launch_flash): one query tile per CTA, two CTAs per SM (ks1) for local attention
-    and for global launches whose 256-query units fill 1.5 to 2 waves of the SMs, else
-    the two-tile kernel (ks)."""
-    import torch
-
-    sms = torch.cuda.get_device_properties(0).multi_processor_count
-    pair_units = -(-q_count // 256) * heads
-    one_tile = seg_len > 0 or 3 * sms <= 2 * pair_units < 4 * sms
-    return "flash_fwd_d64_ks1_kernel" if one_tile else "flash_fwd_d64_ks_kernel"
-
-
 def cpu_threads():
     """Host threads this process may run on (the oracle is given this count
     explicitly, so a launcher's OMP_NUM_THREADS=1 does not apply)."""
@@ -927,6 +914,9 @@ def run_ours(args):
                "sample": f"the full window ({wl.rows} query rows), median of 3 after one warm-up",
                "cpu": cpu_info()}
 
+    # The kernel this rank's launch ran, from the library's own launch plan.
+    sms = torch.cuda.get_device_properties(local_rank).multi_processor_count
+    flash_kernel = va.flash_plan(local, wl.rows, wl.heads, q_offset=row0, sms=sms)["kernel"]
     if rank == 0:
         line = {
             "metric": "global-attention TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
@@ -936,7 +926,7 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, QK-norm gamma 1 beta 0)",
             "config": workload_config(wl, world),
-            "roofline": {"bound": "tensor", "kernel": default_flash_kernel(local, wl.heads), "achieved": round(achieved, 2),
+            "roofline": {"bound": "tensor", "kernel": flash_kernel, "achieved": round(achieved, 2),
                          "peak": peak_tflops, "unit": "TFLOP/s", "frac": round(achieved / peak_tflops, 4),
                          "peak_kind": f"bf16 burst ({peak_kind})", "flops_per_launch": flash_flops,
                          "ms_per_launch": round(flash_ms, 4),

@@ -326,6 +326,16 @@ int va_flash_attention_bf16(va_ctx* ctx, const void* q, const void* k, const voi
                             int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads,
                             int64_t seg_len, int v_f16, int variant, void* out,
                             void* stream);
+
+/* The launch plan va_flash_attention_bf16 (and every layer entry point) makes for a
+ * bf16-V call with these shapes on a GPU of `sms` multiprocessors, with a context's
+ * split workspace; host only, needs no GPU.  fixed_offset and variant as above
+ * (variant < 0: the library default, + 256: the fixed offset).  plan[9] receives:
+ * form, poly, query rows per unit (128 one-tile / 256 two-tile), CTAs per SM the
+ * split plan counts, units run whole, key ranges per tail unit (1: no split), and
+ * the grid (x, y, z).  VA_ERR_INVALID for shapes or a variant the launch rejects. */
+int va_flash_plan(int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads, int64_t seg_len,
+                  int fixed_offset, int variant, int sms, int* plan);
 /* K3-style GEMM: out[M,N] = (a[M,K] * w_t[N,K]^T + bias) * scale (+ residual), bf16
  * in, F32 out; bias/scale/residual may be NULL.  N % 128 == 0, K % 64 == 0. */
 int va_linear_bf16(va_ctx* ctx, const void* a, const void* w_t, const float* bias,

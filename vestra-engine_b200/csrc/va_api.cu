@@ -2091,6 +2091,35 @@ int va_flash_attention_bf16(va_ctx* c, const void* q, const void* k, const void*
   return VA_OK;
 }
 
+int va_flash_plan(int64_t q_count, int64_t q_offset, int64_t kv_rows, int heads, int64_t seg_len,
+                  int fixed_offset, int variant, int sms, int* plan) {
+  if (!plan || sms <= 0 || heads <= 0 || heads > 64 || q_count <= 0 || kv_rows <= 0 || q_offset < 0 ||
+      seg_len < 0 || q_count > 0x7fffffff || kv_rows > 0x7fffffff || q_offset > 0x7fffffff ||
+      seg_len > 0x7fffffff)
+    return VA_ERR_INVALID;
+  va::FlashArgs fa{};
+  fa.q_count = static_cast<int>(q_count);
+  fa.q_offset = static_cast<int>(q_offset);
+  fa.kv_rows = static_cast<int>(kv_rows);
+  fa.seg_len = static_cast<int>(seg_len);
+  fa.heads = heads;
+  fa.embed = heads * 64;
+  fa.fixed_offset = fixed_offset ? 1 : 0;
+  if (variant >= 256) {  // as va_flash_attention_bf16: + 256 = the fixed exponent offset
+    fa.fixed_offset = 1;
+    variant -= 256;
+    if (variant == 255) variant = -1;
+  }
+  fa.poly_per8 = variant < 0 ? -1 : variant;
+  fa.sms = sms;
+  fa.part_slots = va::flash_part_slots(sms);
+  va::FlashPlan p;
+  if (va::flash_plan(fa, sms, 2, true, &p) != cudaSuccess) return VA_ERR_INVALID;
+  const int v[9] = {p.form, p.poly, p.unit_rows, p.per_sm, fa.n_full, fa.splits, p.grid_x, p.grid_y, p.grid_z};
+  for (int i = 0; i < 9; ++i) plan[i] = v[i];
+  return VA_OK;
+}
+
 int va_linear_bf16(va_ctx* c, const void* a, const void* w_t, const float* bias, const float* scale,
                    const float* residual, float* out, int64_t m, int n, int k, void* stream) {
   if (!c || !a || !w_t || !out) return VA_ERR_INVALID;

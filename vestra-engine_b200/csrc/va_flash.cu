@@ -2145,21 +2145,106 @@ __global__ void __launch_bounds__(kW20Threads, 1)
 
 }  // namespace
 
-cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                         const FlashArgs& fa_in, int* err, cudaStream_t st) {
-  FlashArgs fa = fa_in;
+bool flash_shapes_valid(const FlashArgs& fa) {
   // Every TMA box must start inside its tensor: q rows [0, q_count), key rows
   // [q_offset + segment start, +seg_len) or [0, kv_rows).
   if (fa.q_count <= 0 || fa.kv_rows <= 0 || fa.heads <= 0 || fa.embed != fa.heads * kHeadDim ||
       fa.q_offset < 0 || fa.seg_len < 0)
-    return cudaErrorInvalidValue;
-  int segs = 1;
-  if (fa.seg_len > 0) {
-    if (fa.q_count % fa.seg_len != 0 || fa.q_offset % fa.seg_len != 0 ||
-        static_cast<int64_t>(fa.q_offset) + fa.q_count > fa.kv_rows)
-      return cudaErrorInvalidValue;
-    segs = fa.q_count / fa.seg_len;
+    return false;
+  if (fa.seg_len > 0 && (fa.q_count % fa.seg_len != 0 || fa.q_offset % fa.seg_len != 0 ||
+                         static_cast<int64_t>(fa.q_offset) + fa.q_count > fa.kv_rows))
+    return false;
+  return true;
+}
+
+cudaError_t flash_plan(FlashArgs& fa, int sms, int one_tile_per_sm, bool split_ok, FlashPlan* plan) {
+  if (!flash_shapes_valid(fa) || sms <= 0 || one_tile_per_sm <= 0) return cudaErrorInvalidValue;
+  FlashPlan& p = *plan;
+  p = FlashPlan{};
+  if (fa.poly_per8 < 0) {
+    fa.poly_per8 = kDefaultPolyPer8;
+    if (fa.fixed_offset && !fa.v_f16) {
+      // Global: the one-tile form where the two-tile units fill 1.5 to 2 waves (their
+      // split tail is then half a wave or more); measured on B200 it loses below
+      // (2,598 queries of 10,392: 549 vs 715 TFLOP/s) and on full windows.
+      const int64_t pair_units = static_cast<int64_t>((fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ)) * fa.heads;
+      const bool tail_heavy = 2 * pair_units >= 3 * static_cast<int64_t>(sms) && pair_units < 2 * sms;
+      fa.poly_per8 = fa.seg_len > 0 || tail_heavy ? kDefaultKeySplit1 : kDefaultKeySplit;
+    }
   }
+  bool no_split = false;
+  p.poly = fa.poly_per8 & 7;
+  p.form = fa.poly_per8 >> 3;
+  if (fa.v_f16) {
+    p.form = 0;
+    p.poly = 0;
+  } else {
+    const int poly = p.poly, form = p.form;
+    if (form >= 9 && form <= 15) {
+      if (poly > (form == 15 ? 2 : 4) || !fa.fixed_offset) return cudaErrorInvalidValue;
+    } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
+      return cudaErrorInvalidValue;
+    }
+    p.w20 = form == 3 || (form >= 5 && form <= 15);
+    p.persistent = form == 14;
+    p.tile1 = form == 15;
+    // form 6: form 3 with the split tail turned off (one CTA per unit).
+    no_split = form == 6;
+  }
+  // Query rows of one unit (a CTA before any key split) and CTAs resident per SM.
+  p.unit_rows = p.tile1 ? kTileQ : 2 * kTileQ;
+  p.per_sm = p.tile1 ? one_tile_per_sm : 1;
+  if (fa.seg_len > 0) {
+    p.grid_x = (fa.seg_len + p.unit_rows - 1) / p.unit_rows;
+    p.grid_y = fa.heads;
+    p.grid_z = fa.q_count / fa.seg_len;
+    fa.n_full = 0;
+    fa.splits = 1;
+  } else {
+    // Units (head, query pair, or query tile for form 15); the partial last wave is
+    // split over key ranges when the caller gave a partial-result workspace.
+    const int qpairs = (fa.q_count + p.unit_rows - 1) / p.unit_rows;
+    const int units = qpairs * fa.heads;
+    const int num_kv = (fa.kv_rows + kTileK - 1) / kTileK;
+    fa.n_full = units;
+    fa.splits = 1;
+    if (p.w20 && !no_split && split_ok) {
+      // The tail of `rem` units cut into s key ranges takes ceil(rem*s/slots) rounds
+      // of 1/s unit time; pick the s with the shortest tail (each split also pays
+      // a few percent for its own setup and the merge).
+      const int slots = sms * p.per_sm;
+      const int rem = units % slots;
+      int best = 1;
+      double best_cost = 1.0;
+      for (int sp = 2; rem && sp <= std::min(kMaxSplits, num_kv); ++sp) {
+        const double cost = static_cast<double>((rem * sp + slots - 1) / slots) / sp + 0.03;
+        if (cost < best_cost && rem * sp * 2 <= fa.part_slots) {
+          best = sp;
+          best_cost = cost;
+        }
+      }
+      if (best >= 2) {
+        fa.n_full = units - rem;
+        fa.splits = best;
+      }
+    }
+    p.grid_x = fa.n_full + (units - fa.n_full) * fa.splits;
+    p.grid_y = p.grid_z = 1;
+  }
+  if (p.persistent) {
+    // One CTA per SM walks the items (global: the launch plan's units and split
+    // pieces in grid order; local: (segment, head, query pair)).
+    fa.items = p.grid_x * p.grid_y * p.grid_z;
+    p.grid_x = std::min(fa.items, sms);
+    p.grid_y = p.grid_z = 1;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                         const FlashArgs& fa_in, int* err, cudaStream_t st) {
+  FlashArgs fa = fa_in;
+  if (!flash_shapes_valid(fa)) return cudaErrorInvalidValue;
   // V is bf16 or f16; TMA copies 2-byte elements either way (zero fill is 0x0000
   // in both types), so one bf16 map description serves both.
   CUtensorMap mq, mk, mv;
@@ -2217,105 +2302,31 @@ cudaError_t launch_flash(const __nv_bfloat16* q, const __nv_bfloat16* k, const _
 #define VA_KS1(KA) {flash_fwd_d64_ks1_kernel<KA, false, true>, flash_fwd_d64_ks1_kernel<KA, true, true>}
   static const Kern ks1[3][2] = {VA_KS1(64), VA_KS1(72), VA_KS1(80)};
 #undef VA_KS1
-  bool persistent = false, tile1 = false;
+  int sms = fa.sms;
+  if (sms <= 0) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  static int t1_per_sm = 0;  // one-tile CTAs resident per SM, queried once (two by design)
+  if (t1_per_sm == 0) {
+    cudaError_t e = cudaFuncSetAttribute(ks1[0][0], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         T1Smem::kLaunchBytes);
+    int nb = 0;
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, ks1[0][0], kT1Threads, T1Smem::kLaunchBytes);
+    if (e != cudaSuccess) return e;
+    t1_per_sm = std::max(1, std::min(nb, 2));
+  }
+  FlashPlan plan;
+  const bool split_ok = fa.part_o && fa.part_ml && fa.counters && fa.sms > 0;
+  cudaError_t pe = flash_plan(fa, sms, t1_per_sm, split_ok, &plan);
+  if (pe != cudaSuccess) return pe;
+  const bool persistent = plan.persistent, tile1 = plan.tile1, w20_kernel = plan.w20;
+  const dim3 grid(plan.grid_x, plan.grid_y, plan.grid_z);
   Kern kern;
   int threads = kRowsThreads;
-  bool w20_kernel = false, no_split = false;
-  if (fa.poly_per8 < 0) {
-    fa.poly_per8 = kDefaultPolyPer8;
-    if (fa.fixed_offset && !fa.v_f16) {
-      int sms = fa.sms;
-      if (sms <= 0) {
-        int dev = 0;
-        cudaError_t e = cudaGetDevice(&dev);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
-      }
-      // Global: the one-tile form where the two-tile units fill 1.5 to 2 waves (their
-      // split tail is then half a wave or more); measured on B200 it loses below
-      // (2,598 queries of 10,392: 549 vs 715 TFLOP/s) and on full windows.
-      const int64_t pair_units = static_cast<int64_t>((fa.q_count + 2 * kTileQ - 1) / (2 * kTileQ)) * fa.heads;
-      const bool tail_heavy = 2 * pair_units >= 3 * static_cast<int64_t>(sms) && pair_units < 2 * sms;
-      fa.poly_per8 = fa.seg_len > 0 || tail_heavy ? kDefaultKeySplit1 : kDefaultKeySplit;
-    }
-  }
-  if (!fa.v_f16) {
-    const int poly = fa.poly_per8 & 7, form = fa.poly_per8 >> 3;
-    if (form >= 9 && form <= 15) {
-      if (poly > (form == 15 ? 2 : 4) || !fa.fixed_offset) return cudaErrorInvalidValue;
-    } else if (poly > 2 || form > 8 || (form == 8 && poly != 0)) {
-      return cudaErrorInvalidValue;
-    }
-    w20_kernel = form == 3 || (form >= 5 && form <= 15);
-    persistent = form == 14;
-    tile1 = form == 15;
-    // form 6: form 3 with the split tail turned off (one CTA per unit).
-    no_split = form == 6;
-  }
-  // Query rows of one unit (a CTA before any key split) and CTAs resident per SM.
-  const int unit_rows = tile1 ? kTileQ : 2 * kTileQ;
-  int per_sm = 1;
-  if (tile1) {
-    static int t1_per_sm = 0;  // measured once: two unless the device disagrees
-    if (t1_per_sm == 0) {
-      cudaError_t e = cudaFuncSetAttribute(ks1[0][0], cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           T1Smem::kLaunchBytes);
-      int nb = 0;
-      if (e == cudaSuccess)
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, ks1[0][0], kT1Threads, T1Smem::kLaunchBytes);
-      if (e != cudaSuccess) return e;
-      t1_per_sm = std::max(1, std::min(nb, 2));
-    }
-    per_sm = t1_per_sm;
-  }
-  dim3 grid;
-  if (fa.seg_len > 0) {
-    grid = dim3((fa.seg_len + unit_rows - 1) / unit_rows, fa.heads, segs);
-    fa.n_full = 0;
-    fa.splits = 1;
-  } else {
-    // Units (head, query pair, or query tile for form 15); the partial last wave is
-    // split over key ranges when the caller gave a partial-result workspace.
-    const int qpairs = (fa.q_count + unit_rows - 1) / unit_rows;
-    const int units = qpairs * fa.heads;
-    const int num_kv = (fa.kv_rows + kTileK - 1) / kTileK;
-    fa.n_full = units;
-    fa.splits = 1;
-    if (w20_kernel && !no_split && fa.part_o && fa.part_ml && fa.counters && fa.sms > 0) {
-      // The tail of `rem` units cut into s key ranges takes ceil(rem*s/slots) rounds
-      // of 1/s unit time; pick the s with the shortest tail (each split also pays
-      // a few percent for its own setup and the merge).
-      const int slots = fa.sms * per_sm;
-      const int rem = units % slots;
-      int best = 1;
-      double best_cost = 1.0;
-      for (int sp = 2; rem && sp <= std::min(kMaxSplits, num_kv); ++sp) {
-        const double cost = static_cast<double>((rem * sp + slots - 1) / slots) / sp + 0.03;
-        if (cost < best_cost && rem * sp * 2 <= fa.part_slots) {
-          best = sp;
-          best_cost = cost;
-        }
-      }
-      if (best >= 2) {
-        fa.n_full = units - rem;
-        fa.splits = best;
-      }
-    }
-    grid = dim3(fa.n_full + (units - fa.n_full) * fa.splits, 1, 1);
-  }
-  if (persistent) {
-    // One CTA per SM walks the items (global: the launch plan's units and split
-    // pieces in grid order; local: (segment, head, query pair)).
-    fa.items = static_cast<int>(grid.x * grid.y * grid.z);
-    int sms = fa.sms;
-    if (sms <= 0) {
-      int dev = 0;
-      cudaError_t e = cudaGetDevice(&dev);
-      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      if (e != cudaSuccess) return e;
-    }
-    grid = dim3(std::min(fa.items, sms), 1, 1);
-  }
   if (fa.v_f16) {
     kern = flash_fwd_d64_kernel<true, 0, 0>;
   } else {

@@ -146,6 +146,22 @@ struct FlashArgs {
   int own_begin = 0;
   int own_end = 0;
 };
+// Launch plan of the attention kernel, computed on the host alone: launch_flash runs
+// it, va_flash_plan reports it.
+struct FlashPlan {
+  int form = 0, poly = 0;  // the variant the launch runs (poly + 8 * form)
+  int unit_rows = 0;       // query rows of one unit before any key split (128 or 256)
+  int per_sm = 1;          // CTAs of this form resident per SM
+  bool tile1 = false, persistent = false, w20 = false;
+  int grid_x = 0, grid_y = 0, grid_z = 0;
+};
+// The shapes every TMA box of a launch needs (q, key window, segments).
+bool flash_shapes_valid(const FlashArgs& fa);
+// Resolves the default variant, validates it, and fills fa.n_full / splits / items
+// and the plan for `sms` multiprocessors; one_tile_per_sm = resident CTAs of the
+// one-tile form; split_ok = the caller gave a split workspace of fa.part_slots.
+cudaError_t flash_plan(FlashArgs& fa, int sms, int one_tile_per_sm, bool split_ok, FlashPlan* plan);
+
 // Value of an exchange flag (see FlashArgs::peer_flags).
 inline unsigned long long peer_flag_value(int epoch, bool complete, int64_t end) {
   return (static_cast<unsigned long long>(static_cast<unsigned>(epoch)) << 32) |

@@ -38,7 +38,7 @@ EXPORTED = [
     "va_version", "va_default_config", "va_create", "va_destroy", "va_last_error", "va_load_layer",
     "va_layer_flags", "va_run_attention", "va_attention_host", "va_attention_device",
     "va_block_attention_device", "va_op_attention_device", "va_flash_attention_bf16",
-    "va_linear_bf16", "va_select_reference_view_saddle", "va_reference_first_order",
+    "va_linear_bf16", "va_flash_plan", "va_select_reference_view_saddle", "va_reference_first_order",
     "va_restore_order", "va_camera_inject_device", "va_permute_views_device", "va_check_device",
     "va_selftest_bounded_wait", "va_set_phase_profile", "va_phase_times", "va_exchange_times", "va_last_exchange",
     "va_load_mlp", "va_block_device", "va_block_device_sharded", "va_run_tail_host",
@@ -134,6 +134,7 @@ def load_library(path: str = LIB_PATH):
         "va_op_attention_noalloc": ([_vp, _vp, _vp, c_int, i64, c_int, _vp, _vp, _vp, _vp, c_float, _vp, c_float,
                                      c_int, _vp, _vp], c_int),
         "va_linear_bf16": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, i64, c_int, c_int, _vp], c_int),
+        "va_flash_plan": ([i64, i64, i64, c_int, i64, c_int, c_int, c_int, _i32p], c_int),
         "va_select_reference_view_saddle": ([_vp, c_int, c_int, _i32p], c_int),
         "va_reference_first_order": ([c_int, c_int, _i32p], c_int),
         "va_restore_order": ([c_int, c_int, _i32p], c_int),
@@ -918,6 +919,31 @@ def shard_rows(window_rows: int, nranks: int, rank: int) -> tuple[int, int]:
         raise ValueError(f"window of {window_rows} tokens does not split into {nranks} equal slices")
     local = window_rows // nranks
     return rank * local, local
+
+
+FLASH_KERNELS = {15: "flash_fwd_d64_ks1_kernel", 14: "flash_fwd_d64_ksp_kernel"}
+
+
+def flash_plan(q_count: int, kv_rows: int, heads: int, seg_len: int = 0, q_offset: int = 0,
+               fixed_offset: bool = True, variant: int = -1, sms: int = 148) -> dict:
+    """The attention launch plan the library makes for these shapes (va_flash_plan; no
+    GPU needed): variant form/poly, the kernel, units, key split and grid."""
+    out = (ctypes.c_int * 9)()
+    rc = load_library().va_flash_plan(q_count, q_offset, kv_rows, heads, seg_len, int(fixed_offset), variant,
+                                      sms, out)
+    if rc != VA_OK:
+        raise VestraError(rc, "flash_plan")
+    form, poly, unit_rows, per_sm, n_full, splits, gx, gy, gz = list(out)
+    if form in FLASH_KERNELS:
+        kernel = FLASH_KERNELS[form]
+    elif form >= 9:
+        kernel = "flash_fwd_d64_ks_kernel"
+    elif form == 3 or form >= 5:
+        kernel = "flash_fwd_d64_w20_kernel"
+    else:
+        kernel = "flash_fwd_d64_kernel"
+    return {"form": form, "poly": poly, "kernel": kernel, "unit_rows": unit_rows, "per_sm": per_sm,
+            "n_full": n_full, "splits": splits, "grid": (gx, gy, gz)}
 
 
 def select_reference_view_saddle(cls) -> int:
